@@ -1,0 +1,265 @@
+/*
+ * pz_sampling.h — C ABI of the B200 token sampler (logits -> token id).
+ *
+ * Two layers:
+ *
+ *  1. The six legacy entry points of Project Zero's sampler, with the same
+ *     names, signatures and semantics.  They take HOST pointers, exactly like
+ *     the CPU code they replace; the library stages the row to the GPU, runs
+ *     the sm_100a kernels and copies the result back.  Defining
+ *     PZ_NO_LEGACY_NAMES before including this header hides the unprefixed
+ *     names; the pz_-prefixed aliases are always exported.
+ *
+ *       reference include/sampling/sampling.h:12  int   sample_argmax(const float*, int)
+ *       reference include/sampling/sampling.h:23  void  apply_temperature(float*, int, float)
+ *       reference include/sampling/sampling.h:36  int   sample_top_p(float*, int, float, unsigned long long*)
+ *       reference include/sampling/sampling.h:49  int   sample_top_k(float*, int, int, unsigned long long*)
+ *       reference include/sampling/rng.h:14       void  rng_seed(unsigned long long*, unsigned long long)
+ *       reference include/sampling/rng.h:21       float rng_float(unsigned long long*)
+ *
+ *  2. A batched, stream-ordered API on DEVICE pointers (device-resident
+ *     hand-off from the LM head: no host round trip).  One call samples B
+ *     rows, each with its own pz_sampler_config, penalty history and RNG
+ *     state.  It replaces the per-step sampling block of the reference's
+ *     generate loop (reference src/transformer/generate.c:146-170) for a
+ *     whole batch, with the penalty / top-k -> top-p composition defined in
+ *     the pipeline contract below.
+ *
+ * Pipeline contract per row (what pz_sample_batch computes):
+ *   x      = logits row, widened to fp32 (bf16 -> fp32 is exact: bits << 16)
+ *   A8     for each distinct id t in the row's history with count c (ids
+ *          outside [0,V) ignored):
+ *            if (rep != 1) x[t] = x[t] > 0 ? x[t] / rep : x[t] * rep;
+ *            x[t] = x[t] - (c * freq + presence)     (float ops, in that order)
+ *   A7     if (T <= 0 || T < 1e-6f): token = argmax(x) (first index of the
+ *          maximum, NaN never wins unless at [0]); no RNG draw.
+ *   A3     x *= 1.0f / T     (reference src/sampling/temperature.c:11-20;
+ *                             PZ_CFG_TEMP_DIVIDE selects x /= T, :22-23)
+ *   A9     k_eff = (k <= 0 || k >= V) ? 0 : min(k, 1024)
+ *          k_eff == 0:  0 < p < 1 -> sample_top_p over the whole row
+ *                                    (reference src/sampling/top_p.c:30-108)
+ *                       otherwise -> softmax + CDF walk in index order
+ *                                    (reference src/transformer/generate.c:157-168)
+ *          k_eff >= 1:  the top-k selection of reference
+ *                       src/sampling/top_k.c:27-48 (value desc, lowest index
+ *                       among ties, entries > -1e30 only, padded with
+ *                       (-1e30, -1)); then
+ *                       0 < p < 1 -> the sample_top_p steps run over that
+ *                                    sorted list (top_p.c:37-105)
+ *                       otherwise -> the top-k softmax and draw (top_k.c:50-72)
+ *   A1     every non-greedy row consumes exactly one xorshift64* draw from
+ *          its RNG state (reference src/sampling/rng.c:8-17).
+ * With no history, k = 0 and fp32 input this IS the reference call sequence
+ * of generate.c:151-170.
+ */
+#ifndef PZ_SAMPLING_H
+#define PZ_SAMPLING_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Status codes.  Modelled on TernaryError (reference include/core/error.h:4-31):
+ * zero is success, every failure has its own code and a string. */
+typedef enum pz_status {
+  PZ_OK = 0,
+  PZ_ERR_INVALID_ARGS = 1,   /* null pointer, bad size, bad dtype ...        */
+  PZ_ERR_CUDA = 2,           /* a CUDA runtime call failed                   */
+  PZ_ERR_OOM = 3,            /* device or host allocation failed             */
+  PZ_ERR_NCCL = 4,           /* NCCL unavailable or a collective failed      */
+  PZ_ERR_TIMEOUT = 5,        /* a bounded wait ran out                       */
+  PZ_ERR_UNSUPPORTED = 6,    /* request outside the library's limits         */
+  PZ_ERR_NO_DEVICE = 7,      /* no CUDA device visible                       */
+  PZ_ERR_COUNT
+} pz_status;
+
+const char *pz_status_str(pz_status s);
+
+/* Per-row status written by the kernels (optional output array). */
+enum {
+  PZ_ROW_OK = 0,
+  PZ_ROW_HISTORY_TOO_LONG = 1, /* row history longer than the ctx's max_history */
+  PZ_ROW_HINT_VIOLATED = 2     /* row needs a full-vocabulary pass the hints excluded */
+};
+
+typedef enum pz_dtype { PZ_DTYPE_F32 = 0, PZ_DTYPE_BF16 = 1 } pz_dtype;
+
+/* Per-row sampler settings, 32 bytes, read by the kernels from device memory. */
+typedef struct pz_sampler_config {
+  float temperature;         /* <= 0 or < 1e-6: greedy (A7)                */
+  int32_t top_k;             /* 0 or >= V: off; clamped to 1024 (A9)       */
+  float top_p;               /* nucleus when 0 < top_p < 1 (A5)            */
+  float repetition_penalty;  /* 1: off (A8)                                */
+  float frequency_penalty;   /* 0: off (A8)                                */
+  float presence_penalty;    /* 0: off (A8)                                */
+  uint32_t flags;            /* PZ_CFG_* bits                              */
+  uint32_t reserved;         /* must be 0                                  */
+} pz_sampler_config;
+
+/* Temperature as `x /= T` (the reference's non-AVX-512 build,
+ * temperature.c:22-23) instead of `x *= 1/T` (its AVX-512 build, :11-20). */
+#define PZ_CFG_TEMP_DIVIDE 0x1u
+
+/* Top-k list cap (reference src/sampling/top_k.c:6 TOP_K_MAX). */
+#define PZ_TOP_K_MAX 1024
+/* sample_top_p falls back to argmax above this vocabulary size
+ * (reference src/sampling/top_p.c:26,33-34). */
+#define PZ_TOP_P_MAX_VOCAB 200000
+
+/* ------------------------------------------------------------------------ */
+/* Layer 1: the reference's six calls (host pointers, one row).             */
+
+/* reference src/sampling/argmax.c:3-13 */
+int pz_sample_argmax(const float *logits, int vocab_size);
+/* reference src/sampling/temperature.c:8-25 (multiply-by-reciprocal variant) */
+void pz_apply_temperature(float *logits, int vocab_size, float temperature);
+/* reference src/sampling/top_p.c:30-108; logits are read, not modified */
+int pz_sample_top_p(float *logits, int vocab_size, float top_p,
+                    unsigned long long *rng_state);
+/* reference src/sampling/top_k.c:8-73; logits are read, not modified */
+int pz_sample_top_k(float *logits, int vocab_size, int k,
+                    unsigned long long *rng_state);
+/* reference src/sampling/rng.c:3-6 */
+void pz_rng_seed(unsigned long long *state, unsigned long long seed);
+/* reference src/sampling/rng.c:8-17 */
+float pz_rng_float(unsigned long long *state);
+
+/* Full-softmax draw of the reference's generate loop
+ * (src/transformer/generate.c:157-168): softmax over the whole row, then the
+ * CDF walk in index order; fallback V-1.  `logits` is overwritten with the
+ * probabilities, as tn_softmax does in the reference. */
+int pz_sample_softmax(float *logits, int vocab_size,
+                      unsigned long long *rng_state);
+
+#ifndef PZ_NO_LEGACY_NAMES
+int sample_argmax(const float *logits, int vocab_size);
+void apply_temperature(float *logits, int vocab_size, float temperature);
+int sample_top_p(float *logits, int vocab_size, float top_p,
+                 unsigned long long *rng_state);
+int sample_top_k(float *logits, int vocab_size, int k,
+                 unsigned long long *rng_state);
+void rng_seed(unsigned long long *state, unsigned long long seed);
+float rng_float(unsigned long long *state);
+#endif
+
+/* Status of the most recent legacy call on this thread (the legacy
+ * signatures have no status return; a failed call returns -1 / leaves the
+ * data unchanged and records the reason here). */
+pz_status pz_last_error(void);
+
+/* ------------------------------------------------------------------------ */
+/* Layer 2: batched device API.                                              */
+
+typedef struct pz_sampler_ctx pz_sampler_ctx;
+
+/* Capacity of a context.  Scratch memory is sized from these at creation;
+ * pz_sample_batch rejects calls beyond them with PZ_ERR_UNSUPPORTED. */
+typedef struct pz_ctx_limits {
+  int32_t max_batch;     /* rows per call                                  */
+  int32_t max_vocab;     /* V per call (vocab slice length when sharded)   */
+  int32_t max_top_k;     /* largest top_k any row will use (<= 1024)       */
+  int32_t max_history;   /* longest penalty history of any row             */
+} pz_ctx_limits;
+
+/* Creates a context on `device` (the caller's current device is restored on
+ * return).  All scratch is allocated here; sampling calls allocate nothing. */
+pz_status pz_ctx_create(pz_sampler_ctx **ctx, int device,
+                        const pz_ctx_limits *limits);
+pz_status pz_ctx_destroy(pz_sampler_ctx *ctx);
+/* Bytes of device scratch the context holds. */
+size_t pz_ctx_scratch_bytes(const pz_sampler_ctx *ctx);
+
+/* Hints that let a call skip work.  Passing NULL means "no promises".
+ *   max_top_k / max_history: upper bounds over the rows of this call
+ *       (0 = use the context limit);
+ *   no_full_vocab: 1 promises that no row needs a full-vocabulary pass
+ *       (every non-greedy row has 1 <= top_k < V).  A row that breaks the
+ *       promise gets token -1 and PZ_ROW_HINT_VIOLATED. */
+typedef struct pz_batch_hints {
+  int32_t max_top_k;
+  int32_t max_history;
+  int32_t no_full_vocab;
+  int32_t reserved;
+} pz_batch_hints;
+
+/* Optional per-row outputs; any pointer may be NULL.
+ *   cand_ids / cand_probs: [B x cand_stride]; for rows with k_eff >= 1 the
+ *       sorted top-k list (ids) and the probabilities the sampler computed
+ *       for it (A5 steps: e*inv in list order, 0 for entries the max-20
+ *       filter dropped; A4: e/sum); other rows get -1 / 0.
+ *   n_cand: [B] number of list entries written (k_eff, or 0).
+ *   row_status: [B] PZ_ROW_* codes. */
+typedef struct pz_batch_outputs {
+  int32_t *cand_ids;
+  float *cand_probs;
+  int32_t *n_cand;
+  int32_t *row_status;
+  int32_t cand_stride;
+  int32_t reserved;
+} pz_batch_outputs;
+
+/* Samples B rows.  All pointers are DEVICE pointers on the ctx's device.
+ *   logits:      B rows of V elements, row r at logits + r*ld (elements).
+ *   cfg:         B configs, one per row.
+ *   hist, hist_off: CSR penalty history: the ids of row r are
+ *                hist[hist_off[r] .. hist_off[r+1]); both may be NULL (no
+ *                history).
+ *   rng_state:   B xorshift64* states, advanced in place (one draw per
+ *                non-greedy row).
+ *   out_tokens:  B sampled ids.
+ * Stream-ordered and asynchronous on `stream` (a cudaStream_t; NULL = the
+ * legacy default stream).  Calls that share a context must be ordered (one
+ * stream, or explicit events): they share the context's scratch. */
+pz_status pz_sample_batch(pz_sampler_ctx *ctx, const void *logits,
+                          pz_dtype dtype, int B, int V, int64_t ld,
+                          const pz_sampler_config *cfg, const int32_t *hist,
+                          const int32_t *hist_off,
+                          unsigned long long *rng_state, int32_t *out_tokens,
+                          const pz_batch_hints *hints,
+                          const pz_batch_outputs *outputs, void *stream);
+
+/* Seeds B RNG states on the device: state[r] = seed_base + r (0 -> 1, as
+ * rng_seed does), or state[r] = seeds[r] when `seeds` (device) is non-NULL. */
+pz_status pz_rng_seed_batch(unsigned long long *rng_state, int B,
+                            unsigned long long seed_base,
+                            const unsigned long long *seeds, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Multi-GPU.                                                                */
+
+/* Row sharding: the contiguous row range [*begin, *begin + *count) that rank
+ * `rank` of `world` owns in a batch of B rows (no communication). */
+void pz_row_shard(int B, int world, int rank, int *begin, int *count);
+
+/* Vocab sharding: each rank holds the columns [v_offset, v_offset + V_local)
+ * of every row.  The rank computes its local top-k candidates, all ranks
+ * exchange them with ONE NCCL allgather, and every rank merges the G*k
+ * candidates into the exact global top-k (value desc, global id asc) and
+ * draws with the row's RNG state.  Every rank returns the same tokens and
+ * advances the same RNG states.  Penalty history is given in GLOBAL ids;
+ * each rank applies the ids that fall in its slice (no extra collective).
+ * Requires every non-greedy row to have 1 <= top_k < V_global — other rows
+ * get token -1 and PZ_ROW_HINT_VIOLATED.  Greedy rows take the global
+ * argmax. */
+pz_status pz_nccl_get_unique_id(void *id_out, size_t id_bytes);
+pz_status pz_ctx_init_nccl(pz_sampler_ctx *ctx, int world, int rank,
+                           const void *unique_id, size_t id_bytes);
+pz_status pz_sample_batch_vocab_sharded(
+    pz_sampler_ctx *ctx, const void *logits_slice, pz_dtype dtype, int B,
+    int V_local, int64_t ld, int64_t v_offset, int V_global,
+    const pz_sampler_config *cfg, const int32_t *hist,
+    const int32_t *hist_off, unsigned long long *rng_state,
+    int32_t *out_tokens, const pz_batch_outputs *outputs, void *stream);
+
+/* Library version string. */
+const char *pz_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PZ_SAMPLING_H */

@@ -1,0 +1,627 @@
+// pz_capi.cu — the C ABI of include/pz_sampling.h: contexts, scratch, the
+// reference's six legacy calls, the batched device API, and NCCL vocab
+// sharding.  No torch types cross this boundary.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/pz_sampling.h"
+#include "pz_kernels.cuh"
+
+using pz::FullArgs;
+using pz::MergeArgs;
+using pz::SliceArgs;
+
+namespace {
+
+thread_local pz_status g_last_error = PZ_OK;
+
+pz_status fail(pz_status s) {
+  g_last_error = s;
+  return s;
+}
+
+int next_pow2(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) return;
+    ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+// ---- NCCL, loaded at run time (the process may already hold torch's) ----
+struct NcclApi {
+  bool loaded = false;
+  void *h = nullptr;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t,
+                            ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+};
+std::mutex g_nccl_mu;
+NcclApi g_nccl;
+
+bool load_nccl() {
+  std::lock_guard<std::mutex> lk(g_nccl_mu);
+  if (g_nccl.loaded) return true;
+  const char *names[] = {"libnccl.so.2", "libnccl.so"};
+  for (const char *n : names) {
+    g_nccl.h = dlopen(n, RTLD_NOW | RTLD_GLOBAL);
+    if (g_nccl.h) break;
+  }
+  if (!g_nccl.h) return false;
+#define PZ_SYM(field, name)                                                   \
+  g_nccl.field = reinterpret_cast<decltype(g_nccl.field)>(dlsym(g_nccl.h, name)); \
+  if (!g_nccl.field) return false;
+  PZ_SYM(GetUniqueId, "ncclGetUniqueId")
+  PZ_SYM(CommInitRank, "ncclCommInitRank")
+  PZ_SYM(AllGather, "ncclAllGather")
+  PZ_SYM(CommDestroy, "ncclCommDestroy")
+  PZ_SYM(CommAbort, "ncclCommAbort")
+  PZ_SYM(CommGetAsyncError, "ncclCommGetAsyncError")
+#undef PZ_SYM
+  g_nccl.loaded = true;
+  return true;
+}
+
+}  // namespace
+
+struct pz_sampler_ctx {
+  int device = 0;
+  int num_sms = 148;
+  pz_ctx_limits lim{};
+  int kcap_max = 1;
+  int hcap_max = 0;
+  int slices_cap = 0;
+  size_t scratch = 0;
+  std::vector<void *> allocs;
+  unsigned long long *slice_keys = nullptr;
+  int32_t *slice_cnt = nullptr;
+  uint32_t *row_arrive = nullptr;
+  uint32_t *row_flags = nullptr;
+  unsigned long long *row_best = nullptr;
+  int32_t *full_rows = nullptr;
+  int32_t *n_full = nullptr;
+  uint32_t *sort_a = nullptr;
+  uint32_t *sort_b = nullptr;
+  int64_t sort_stride = 0;
+  int full_grid = 0;
+  // vocab sharding
+  ncclComm_t comm = nullptr;
+  int world = 1, rank = 0;
+  unsigned long long *emit = nullptr;
+  unsigned long long *gathered = nullptr;
+
+  template <typename T>
+  bool alloc(T **p, size_t count) {
+    void *q = nullptr;
+    const size_t bytes = std::max<size_t>(count, 1) * sizeof(T);
+    if (cudaMalloc(&q, bytes) != cudaSuccess) return false;
+    if (cudaMemset(q, 0, bytes) != cudaSuccess) {
+      cudaFree(q);
+      return false;
+    }
+    allocs.push_back(q);
+    scratch += bytes;
+    *p = static_cast<T *>(q);
+    return true;
+  }
+  void release() {
+    for (void *q : allocs) cudaFree(q);
+    allocs.clear();
+  }
+};
+
+extern "C" {
+
+const char *pz_status_str(pz_status s) {
+  switch (s) {
+    case PZ_OK: return "ok";
+    case PZ_ERR_INVALID_ARGS: return "invalid arguments";
+    case PZ_ERR_CUDA: return "CUDA runtime error";
+    case PZ_ERR_OOM: return "out of memory";
+    case PZ_ERR_NCCL: return "NCCL unavailable or failed";
+    case PZ_ERR_TIMEOUT: return "timed out";
+    case PZ_ERR_UNSUPPORTED: return "request beyond the context's limits";
+    case PZ_ERR_NO_DEVICE: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+
+const char *pz_version(void) { return "pz-sample-b200 0.1 (sm_100a)"; }
+
+pz_status pz_last_error(void) { return g_last_error; }
+
+pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
+                        const pz_ctx_limits *limits) {
+  if (!out || !limits) return fail(PZ_ERR_INVALID_ARGS);
+  *out = nullptr;
+  const pz_ctx_limits L = *limits;
+  if (L.max_batch <= 0 || L.max_vocab <= 0 || L.max_top_k < 0 ||
+      L.max_top_k > PZ_TOP_K_MAX || L.max_history < 0 || L.max_history > 8192)
+    return fail(PZ_ERR_INVALID_ARGS);
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(PZ_ERR_NO_DEVICE);
+  if (device < 0 || device >= ndev) return fail(PZ_ERR_INVALID_ARGS);
+  DeviceGuard g(device);
+  if (!g.ok) return fail(PZ_ERR_CUDA);
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] { attr_err = pz::set_kernel_attributes(); });
+  if (attr_err != cudaSuccess) return fail(PZ_ERR_CUDA);
+
+  pz_sampler_ctx *c = new pz_sampler_ctx();
+  c->device = device;
+  c->lim = L;
+  cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+  c->kcap_max = next_pow2(std::max(L.max_top_k, 1));
+  c->hcap_max = L.max_history > 0 ? next_pow2(L.max_history) : 0;
+  c->slices_cap = std::max(L.max_batch, 8192);
+  c->full_grid = c->num_sms;
+  c->sort_stride = 2 * static_cast<int64_t>(L.max_vocab);
+  const int B = L.max_batch;
+  bool ok = c->alloc(&c->slice_keys, static_cast<size_t>(c->slices_cap) * c->kcap_max) &&
+            c->alloc(&c->slice_cnt, c->slices_cap) && c->alloc(&c->row_arrive, B) &&
+            c->alloc(&c->row_flags, B) && c->alloc(&c->row_best, B) &&
+            c->alloc(&c->full_rows, B) && c->alloc(&c->n_full, 1) &&
+            c->alloc(&c->sort_a, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
+            c->alloc(&c->sort_b, static_cast<size_t>(c->full_grid) * c->sort_stride);
+  if (!ok) {
+    c->release();
+    delete c;
+    return fail(PZ_ERR_OOM);
+  }
+  *out = c;
+  return PZ_OK;
+}
+
+pz_status pz_ctx_destroy(pz_sampler_ctx *ctx) {
+  if (!ctx) return PZ_OK;
+  DeviceGuard g(ctx->device);
+  cudaDeviceSynchronize();
+  if (ctx->comm && g_nccl.loaded) g_nccl.CommDestroy(ctx->comm);
+  ctx->release();
+  delete ctx;
+  return PZ_OK;
+}
+
+size_t pz_ctx_scratch_bytes(const pz_sampler_ctx *ctx) { return ctx ? ctx->scratch : 0; }
+
+void pz_row_shard(int B, int world, int rank, int *begin, int *count) {
+  if (world <= 0 || rank < 0 || rank >= world || B < 0) {
+    if (begin) *begin = 0;
+    if (count) *count = 0;
+    return;
+  }
+  const int base = B / world, rem = B % world;
+  const int b = rank * base + std::min(rank, rem);
+  if (begin) *begin = b;
+  if (count) *count = base + (rank < rem ? 1 : 0);
+}
+
+// Slices per row: enough CTAs to fill the GPU several times over, slices of
+// at least 2048 columns, and B*S within the context's scratch.
+static void choose_slices(const pz_sampler_ctx *c, int B, int V, int *S_out,
+                          int *L_out) {
+  const int target = c->num_sms * 32;
+  int S = (target + B - 1) / B;
+  S = std::min(S, std::max(1, (V + 2047) / 2048));
+  S = std::min(S, std::max(1, c->slices_cap / std::max(B, 1)));
+  S = std::max(S, 1);
+  int L = (V + S - 1) / S;
+  L = (L + 7) / 8 * 8;
+  S = (V + L - 1) / L;
+  *S_out = S;
+  *L_out = L;
+}
+
+static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
+                             pz_dtype dtype, int B, int V, int64_t ld,
+                             int64_t v_offset, int V_global,
+                             const pz_sampler_config *cfg, const int32_t *hist,
+                             const int32_t *hist_off,
+                             unsigned long long *rng_state, int32_t *out,
+                             const pz_batch_hints *hints,
+                             const pz_batch_outputs *outputs, void *stream,
+                             bool emit) {
+  if (!ctx || !logits || !cfg || B < 0 || V <= 0 || ld < V) return fail(PZ_ERR_INVALID_ARGS);
+  if (dtype != PZ_DTYPE_F32 && dtype != PZ_DTYPE_BF16) return fail(PZ_ERR_INVALID_ARGS);
+  if (!emit && (!rng_state || !out)) return fail(PZ_ERR_INVALID_ARGS);
+  if ((hist == nullptr) != (hist_off == nullptr)) return fail(PZ_ERR_INVALID_ARGS);
+  if (B == 0) return PZ_OK;
+  if (B > ctx->lim.max_batch || V > ctx->lim.max_vocab) return fail(PZ_ERR_UNSUPPORTED);
+  if (outputs && (outputs->cand_ids || outputs->cand_probs) && outputs->cand_stride < 1)
+    return fail(PZ_ERR_INVALID_ARGS);
+  int kmax = ctx->lim.max_top_k, hmax = ctx->lim.max_history, no_full = 0;
+  if (hints) {
+    if (hints->max_top_k > 0) kmax = std::min(kmax, hints->max_top_k);
+    if (hints->max_history > 0) hmax = std::min(hmax, hints->max_history);
+    no_full = hints->no_full_vocab ? 1 : 0;
+  }
+  if (outputs && (outputs->cand_ids || outputs->cand_probs) && outputs->cand_stride < kmax)
+    return fail(PZ_ERR_INVALID_ARGS);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(PZ_ERR_CUDA);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  SliceArgs a{};
+  a.logits = logits;
+  a.ld = ld;
+  a.V = V;
+  a.V_global = V_global;
+  a.v_offset = v_offset;
+  a.B = B;
+  a.cfg = cfg;
+  a.hist = hist;
+  a.hist_off = hist_off;
+  choose_slices(ctx, B, V, &a.S, &a.L);
+  a.kcap = next_pow2(std::max(kmax, 1));
+  a.kmax = std::max(kmax, 1);
+  a.hcap = (hist != nullptr && hmax > 0) ? next_pow2(hmax) : 0;
+  a.bm_words = a.hcap > 0 ? a.L / 32 + 3 : 0;
+  a.mode_emit = emit ? 1 : 0;
+  a.no_full_vocab = no_full;
+  a.slice_keys = ctx->slice_keys;
+  a.slice_cnt = ctx->slice_cnt;
+  a.row_arrive = ctx->row_arrive;
+  a.row_flags = ctx->row_flags;
+  a.row_best = ctx->row_best;
+  a.full_rows = ctx->full_rows;
+  a.n_full = ctx->n_full;
+  a.emit_keys = ctx->emit;
+  a.rng = rng_state;
+  a.out = out;
+  if (outputs) {
+    a.cand_ids = outputs->cand_ids;
+    a.cand_probs = outputs->cand_probs;
+    a.n_cand = outputs->n_cand;
+    a.row_status = outputs->row_status;
+    a.cand_stride = outputs->cand_stride;
+  }
+  const size_t smem = pz::slice_smem_bytes(a.kcap, a.hcap, a.bm_words);
+  if (smem > 227 * 1024) return fail(PZ_ERR_UNSUPPORTED);
+  const bool full_pass = !emit && !no_full;
+  if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t), st) != cudaSuccess)
+    return fail(PZ_ERR_CUDA);
+  if (pz::launch_slice(a, dtype, smem, st) != cudaSuccess) return fail(PZ_ERR_CUDA);
+  if (full_pass) {
+    FullArgs f{};
+    f.logits = logits;
+    f.ld = ld;
+    f.V = V;
+    f.B = B;
+    f.cfg = cfg;
+    f.hist = hist;
+    f.hist_off = hist_off;
+    f.hcap = a.hcap;
+    f.row_best = ctx->row_best;
+    f.row_flags = ctx->row_flags;
+    f.full_rows = ctx->full_rows;
+    f.n_full = ctx->n_full;
+    f.sort_a = ctx->sort_a;
+    f.sort_b = ctx->sort_b;
+    f.sort_stride = ctx->sort_stride;
+    f.rng = rng_state;
+    f.out = out;
+    const size_t fsmem = pz::full_smem_bytes(V, a.hcap);
+    if (fsmem > 227 * 1024) return fail(PZ_ERR_UNSUPPORTED);
+    const int grid = std::min(ctx->full_grid, B);
+    if (pz::launch_full(f, dtype, grid, fsmem, st) != cudaSuccess) return fail(PZ_ERR_CUDA);
+  }
+  return PZ_OK;
+}
+
+pz_status pz_sample_batch(pz_sampler_ctx *ctx, const void *logits,
+                          pz_dtype dtype, int B, int V, int64_t ld,
+                          const pz_sampler_config *cfg, const int32_t *hist,
+                          const int32_t *hist_off,
+                          unsigned long long *rng_state, int32_t *out_tokens,
+                          const pz_batch_hints *hints,
+                          const pz_batch_outputs *outputs, void *stream) {
+  return sample_impl(ctx, logits, dtype, B, V, ld, 0, V, cfg, hist, hist_off,
+                     rng_state, out_tokens, hints, outputs, stream, false);
+}
+
+pz_status pz_rng_seed_batch(unsigned long long *rng_state, int B,
+                            unsigned long long seed_base,
+                            const unsigned long long *seeds, void *stream) {
+  if (!rng_state || B < 0) return fail(PZ_ERR_INVALID_ARGS);
+  if (B == 0) return PZ_OK;
+  if (pz::launch_rng_seed(rng_state, B, seed_base, seeds,
+                          static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return fail(PZ_ERR_CUDA);
+  return PZ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// vocab sharding
+// ---------------------------------------------------------------------------
+pz_status pz_nccl_get_unique_id(void *id_out, size_t id_bytes) {
+  if (!id_out || id_bytes < sizeof(ncclUniqueId)) return fail(PZ_ERR_INVALID_ARGS);
+  if (!load_nccl()) return fail(PZ_ERR_NCCL);
+  ncclUniqueId id;
+  if (g_nccl.GetUniqueId(&id) != ncclSuccess) return fail(PZ_ERR_NCCL);
+  std::memcpy(id_out, &id, sizeof id);
+  return PZ_OK;
+}
+
+pz_status pz_ctx_init_nccl(pz_sampler_ctx *ctx, int world, int rank,
+                           const void *unique_id, size_t id_bytes) {
+  if (!ctx || !unique_id || id_bytes < sizeof(ncclUniqueId) || world < 1 ||
+      rank < 0 || rank >= world)
+    return fail(PZ_ERR_INVALID_ARGS);
+  if (!load_nccl()) return fail(PZ_ERR_NCCL);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(PZ_ERR_CUDA);
+  const size_t per_rank = static_cast<size_t>(ctx->lim.max_batch) * (ctx->kcap_max + 1);
+  if (!ctx->emit && !ctx->alloc(&ctx->emit, per_rank)) return fail(PZ_ERR_OOM);
+  if (!ctx->gathered && !ctx->alloc(&ctx->gathered, per_rank * world)) return fail(PZ_ERR_OOM);
+  ncclUniqueId id;
+  std::memcpy(&id, unique_id, sizeof id);
+  ncclComm_t comm = nullptr;
+  if (g_nccl.CommInitRank(&comm, world, id, rank) != ncclSuccess) return fail(PZ_ERR_NCCL);
+  ctx->comm = comm;
+  ctx->world = world;
+  ctx->rank = rank;
+  return PZ_OK;
+}
+
+pz_status pz_sample_batch_vocab_sharded(
+    pz_sampler_ctx *ctx, const void *logits_slice, pz_dtype dtype, int B,
+    int V_local, int64_t ld, int64_t v_offset, int V_global,
+    const pz_sampler_config *cfg, const int32_t *hist, const int32_t *hist_off,
+    unsigned long long *rng_state, int32_t *out_tokens,
+    const pz_batch_outputs *outputs, void *stream) {
+  if (!ctx || !ctx->comm || !rng_state || !out_tokens) return fail(PZ_ERR_INVALID_ARGS);
+  if (outputs && (outputs->cand_ids || outputs->cand_probs) &&
+      outputs->cand_stride < std::max(ctx->lim.max_top_k, 1))
+    return fail(PZ_ERR_INVALID_ARGS);
+  if (V_global < V_local || v_offset < 0 || v_offset + V_local > V_global)
+    return fail(PZ_ERR_INVALID_ARGS);
+  pz_batch_hints h{};
+  h.no_full_vocab = 1;
+  pz_status s = sample_impl(ctx, logits_slice, dtype, B, V_local, ld, v_offset,
+                            V_global, cfg, hist, hist_off, nullptr, nullptr, &h,
+                            nullptr, stream, true);
+  if (s != PZ_OK) return s;
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int kcap = next_pow2(std::max(ctx->lim.max_top_k, 1));
+  const size_t per_rank = static_cast<size_t>(B) * (kcap + 1);
+  // ONE allgather: every rank's [B][kcap+1] list block, counts included.
+  if (g_nccl.AllGather(ctx->emit, ctx->gathered, per_rank, ncclUint64, ctx->comm, st) != ncclSuccess)
+    return fail(PZ_ERR_NCCL);
+  MergeArgs m{};
+  m.gathered = ctx->gathered;
+  m.G = ctx->world;
+  m.B = B;
+  m.kcap = kcap;
+  m.kmax = std::max(ctx->lim.max_top_k, 1);
+  m.V_global = V_global;
+  m.cfg = cfg;
+  m.rng = rng_state;
+  m.out = out_tokens;
+  if (outputs) {
+    m.cand_ids = outputs->cand_ids;
+    m.cand_probs = outputs->cand_probs;
+    m.n_cand = outputs->n_cand;
+    m.row_status = outputs->row_status;
+    m.cand_stride = outputs->cand_stride;
+  }
+  if (pz::launch_merge(m, pz::merge_smem_bytes(kcap), st) != cudaSuccess) return fail(PZ_ERR_CUDA);
+  return PZ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Layer 1: the reference's six calls on host pointers.
+// ---------------------------------------------------------------------------
+namespace {
+struct LegacyState {
+  std::mutex mu;
+  pz_sampler_ctx *ctx = nullptr;
+  int vocab = 0;
+  cudaStream_t st = nullptr;
+  float *d_logits = nullptr;
+  pz_sampler_config *d_cfg = nullptr;
+  unsigned long long *d_rng = nullptr;
+  int32_t *d_out = nullptr;
+  int device = -1;
+};
+LegacyState g_legacy;
+
+void legacy_free() {
+  if (g_legacy.d_logits) cudaFree(g_legacy.d_logits);
+  if (g_legacy.d_cfg) cudaFree(g_legacy.d_cfg);
+  if (g_legacy.d_rng) cudaFree(g_legacy.d_rng);
+  if (g_legacy.d_out) cudaFree(g_legacy.d_out);
+  g_legacy.d_logits = nullptr;
+  g_legacy.d_cfg = nullptr;
+  g_legacy.d_rng = nullptr;
+  g_legacy.d_out = nullptr;
+  if (g_legacy.ctx) pz_ctx_destroy(g_legacy.ctx);
+  g_legacy.ctx = nullptr;
+  g_legacy.vocab = 0;
+}
+
+// Prepares the single-row context for V columns on the current device.
+pz_status legacy_ready(int V) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PZ_ERR_NO_DEVICE;
+  if (g_legacy.ctx && g_legacy.vocab >= V && g_legacy.device == dev) return PZ_OK;
+  legacy_free();
+  if (!g_legacy.st && cudaStreamCreateWithFlags(&g_legacy.st, cudaStreamNonBlocking) != cudaSuccess)
+    return PZ_ERR_CUDA;
+  pz_ctx_limits L{};
+  L.max_batch = 1;
+  L.max_vocab = std::max(V, 1024);
+  L.max_top_k = PZ_TOP_K_MAX;
+  L.max_history = 0;
+  pz_status s = pz_ctx_create(&g_legacy.ctx, dev, &L);
+  if (s != PZ_OK) return s;
+  if (cudaMalloc(&g_legacy.d_logits, sizeof(float) * L.max_vocab) != cudaSuccess ||
+      cudaMalloc(&g_legacy.d_cfg, sizeof(pz_sampler_config)) != cudaSuccess ||
+      cudaMalloc(&g_legacy.d_rng, sizeof(unsigned long long)) != cudaSuccess ||
+      cudaMalloc(&g_legacy.d_out, sizeof(int32_t)) != cudaSuccess) {
+    legacy_free();
+    return PZ_ERR_OOM;
+  }
+  g_legacy.vocab = L.max_vocab;
+  g_legacy.device = dev;
+  return PZ_OK;
+}
+
+// One row through the batch pipeline with a legacy-shaped config.
+int legacy_row(const float *logits, int V, const pz_sampler_config &cfg,
+               unsigned long long *rng_state) {
+  if (!logits || V <= 0) {
+    g_last_error = PZ_ERR_INVALID_ARGS;
+    return -1;
+  }
+  std::lock_guard<std::mutex> lk(g_legacy.mu);
+  pz_status s = legacy_ready(V);
+  if (s != PZ_OK) {
+    g_last_error = s;
+    return -1;
+  }
+  cudaStream_t st = g_legacy.st;
+  unsigned long long state = rng_state ? *rng_state : 1ull;
+  int32_t tok = -1;
+  if (cudaMemcpyAsync(g_legacy.d_logits, logits, sizeof(float) * V, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(g_legacy.d_cfg, &cfg, sizeof cfg, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(g_legacy.d_rng, &state, sizeof state, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+    g_last_error = PZ_ERR_CUDA;
+    return -1;
+  }
+  s = pz_sample_batch(g_legacy.ctx, g_legacy.d_logits, PZ_DTYPE_F32, 1, V, V, g_legacy.d_cfg,
+                      nullptr, nullptr, g_legacy.d_rng, g_legacy.d_out, nullptr, nullptr, st);
+  if (s != PZ_OK) {
+    g_last_error = s;
+    return -1;
+  }
+  if (cudaMemcpyAsync(&tok, g_legacy.d_out, sizeof tok, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaMemcpyAsync(&state, g_legacy.d_rng, sizeof state, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess) {
+    g_last_error = PZ_ERR_CUDA;
+    return -1;
+  }
+  if (rng_state) *rng_state = state;
+  g_last_error = PZ_OK;
+  return tok;
+}
+
+pz_sampler_config legacy_cfg() {
+  pz_sampler_config c{};
+  c.temperature = 1.0f;  // x * (1/1) leaves every value unchanged
+  c.top_k = 0;
+  c.top_p = 1.0f;
+  c.repetition_penalty = 1.0f;
+  return c;
+}
+}  // namespace
+
+int pz_sample_argmax(const float *logits, int vocab_size) {
+  pz_sampler_config c = legacy_cfg();
+  c.temperature = 0.0f;
+  return legacy_row(logits, vocab_size, c, nullptr);
+}
+
+void pz_apply_temperature(float *logits, int vocab_size, float temperature) {
+  if (!logits || vocab_size <= 0) {
+    g_last_error = PZ_ERR_INVALID_ARGS;
+    return;
+  }
+  std::lock_guard<std::mutex> lk(g_legacy.mu);
+  pz_status s = legacy_ready(vocab_size);
+  if (s != PZ_OK) {
+    g_last_error = s;
+    return;
+  }
+  cudaStream_t st = g_legacy.st;
+  if (cudaMemcpyAsync(g_legacy.d_logits, logits, sizeof(float) * vocab_size, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      pz::launch_temperature(g_legacy.d_logits, vocab_size, temperature, st) != cudaSuccess ||
+      cudaMemcpyAsync(logits, g_legacy.d_logits, sizeof(float) * vocab_size, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess) {
+    g_last_error = PZ_ERR_CUDA;
+    return;
+  }
+  g_last_error = PZ_OK;
+}
+
+int pz_sample_top_p(float *logits, int vocab_size, float top_p,
+                    unsigned long long *rng_state) {
+  pz_sampler_config c = legacy_cfg();
+  c.top_p = top_p;
+  c.flags = PZ_CFG_TOPP_ALWAYS;
+  return legacy_row(logits, vocab_size, c, rng_state);
+}
+
+int pz_sample_top_k(float *logits, int vocab_size, int k,
+                    unsigned long long *rng_state) {
+  pz_sampler_config c = legacy_cfg();
+  c.top_k = k;
+  c.flags = PZ_CFG_TOPK_LEGACY;
+  return legacy_row(logits, vocab_size, c, rng_state);
+}
+
+int pz_sample_softmax(float *logits, int vocab_size,
+                      unsigned long long *rng_state) {
+  pz_sampler_config c = legacy_cfg();
+  return legacy_row(logits, vocab_size, c, rng_state);
+}
+
+// The RNG word lives in host memory in the legacy API (a stack variable of
+// the reference's generate loop, generate.c:125); these two run on the host,
+// with the same arithmetic as the device draw.
+void pz_rng_seed(unsigned long long *state, unsigned long long seed) {
+  if (state) *state = (seed == 0) ? 1ull : seed;  // rng.c:3-6
+}
+
+float pz_rng_float(unsigned long long *state) {  // rng.c:8-17
+  unsigned long long s = *state;
+  s ^= s >> 12;
+  s ^= s << 25;
+  s ^= s >> 27;
+  *state = s;
+  return static_cast<float>((s * 0x2545F4914F6CDD1DULL) >> 33) / static_cast<float>(1u << 31);
+}
+
+int sample_argmax(const float *logits, int vocab_size) {
+  return pz_sample_argmax(logits, vocab_size);
+}
+void apply_temperature(float *logits, int vocab_size, float temperature) {
+  pz_apply_temperature(logits, vocab_size, temperature);
+}
+int sample_top_p(float *logits, int vocab_size, float top_p,
+                 unsigned long long *rng_state) {
+  return pz_sample_top_p(logits, vocab_size, top_p, rng_state);
+}
+int sample_top_k(float *logits, int vocab_size, int k,
+                 unsigned long long *rng_state) {
+  return pz_sample_top_k(logits, vocab_size, k, rng_state);
+}
+void rng_seed(unsigned long long *state, unsigned long long seed) {
+  pz_rng_seed(state, seed);
+}
+float rng_float(unsigned long long *state) { return pz_rng_float(state); }
+
+}  // extern "C"

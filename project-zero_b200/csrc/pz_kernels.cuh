@@ -1,0 +1,114 @@
+// pz_kernels.cuh — launch arguments of the sampler kernels (host + device).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/pz_sampling.h"
+
+// Config flags used only by the legacy single-row entry points.
+// sample_top_k's own clamping (reference src/sampling/top_k.c:11-18):
+// k > V -> V, k <= 0 -> 1, k > 1024 -> 1024; the list may cover the row.
+#define PZ_CFG_TOPK_LEGACY 0x2u
+// sample_top_p's steps whatever p is (reference src/sampling/top_p.c:30-108
+// is called only for 0 < p < 1 by the generate loop, but the function itself
+// accepts any p).
+#define PZ_CFG_TOPP_ALWAYS 0x4u
+
+namespace pz {
+
+constexpr int kSliceThreads = 256;
+constexpr int kFullThreads = 1024;
+constexpr int kCapB = 1024;   // candidate buffer room above the list length
+constexpr int kRowBits = 2;   // row_flags bits
+
+struct SliceArgs {
+  const void *logits;
+  int64_t ld;           // elements between rows
+  int V;                // columns held here (slice of the vocabulary when sharded)
+  int V_global;         // vocabulary size the row's settings refer to
+  int64_t v_offset;     // global id of column 0
+  int B;
+  const pz_sampler_config *cfg;
+  const int32_t *hist;
+  const int32_t *hist_off;
+  int S;                // CTAs per row
+  int L;                // columns per CTA (multiple of 8)
+  int kcap;             // power of two >= largest k_eff in the launch
+  int kmax;             // declared largest k_eff (rows above it are rejected)
+  int hcap;             // power of two >= longest history (0: no history SMEM)
+  int bm_words;         // bitmap words per CTA
+  int mode_emit;        // 1: write the merged local list (vocab sharding), no draw
+  int no_full_vocab;
+  // scratch
+  unsigned long long *slice_keys;  // [B*S][kcap]
+  int32_t *slice_cnt;              // [B*S]
+  uint32_t *row_arrive;            // [B]
+  uint32_t *row_flags;             // [B]
+  unsigned long long *row_best;    // [B]
+  int32_t *full_rows;              // [B]
+  int32_t *n_full;                 // [1]
+  unsigned long long *emit_keys;   // [B][kcap+1] (mode_emit); slot kcap = count | flags
+  // outputs
+  unsigned long long *rng;
+  int32_t *out;
+  int32_t *cand_ids;
+  float *cand_probs;
+  int32_t *n_cand;
+  int32_t *row_status;
+  int cand_stride;
+};
+
+struct FullArgs {
+  const void *logits;
+  int64_t ld;
+  int V;
+  int B;
+  const pz_sampler_config *cfg;
+  const int32_t *hist;
+  const int32_t *hist_off;
+  int hcap;
+  const unsigned long long *row_best;
+  const uint32_t *row_flags;
+  const int32_t *full_rows;
+  const int32_t *n_full;
+  uint32_t *sort_a;     // [gridDim][2*maxV] (prob key, index) pairs
+  uint32_t *sort_b;
+  int64_t sort_stride;  // uint32 elements per CTA in sort_a/sort_b
+  unsigned long long *rng;
+  int32_t *out;
+};
+
+struct MergeArgs {               // vocab-sharded merge after the allgather
+  const unsigned long long *gathered;  // [G][B][kcap+1]; slot kcap = count | flags
+  int G;
+  int B;
+  int kcap;
+  int kmax;
+  int V_global;
+  const pz_sampler_config *cfg;
+  unsigned long long *rng;
+  int32_t *out;
+  int32_t *cand_ids;
+  float *cand_probs;
+  int32_t *n_cand;
+  int32_t *row_status;
+  int cand_stride;
+};
+
+// Launchers (pz_kernels.cu).  Return cudaGetLastError() after the launch.
+cudaError_t launch_slice(const SliceArgs &a, int dtype, size_t smem,
+                         cudaStream_t st);
+size_t slice_smem_bytes(int kcap, int hcap, int bm_words);
+cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem,
+                        cudaStream_t st);
+size_t full_smem_bytes(int V, int hcap);
+cudaError_t launch_merge(const MergeArgs &a, size_t smem, cudaStream_t st);
+size_t merge_smem_bytes(int kcap);
+cudaError_t launch_temperature(float *x, int n, float T, cudaStream_t st);
+cudaError_t launch_rng_seed(unsigned long long *s, int B,
+                            unsigned long long base,
+                            const unsigned long long *seeds, cudaStream_t st);
+cudaError_t set_kernel_attributes();
+
+}  // namespace pz

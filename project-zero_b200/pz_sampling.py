@@ -1,0 +1,339 @@
+"""Python host side of the B200 token sampler (ctypes over libpz_sampling.so).
+
+Mirrors the reference's sampler interface (Project Zero include/sampling/
+sampling.h and rng.h) with the same names, argument meaning and results:
+
+    sample_argmax(logits)                   -> int     (argmax.c:3-13)
+    apply_temperature(logits, T)            -> array   (temperature.c:8-25)
+    sample_top_p(logits, p, state)          -> (int, state)   (top_p.c:30-108)
+    sample_top_k(logits, k, state)          -> (int, state)   (top_k.c:8-73)
+    rng_seed(seed)                          -> state   (rng.c:3-6)
+    rng_float(state)                        -> (float, state) (rng.c:8-17)
+
+The C functions update the RNG word and logits in place; Python integers are
+immutable, so these wrappers return the new state (and apply_temperature
+returns the scaled array, writing it back when given a float32 numpy array).
+
+`Sampler` wraps the batched device API: logits already on the GPU (a torch
+tensor or a raw device pointer), per-row configs, penalty histories and RNG
+states, sampled on a CUDA stream with no host round trip.
+
+There is no CPU fallback: importing this module without the built library
+raises.  torch is only used here to pass device pointers and streams.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libpz_sampling.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(
+        f"{LIB_PATH} is not built (run `make -C {HERE}`); the sampler has no CPU fallback")
+
+_lib = ctypes.CDLL(LIB_PATH)
+
+PZ_OK = 0
+PZ_DTYPE_F32, PZ_DTYPE_BF16 = 0, 1
+PZ_CFG_TEMP_DIVIDE = 0x1
+PZ_ROW_OK, PZ_ROW_HISTORY_TOO_LONG, PZ_ROW_HINT_VIOLATED = 0, 1, 2
+TOP_K_MAX = 1024
+
+_vp = ctypes.c_void_p
+_u64p = ctypes.POINTER(ctypes.c_ulonglong)
+_f32p = ctypes.POINTER(ctypes.c_float)
+
+
+class CtxLimits(ctypes.Structure):
+    _fields_ = [("max_batch", ctypes.c_int32), ("max_vocab", ctypes.c_int32),
+                ("max_top_k", ctypes.c_int32), ("max_history", ctypes.c_int32)]
+
+
+class BatchHints(ctypes.Structure):
+    _fields_ = [("max_top_k", ctypes.c_int32), ("max_history", ctypes.c_int32),
+                ("no_full_vocab", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+class BatchOutputs(ctypes.Structure):
+    _fields_ = [("cand_ids", _vp), ("cand_probs", _vp), ("n_cand", _vp),
+                ("row_status", _vp), ("cand_stride", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
+
+
+# pz_sampler_config, 32 bytes
+CONFIG_DTYPE = np.dtype([
+    ("temperature", "<f4"), ("top_k", "<i4"), ("top_p", "<f4"),
+    ("repetition_penalty", "<f4"), ("frequency_penalty", "<f4"),
+    ("presence_penalty", "<f4"), ("flags", "<u4"), ("reserved", "<u4")])
+assert CONFIG_DTYPE.itemsize == 32
+
+
+def make_configs(B, temperature=1.0, top_k=0, top_p=1.0, rep=1.0, freq=0.0,
+                 pres=0.0, flags=0):
+    """Structured array of B pz_sampler_config; scalars broadcast."""
+    c = np.zeros(B, dtype=CONFIG_DTYPE)
+    c["temperature"] = temperature
+    c["top_k"] = top_k
+    c["top_p"] = top_p
+    c["repetition_penalty"] = rep
+    c["frequency_penalty"] = freq
+    c["presence_penalty"] = pres
+    c["flags"] = flags
+    return c
+
+
+def _sig(name, res, args):
+    f = getattr(_lib, name)
+    f.restype = res
+    f.argtypes = args
+    return f
+
+
+_sig("pz_status_str", ctypes.c_char_p, [ctypes.c_int])
+_sig("pz_version", ctypes.c_char_p, [])
+_sig("pz_last_error", ctypes.c_int, [])
+_sig("pz_sample_argmax", ctypes.c_int, [_f32p, ctypes.c_int])
+_sig("pz_apply_temperature", None, [_f32p, ctypes.c_int, ctypes.c_float])
+_sig("pz_sample_top_p", ctypes.c_int, [_f32p, ctypes.c_int, ctypes.c_float, _u64p])
+_sig("pz_sample_top_k", ctypes.c_int, [_f32p, ctypes.c_int, ctypes.c_int, _u64p])
+_sig("pz_sample_softmax", ctypes.c_int, [_f32p, ctypes.c_int, _u64p])
+_sig("pz_rng_seed", None, [_u64p, ctypes.c_ulonglong])
+_sig("pz_rng_float", ctypes.c_float, [_u64p])
+_sig("pz_ctx_create", ctypes.c_int, [ctypes.POINTER(_vp), ctypes.c_int, ctypes.POINTER(CtxLimits)])
+_sig("pz_ctx_destroy", ctypes.c_int, [_vp])
+_sig("pz_ctx_scratch_bytes", ctypes.c_size_t, [_vp])
+_sig("pz_sample_batch", ctypes.c_int,
+     [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp,
+      ctypes.POINTER(BatchHints), ctypes.POINTER(BatchOutputs), _vp])
+_sig("pz_rng_seed_batch", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_ulonglong, _vp, _vp])
+_sig("pz_row_shard", None, [ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                            ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)])
+_sig("pz_nccl_get_unique_id", ctypes.c_int, [_vp, ctypes.c_size_t])
+_sig("pz_ctx_init_nccl", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_size_t])
+_sig("pz_sample_batch_vocab_sharded", ctypes.c_int,
+     [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
+      ctypes.c_int, _vp, _vp, _vp, _vp, _vp, ctypes.POINTER(BatchOutputs), _vp])
+
+
+class PZError(RuntimeError):
+    def __init__(self, status, what=""):
+        self.status = status
+        super().__init__(f"{what}: {_lib.pz_status_str(status).decode()} (status {status})")
+
+
+def _check(status, what):
+    if status != PZ_OK:
+        raise PZError(status, what)
+
+
+def version() -> str:
+    return _lib.pz_version().decode()
+
+
+def library_path() -> str:
+    return LIB_PATH
+
+
+# --------------------------------------------------------------------------
+# The reference's six calls (host arrays; the row is staged to the GPU).
+# --------------------------------------------------------------------------
+def _f32(x):
+    return np.ascontiguousarray(x, dtype=np.float32)
+
+
+def _legacy_check(what):
+    s = _lib.pz_last_error()
+    if s != PZ_OK:
+        raise PZError(s, what)
+
+
+def sample_argmax(logits) -> int:
+    x = _f32(logits)
+    t = _lib.pz_sample_argmax(x.ctypes.data_as(_f32p), x.size)
+    _legacy_check("sample_argmax")
+    return int(t)
+
+
+def apply_temperature(logits, temperature):
+    """Scales in place when given a float32 array; returns the scaled array."""
+    inplace = isinstance(logits, np.ndarray) and logits.dtype == np.float32 and logits.flags.c_contiguous
+    x = logits if inplace else np.array(logits, dtype=np.float32)
+    _lib.pz_apply_temperature(x.ctypes.data_as(_f32p), x.size, ctypes.c_float(temperature))
+    _legacy_check("apply_temperature")
+    return x
+
+
+def sample_top_p(logits, top_p, state):
+    x = _f32(logits)
+    s = ctypes.c_ulonglong(state)
+    t = _lib.pz_sample_top_p(x.ctypes.data_as(_f32p), x.size, ctypes.c_float(top_p), ctypes.byref(s))
+    _legacy_check("sample_top_p")
+    return int(t), s.value
+
+
+def sample_top_k(logits, k, state):
+    x = _f32(logits)
+    s = ctypes.c_ulonglong(state)
+    t = _lib.pz_sample_top_k(x.ctypes.data_as(_f32p), x.size, int(k), ctypes.byref(s))
+    _legacy_check("sample_top_k")
+    return int(t), s.value
+
+
+def sample_softmax(logits, state):
+    """Full-softmax draw of the reference's generate loop (generate.c:157-168)."""
+    x = _f32(logits)
+    s = ctypes.c_ulonglong(state)
+    t = _lib.pz_sample_softmax(x.ctypes.data_as(_f32p), x.size, ctypes.byref(s))
+    _legacy_check("sample_softmax")
+    return int(t), s.value
+
+
+def rng_seed(seed) -> int:
+    s = ctypes.c_ulonglong(0)
+    _lib.pz_rng_seed(ctypes.byref(s), ctypes.c_ulonglong(seed))
+    return s.value
+
+
+def rng_float(state):
+    s = ctypes.c_ulonglong(state)
+    v = _lib.pz_rng_float(ctypes.byref(s))
+    return float(np.float32(v)), s.value
+
+
+def row_shard(B, world, rank):
+    """Contiguous row range (begin, count) that `rank` owns."""
+    b, c = ctypes.c_int(0), ctypes.c_int(0)
+    _lib.pz_row_shard(B, world, rank, ctypes.byref(b), ctypes.byref(c))
+    return b.value, c.value
+
+
+# --------------------------------------------------------------------------
+# Batched device API.
+# --------------------------------------------------------------------------
+def _ptr(t):
+    """Device pointer of a torch tensor (or an int pointer, or None)."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def _stream_handle(stream):
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+class Sampler:
+    """One device's sampling context (owns the scratch; allocation happens
+    here, never inside sample())."""
+
+    def __init__(self, device=0, max_batch=1024, max_vocab=262144, max_top_k=TOP_K_MAX,
+                 max_history=2048):
+        self.device = device
+        self.limits = CtxLimits(max_batch, max_vocab, max_top_k, max_history)
+        h = _vp()
+        _check(_lib.pz_ctx_create(ctypes.byref(h), device, ctypes.byref(self.limits)), "pz_ctx_create")
+        self._h = h
+        self.world, self.rank = 1, 0
+
+    @property
+    def scratch_bytes(self) -> int:
+        return int(_lib.pz_ctx_scratch_bytes(self._h))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.pz_ctx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @staticmethod
+    def _dtype_code(logits):
+        import torch
+        if logits.dtype == torch.float32:
+            return PZ_DTYPE_F32
+        if logits.dtype == torch.bfloat16:
+            return PZ_DTYPE_BF16
+        raise TypeError(f"logits dtype {logits.dtype} (want float32 or bfloat16)")
+
+    @staticmethod
+    def _outputs(cand_ids=None, cand_probs=None, n_cand=None, row_status=None):
+        if cand_ids is None and cand_probs is None and n_cand is None and row_status is None:
+            return None
+        stride = 0
+        if cand_ids is not None:
+            stride = cand_ids.shape[1]
+        elif cand_probs is not None:
+            stride = cand_probs.shape[1]
+        return BatchOutputs(_ptr(cand_ids), _ptr(cand_probs), _ptr(n_cand), _ptr(row_status), stride, 0)
+
+    def sample(self, logits, cfg, rng_state, out, hist=None, hist_off=None, *,
+               max_top_k=0, max_history=0, no_full_vocab=False, cand_ids=None,
+               cand_probs=None, n_cand=None, row_status=None, stream=None):
+        """logits: [B, V] (row stride = logits.stride(0)) float32/bfloat16 CUDA
+        tensor; cfg: device tensor holding B pz_sampler_config (32 bytes each);
+        rng_state: [B] int64 device tensor (xorshift64* words, advanced in
+        place); out: [B] int32 device tensor; hist/hist_off: CSR int32 device
+        tensors or None."""
+        B, V = logits.shape
+        hints = BatchHints(max_top_k, max_history, 1 if no_full_vocab else 0, 0)
+        outs = self._outputs(cand_ids, cand_probs, n_cand, row_status)
+        st = _lib.pz_sample_batch(
+            self._h, _ptr(logits), self._dtype_code(logits), B, V, logits.stride(0),
+            _ptr(cfg), _ptr(hist), _ptr(hist_off), _ptr(rng_state), _ptr(out),
+            ctypes.byref(hints), ctypes.byref(outs) if outs is not None else None,
+            _stream_handle(stream))
+        _check(st, "pz_sample_batch")
+        return out
+
+    # ---- vocab sharding --------------------------------------------------
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        _check(_lib.pz_nccl_get_unique_id(buf, 128), "pz_nccl_get_unique_id")
+        return buf.raw
+
+    def init_nccl(self, world, rank, unique_id: bytes):
+        buf = ctypes.create_string_buffer(unique_id, 128)
+        _check(_lib.pz_ctx_init_nccl(self._h, world, rank, buf, 128), "pz_ctx_init_nccl")
+        self.world, self.rank = world, rank
+
+    def sample_vocab_sharded(self, logits_slice, v_offset, V_global, cfg, rng_state, out,
+                             hist=None, hist_off=None, *, cand_ids=None, cand_probs=None,
+                             n_cand=None, row_status=None, stream=None):
+        B, V_local = logits_slice.shape
+        outs = self._outputs(cand_ids, cand_probs, n_cand, row_status)
+        st = _lib.pz_sample_batch_vocab_sharded(
+            self._h, _ptr(logits_slice), self._dtype_code(logits_slice), B, V_local,
+            logits_slice.stride(0), v_offset, V_global, _ptr(cfg), _ptr(hist), _ptr(hist_off),
+            _ptr(rng_state), _ptr(out), ctypes.byref(outs) if outs is not None else None,
+            _stream_handle(stream))
+        _check(st, "pz_sample_batch_vocab_sharded")
+        return out
+
+
+def seed_states(rng_state, seed_base=0, seeds=None, stream=None):
+    """state[r] = seeds[r] (device tensor) or seed_base + r; 0 becomes 1."""
+    _check(_lib.pz_rng_seed_batch(_ptr(rng_state), rng_state.numel(), seed_base, _ptr(seeds),
+                                  _stream_handle(stream)), "pz_rng_seed_batch")
+    return rng_state
+
+
+def configs_to_device(cfg_np, device="cuda"):
+    """Copies a CONFIG_DTYPE array to a device byte tensor."""
+    import torch
+    raw = np.ascontiguousarray(cfg_np, dtype=CONFIG_DTYPE).view(np.uint8)
+    return torch.from_numpy(raw.copy()).to(device)

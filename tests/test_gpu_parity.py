@@ -1,0 +1,182 @@
+"""Parity of the CUDA sampler (through the C ABI) with the reference.
+
+Bar: greedy ids and top-k id sets bit-exact;
+post-penalty probabilities within 1e-6 relative; sampled ids identical
+except draws within 1e-6 of a CDF boundary (counted; the golden cases and
+the full-size config-3 batch must have none)."""
+import numpy as np
+import pytest
+
+import cases
+import synth
+from gpu_helpers import compare_with_oracle, run_gpu
+
+pytestmark = pytest.mark.gpu
+
+PROB_RTOL = 1e-6
+
+
+@pytest.mark.parametrize("name", list(cases.PIPELINE_SPECS))
+def test_golden_pipeline(cuda, pz, golden, oracle_lib, name):
+    case = next(c for c in golden["pipeline"] if c["name"] == name)
+    d = cases.build(case["spec"])
+    g = run_gpu(cuda, pz, d)
+    assert g["tokens"].tolist() == case["tokens"]
+    assert [int(v) for v in g["rng"]] == case["rng_out"]
+    assert (g["status"] == 0).all()
+    mism, _, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+    assert mism == 0
+
+
+def test_edge_rows(cuda, pz, golden):
+    want = {c["name"]: c for c in golden["edge"]}
+    s = pz.Sampler(0, max_batch=4, max_vocab=64, max_top_k=1024, max_history=0)
+    for name, x, cfg, rng in cases.edge_rows():
+        g = run_gpu(cuda, pz, dict(logits=x, cfg=cfg, rng=rng, hist=None, hist_off=None), sampler=s)
+        assert g["tokens"].tolist() == want[name]["tokens"], name
+        assert [int(v) for v in g["rng"]] == want[name]["rng_out"], name
+    s.close()
+
+
+def test_legacy_six_calls(cuda, pz, golden):
+    L = golden["legacy"]
+    for vals, want in L["argmax"]:
+        assert pz.sample_argmax(vals) == want
+    for rec in L["top_k"]:
+        s = pz.rng_seed(rec["seed"])
+        got = []
+        for _ in rec["tokens"]:
+            t, s = pz.sample_top_k(rec["logits"], rec["k"], s)
+            got.append(t)
+        assert got == rec["tokens"] and s == rec["final"], rec["k"]
+    for rec in L["top_p"]:
+        s = pz.rng_seed(rec["seed"])
+        got = []
+        for _ in rec["tokens"]:
+            t, s = pz.sample_top_p(rec["logits"], rec["p"], s)
+            got.append(t)
+        assert got == rec["tokens"] and s == rec["final"], rec["p"]
+    for rec in L["temperature"]:
+        y = pz.apply_temperature(np.array(rec["logits"], dtype=np.float32), rec["T"])
+        assert [int(b) for b in y.view(np.uint32)] == rec["bits"]
+
+
+def test_draw_of_exactly_one(cuda, pz, golden):
+    s1 = golden["legacy"]["rng_one_state"]
+    for rec in golden["legacy"]["draw_one"]:
+        if rec["kind"] == "top_k":
+            t, s = pz.sample_top_k(rec["logits"], rec["arg"], s1)
+        elif rec["kind"] == "top_p":
+            t, s = pz.sample_top_p(rec["logits"], rec["arg"], s1)
+        else:
+            t, s = pz.sample_softmax(rec["logits"], s1)
+        assert (t, s) == (rec["token"], rec["final"]), rec["kind"]
+
+
+def test_config3_full_size(cuda, pz, oracle_lib):
+    """BASELINE config 3 at its full size, every row against the oracle."""
+    spec = dict(seed=31, B=1024, V=128256, sd=2.5, boosts=[8, 5.0, 15.0], hist_len=1024,
+                cfg=dict(temperature=0.7, top_k=50, top_p=0.9, rep=1.1, freq=0.2, pres=0.1))
+    d = cases.build(spec)
+    g = run_gpu(cuda, pz, d, max_top_k=50, max_history=1024, no_full_vocab=True)
+    mism, n, maxrel = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+    print(f"config3: {mism} boundary mismatches in {n} rows, max prob rel err {maxrel:.2e}")
+    assert mism == 0
+
+
+def test_config2_full_size_greedy(cuda, pz, oracle_lib):
+    spec = dict(seed=21, B=256, V=151936, sd=3.0, spike=[8.0, 20.0], cfg=dict(temperature=0.0))
+    d = cases.build(spec)
+    g = run_gpu(cuda, pz, d, max_top_k=1, no_full_vocab=True)
+    tok, rng, *_ = oracle_lib.sample_batch(d["logits"], d["cfg"], d["rng"])
+    assert (g["tokens"] == tok).all()
+    assert (g["rng"] == d["rng"]).all()  # greedy rows draw nothing
+
+
+def test_config4_heterogeneous(cuda, pz, oracle_lib):
+    spec = dict(seed=41, B=256, V=151936, sd=2.0, zipf=[256, 10.0], dtype="bf16", cfg="hetero")
+    d = cases.build(spec)
+    g = run_gpu(cuda, pz, d)
+    mism, n, maxrel = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+    print(f"config4: {mism} mismatches in {n} rows, max prob rel err {maxrel:.2e}")
+    assert mism <= 1
+
+
+def test_full_vocab_rows_exact(cuda, pz, oracle_lib):
+    """k = 0 rows: top-p over the whole row and the softmax CDF walk replay
+    the reference's sequential float sums exactly."""
+    for spec in [dict(seed=51, B=16, V=128256, sd=2.5, boosts=[8, 5.0, 15.0],
+                      cfg=dict(temperature=0.8, top_k=0, top_p=0.95)),
+                 dict(seed=52, B=8, V=151936, sd=2.0, zipf=[128, 8.0], dtype="bf16",
+                      cfg=dict(temperature=1.4, top_k=0, top_p=0.99)),
+                 dict(seed=53, B=8, V=128256, sd=2.5, hist_len=300,
+                      cfg=dict(temperature=1.0, top_k=0, top_p=1.0, rep=1.2))]:
+        d = cases.build(spec)
+        g = run_gpu(cuda, pz, d)
+        mism, n, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+        assert mism <= 1, (spec["seed"], mism)
+
+
+def test_strided_and_unaligned_rows(cuda, pz, oracle_lib):
+    """Row stride > V and a base that is not 16-byte aligned exercise the
+    scalar head/tail paths."""
+    torch = cuda
+    B, V, ld = 6, 3001, 3013
+    wide = synth.logits_normal(61, B, ld, 2.0)
+    cfg = cases.configs(B, temperature=0.9, top_k=17, top_p=0.9)
+    rng = np.arange(1, B + 1, dtype=np.uint64)
+    full = torch.from_numpy(wide).cuda()
+    x = full[:, 1:1 + V]  # base offset by 4 bytes, row stride 3013
+    s = pz.Sampler(0, max_batch=B, max_vocab=V, max_top_k=32, max_history=0)
+    out = torch.zeros(B, dtype=torch.int32, device="cuda")
+    r = torch.from_numpy(rng.view(np.int64).copy()).cuda()
+    c = torch.from_numpy(np.ascontiguousarray(cfg).view(np.uint8).copy()).cuda()
+    s.sample(x, c, r, out)
+    torch.cuda.synchronize()
+    tok, rr, *_ = oracle_lib.sample_batch(np.ascontiguousarray(wide[:, 1:1 + V]), cfg, rng)
+    assert (out.cpu().numpy() == tok).all()
+    assert (r.cpu().numpy().view(np.uint64) == rr).all()
+    s.close()
+
+
+def test_repeat_calls_are_identical(cuda, pz):
+    spec = dict(seed=71, B=64, V=50000, sd=2.0, hist_len=100,
+                cfg=dict(temperature=0.8, top_k=30, top_p=0.9, rep=1.2))
+    d = cases.build(spec)
+    s = pz.Sampler(0, max_batch=64, max_vocab=50000, max_top_k=64, max_history=128)
+    a = run_gpu(cuda, pz, d, sampler=s)
+    b = run_gpu(cuda, pz, d, sampler=s)
+    assert (a["tokens"] == b["tokens"]).all() and (a["rng"] == b["rng"]).all()
+    s.close()
+
+
+def test_hint_and_limit_violations_fail_loudly(cuda, pz):
+    spec = dict(seed=81, B=4, V=5000, sd=2.0, hist_len=300,
+                cfg=dict(temperature=0.8, top_k=0, top_p=0.9, rep=1.2))
+    d = cases.build(spec)
+    g = run_gpu(cuda, pz, d, no_full_vocab=True)
+    assert (g["tokens"] == -1).all() and (g["status"] == pz.PZ_ROW_HINT_VIOLATED).all()
+    g = run_gpu(cuda, pz, d, max_history=128)
+    assert (g["tokens"] == -1).all() and (g["status"] == pz.PZ_ROW_HISTORY_TOO_LONG).all()
+    d["cfg"]["top_k"] = 100
+    g = run_gpu(cuda, pz, d, max_top_k=64)
+    assert (g["tokens"] == -1).all() and (g["status"] == pz.PZ_ROW_HINT_VIOLATED).all()
+
+
+def test_vocab_sharded_single_rank(cuda, pz, golden):
+    """The vocab-sharded path (emit -> NCCL allgather -> merge) with one rank
+    gives the golden tokens of config 5."""
+    torch = cuda
+    case = next(c for c in golden["pipeline"] if c["name"] == "c5_vocab")
+    d = cases.build(case["spec"])
+    from gpu_helpers import to_device
+    x, cfg, rng, hist, hist_off = to_device(torch, d)
+    B, V = x.shape
+    s = pz.Sampler(0, max_batch=B, max_vocab=V, max_top_k=64, max_history=0)
+    s.init_nccl(1, 0, pz.Sampler.nccl_unique_id())
+    out = torch.zeros(B, dtype=torch.int32, device="cuda")
+    s.sample_vocab_sharded(x, 0, V, cfg, rng, out)
+    torch.cuda.synchronize()
+    assert out.cpu().tolist() == case["tokens"]
+    assert [int(v) for v in rng.cpu().numpy().view(np.uint64)] == case["rng_out"]
+    s.close()
