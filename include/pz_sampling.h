@@ -83,7 +83,8 @@ const char *pz_status_str(pz_status s);
 enum {
   PZ_ROW_OK = 0,
   PZ_ROW_HISTORY_TOO_LONG = 1, /* row history longer than the ctx's max_history */
-  PZ_ROW_HINT_VIOLATED = 2     /* row needs a full-vocabulary pass the hints excluded */
+  PZ_ROW_HINT_VIOLATED = 2,    /* row needs a full-vocabulary pass the hints excluded */
+  PZ_ROW_TIMEOUT = 3           /* a bounded wait inside the kernel ran out */
 };
 
 typedef enum pz_dtype { PZ_DTYPE_F32 = 0, PZ_DTYPE_BF16 = 1 } pz_dtype;
@@ -150,6 +151,8 @@ float rng_float(unsigned long long *state);
  * signatures have no status return; a failed call returns -1 / leaves the
  * data unchanged and records the reason here). */
 pz_status pz_last_error(void);
+/* Text of the CUDA error behind the last PZ_ERR_CUDA on this thread ("" if none). */
+const char *pz_last_error_detail(void);
 
 /* ------------------------------------------------------------------------ */
 /* Layer 2: batched device API.                                              */

@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -21,10 +22,24 @@ using pz::SliceArgs;
 namespace {
 
 thread_local pz_status g_last_error = PZ_OK;
+thread_local char g_detail[256] = "";
 
 pz_status fail(pz_status s) {
   g_last_error = s;
+  if (s == PZ_ERR_CUDA) {
+    const cudaError_t e = cudaGetLastError();
+    std::snprintf(g_detail, sizeof g_detail, "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+  } else {
+    std::snprintf(g_detail, sizeof g_detail, "%s", "");
+  }
   return s;
+}
+
+// Records a failed CUDA call's error text and returns PZ_ERR_CUDA.
+pz_status fail_cuda(cudaError_t e) {
+  g_last_error = PZ_ERR_CUDA;
+  std::snprintf(g_detail, sizeof g_detail, "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+  return PZ_ERR_CUDA;
 }
 
 int next_pow2(int x) {
@@ -99,6 +114,7 @@ struct pz_sampler_ctx {
   int32_t *slice_cnt = nullptr;
   uint32_t *row_arrive = nullptr;
   uint32_t *row_flags = nullptr;
+  unsigned long long *row_tau = nullptr;
   unsigned long long *row_best = nullptr;
   int32_t *full_rows = nullptr;
   int32_t *n_full = nullptr;
@@ -152,6 +168,8 @@ const char *pz_version(void) { return "pz-sample-b200 0.1 (sm_100a)"; }
 
 pz_status pz_last_error(void) { return g_last_error; }
 
+const char *pz_last_error_detail(void) { return g_detail; }
+
 pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
                         const pz_ctx_limits *limits) {
   if (!out || !limits) return fail(PZ_ERR_INVALID_ARGS);
@@ -168,7 +186,7 @@ pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] { attr_err = pz::set_kernel_attributes(); });
-  if (attr_err != cudaSuccess) return fail(PZ_ERR_CUDA);
+  if (attr_err != cudaSuccess) return fail_cuda(attr_err);
 
   pz_sampler_ctx *c = new pz_sampler_ctx();
   c->device = device;
@@ -182,7 +200,7 @@ pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
   const int B = L.max_batch;
   bool ok = c->alloc(&c->slice_keys, static_cast<size_t>(c->slices_cap) * c->kcap_max) &&
             c->alloc(&c->slice_cnt, c->slices_cap) && c->alloc(&c->row_arrive, B) &&
-            c->alloc(&c->row_flags, B) && c->alloc(&c->row_best, B) &&
+            c->alloc(&c->row_flags, B) && c->alloc(&c->row_tau, B) && c->alloc(&c->row_best, B) &&
             c->alloc(&c->full_rows, B) && c->alloc(&c->n_full, 1) &&
             c->alloc(&c->sort_a, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
             c->alloc(&c->sort_b, static_cast<size_t>(c->full_grid) * c->sort_stride);
@@ -219,14 +237,27 @@ void pz_row_shard(int B, int world, int rank, int *begin, int *count) {
   if (count) *count = base + (rank < rem ? 1 : 0);
 }
 
-// Slices per row: enough CTAs to fill the GPU several times over, slices of
-// at least 2048 columns, and B*S within the context's scratch.
-static void choose_slices(const pz_sampler_ctx *c, int B, int V, int *S_out,
-                          int *L_out) {
-  const int target = c->num_sms * 32;
+// Slices per row.  Enough CTAs for ~6.5 waves of the GPU at the kernel's
+// occupancy (fewer slices means less per-CTA setup, more slices means a
+// smaller last-wave tail), slices of at least 2048 columns, B*S within the
+// context's scratch, and S lists of the launch's list length fitting the
+// finalizer's merge area (4096 keys).
+static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
+                          size_t smem, int *S_out, int *L_out) {
+  const size_t per_sm = 228 * 1024;
+  int occ = static_cast<int>(per_sm / (smem + 2048));
+  occ = std::max(1, std::min(occ, 3));
+  const int target = static_cast<int>(c->num_sms * occ * 6.5);
   int S = (target + B - 1) / B;
+  // PZ_SLICES_PER_ROW: tuning override of the slice count
+  static const int forced = [] {
+    const char *e = std::getenv("PZ_SLICES_PER_ROW");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (forced > 0) S = forced;
   S = std::min(S, std::max(1, (V + 2047) / 2048));
   S = std::min(S, std::max(1, c->slices_cap / std::max(B, 1)));
+  S = std::min(S, std::max(1, 4096 / std::max(kcap, 1)));
   S = std::max(S, 1);
   int L = (V + S - 1) / S;
   L = (L + 7) / 8 * 8;
@@ -274,17 +305,19 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   a.cfg = cfg;
   a.hist = hist;
   a.hist_off = hist_off;
-  choose_slices(ctx, B, V, &a.S, &a.L);
   a.kcap = next_pow2(std::max(kmax, 1));
   a.kmax = std::max(kmax, 1);
-  a.hcap = (hist != nullptr && hmax > 0) ? next_pow2(hmax) : 0;
-  a.bm_words = a.hcap > 0 ? a.L / 32 + 3 : 0;
+  a.hcap = (hist != nullptr && hmax > 0) ? hmax : 0;
+  a.hts = a.hcap > 0 ? next_pow2(2 * a.hcap) : 0;
+  a.hshift = 32;
+  for (int t = a.hts; t > 1; t >>= 1) a.hshift--;
   a.mode_emit = emit ? 1 : 0;
   a.no_full_vocab = no_full;
   a.slice_keys = ctx->slice_keys;
   a.slice_cnt = ctx->slice_cnt;
   a.row_arrive = ctx->row_arrive;
   a.row_flags = ctx->row_flags;
+  a.row_tau = ctx->row_tau;
   a.row_best = ctx->row_best;
   a.full_rows = ctx->full_rows;
   a.n_full = ctx->n_full;
@@ -298,12 +331,15 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     a.row_status = outputs->row_status;
     a.cand_stride = outputs->cand_stride;
   }
-  const size_t smem = pz::slice_smem_bytes(a.kcap, a.hcap, a.bm_words);
-  if (smem > 227 * 1024) return fail(PZ_ERR_UNSUPPORTED);
+  a.nstages = pz::slice_stages(a.kcap, a.hts);
+  const size_t smem = pz::slice_smem_bytes(a.kcap, a.hts, a.nstages);
+  choose_slices(ctx, B, V, a.kcap, smem, &a.S, &a.L);
+  if (smem > static_cast<size_t>(pz::max_dynamic_smem())) return fail(PZ_ERR_UNSUPPORTED);
   const bool full_pass = !emit && !no_full;
   if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t), st) != cudaSuccess)
     return fail(PZ_ERR_CUDA);
-  if (pz::launch_slice(a, dtype, smem, st) != cudaSuccess) return fail(PZ_ERR_CUDA);
+  cudaError_t ce = pz::launch_slice(a, dtype, smem, st);
+  if (ce != cudaSuccess) return fail_cuda(ce);
   if (full_pass) {
     FullArgs f{};
     f.logits = logits;
@@ -313,7 +349,7 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     f.cfg = cfg;
     f.hist = hist;
     f.hist_off = hist_off;
-    f.hcap = a.hcap;
+    f.hcap = a.hcap > 0 ? next_pow2(a.hcap) : 0;
     f.row_best = ctx->row_best;
     f.row_flags = ctx->row_flags;
     f.full_rows = ctx->full_rows;
@@ -323,10 +359,11 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     f.sort_stride = ctx->sort_stride;
     f.rng = rng_state;
     f.out = out;
-    const size_t fsmem = pz::full_smem_bytes(V, a.hcap);
-    if (fsmem > 227 * 1024) return fail(PZ_ERR_UNSUPPORTED);
+    const size_t fsmem = pz::full_smem_bytes(V, f.hcap);
+    if (fsmem > static_cast<size_t>(pz::max_dynamic_smem())) return fail(PZ_ERR_UNSUPPORTED);
     const int grid = std::min(ctx->full_grid, B);
-    if (pz::launch_full(f, dtype, grid, fsmem, st) != cudaSuccess) return fail(PZ_ERR_CUDA);
+    ce = pz::launch_full(f, dtype, grid, fsmem, st);
+    if (ce != cudaSuccess) return fail_cuda(ce);
   }
   return PZ_OK;
 }

@@ -20,6 +20,9 @@
 #include "pz_kernels.cuh"
 #include "pz_select.cuh"
 #include "pz_seqsum.cuh"
+#include "pz_tma.cuh"
+#include "pz_warpsel.cuh"
+#include "pz_listmath.cuh"
 
 namespace pz {
 
@@ -145,12 +148,20 @@ __device__ __forceinline__ int sorted_count(const int32_t *a, int n, int t) {
 // Thread 0 runs the sequential float accumulations in the reference's order.
 // ---------------------------------------------------------------------------
 template <int NT>
-__device__ int sample_list(const unsigned long long *lk, int n_sel,
+__device__ __forceinline__ void grp_sync() {
+  if (NT == 32)
+    __syncwarp();
+  else
+    __syncthreads();
+}
+
+template <int NT>
+__device__ __noinline__ int sample_list(const unsigned long long *lk, int n_sel,
                            const RowPlan &P, unsigned long long &rs, float *e,
                            float *pr, int *order, int *s_tok, int32_t *cids,
                            float *cprobs) {
   const int keff = P.keff;
-  const int tid = threadIdx.x;
+  const int tid = static_cast<int>(threadIdx.x) & (NT - 1);
   auto val = [&](int i) -> float { return i < n_sel ? key_val(lk[i]) : -1e30f; };
   auto idv = [&](int i) -> int { return i < n_sel ? key_idx(lk[i]) : -1; };
   const float mx = val(0);
@@ -160,142 +171,249 @@ __device__ int sample_list(const unsigned long long *lk, int n_sel,
       const float v = val(i);
       e[i] = (v >= thr) ? cr_expf(__fsub_rn(v, mx)) : -1.0f;           // :58-59
     }
-    __syncthreads();
+    grp_sync<NT>();
     if (tid == 0) {
+      // The list is sorted by value, so the entries the max-20 filter keeps
+      // are a prefix, in the reference's candidate order.
       float sum = 0.0f;
       int n = 0;
-      for (int i = 0; i < keff; i++)
-        if (e[i] >= 0.0f) {
-          order[n++] = i;
-          sum = __fadd_rn(sum, e[i]);                                   // :62
-        }
+      while (n < keff && e[n] >= 0.0f) sum = __fadd_rn(sum, e[n++]);   // :62
       int tok;
       if (n == 0) {
-        for (int i = 0; i < keff; i++) pr[i] = 0.0f;
         tok = idv(0);                                                   // :68-69
       } else {
         const float inv = __fdiv_rn(1.0f, sum);                         // :72
-        for (int i = 0; i < keff; i++)
-          pr[i] = e[i] >= 0.0f ? __fmul_rn(e[i], inv) : 0.0f;           // :73-74
-        // stable sort by probability descending (:77; glibc's qsort is a
-        // stable mergesort).  The list is already in value order, so this
-        // insertion sort is linear unless exp rounding ties reorder it.
-        for (int j = 1; j < n; j++) {
-          const int o = order[j];
-          const float po = pr[o];
-          int q = j - 1;
-          while (q >= 0 && po > pr[order[q]]) {
-            order[q + 1] = order[q];
-            q--;
-          }
-          order[q + 1] = o;
+        bool sorted = true;
+        for (int i = 0; i < n; i++) {
+          pr[i] = __fmul_rn(e[i], inv);                                 // :73-74
+          order[i] = i;
+          if (i > 0 && pr[i] > pr[i - 1]) sorted = false;
         }
+        if (!sorted) {
+          // stable sort by probability descending (:77; glibc's qsort is a
+          // stable mergesort).  Exp is monotone, so this never runs unless
+          // rounding ties reorder neighbours.
+          for (int j = 1; j < n; j++) {
+            const int o = order[j];
+            const float po = pr[o];
+            int q = j - 1;
+            while (q >= 0 && po > pr[order[q]]) {
+              order[q + 1] = order[q];
+              q--;
+            }
+            order[q + 1] = o;
+          }
+        }
+        // cumulative to the cutoff (:80-88); the truncated sum (:91-93) and
+        // the walk's CDF (:98-105) repeat exactly these additions, so the
+        // prefix sums are kept (in e[], no longer needed) and reused.
         float cum = 0.0f;
         int cutoff = n;
-        for (int j = 0; j < n; j++) {                                   // :80-88
+        for (int j = 0; j < n; j++) {
           cum = __fadd_rn(cum, pr[order[j]]);
+          e[j] = cum;
           if (cum >= P.p) {
             cutoff = j + 1;
             break;
           }
         }
-        float tr = 0.0f;
-        for (int j = 0; j < cutoff; j++) tr = __fadd_rn(tr, pr[order[j]]);  // :91-93
-        const float r = __fmul_rn(rng_next(rs), tr);                    // :96
-        float cdf = 0.0f;
+        const float r = __fmul_rn(rng_next(rs), e[cutoff - 1]);         // :96
         int res = order[0];
-        for (int j = 0; j < cutoff; j++) {                              // :98-105
-          cdf = __fadd_rn(cdf, pr[order[j]]);
-          if (r < cdf) {
+        for (int j = 0; j < cutoff; j++)
+          if (r < e[j]) {
             res = order[j];
             break;
           }
-        }
         tok = idv(res);
+        for (int i = n; i < keff; i++) pr[i] = 0.0f;
       }
+      if (n == 0)
+        for (int i = 0; i < keff; i++) pr[i] = 0.0f;
       *s_tok = tok;
     }
   } else {
     for (int i = tid; i < keff; i += NT) e[i] = cr_expf(__fsub_rn(val(i), mx));  // top_k.c:54
-    __syncthreads();
+    grp_sync<NT>();
     if (tid == 0) {
       float sum = 0.0f;
       for (int i = 0; i < keff; i++) sum = __fadd_rn(sum, e[i]);        // :55
-      for (int i = 0; i < keff; i++) pr[i] = __fdiv_rn(e[i], sum);      // :57-59
       const float r = rng_next(rs);                                     // :62
       float cdf = 0.0f;
       int tok = idv(0);                                                 // :72
-      for (int i = 0; i < keff; i++) {
+      int i = 0;
+      for (; i < keff; i++) {
+        pr[i] = __fdiv_rn(e[i], sum);                                   // :57-59
         cdf = __fadd_rn(cdf, pr[i]);
         if (r < cdf) {
           tok = idv(i);
+          i++;
           break;
         }
       }
+      for (; i < keff; i++) pr[i] = __fdiv_rn(e[i], sum);
       *s_tok = tok;
     }
   }
-  __syncthreads();
+  grp_sync<NT>();
   if (cids != nullptr)
     for (int i = tid; i < keff; i += NT) cids[i] = idv(i);
   if (cprobs != nullptr)
     for (int i = tid; i < keff; i += NT) cprobs[i] = pr[i];
   const int tok = *s_tok;
-  __syncthreads();
+  grp_sync<NT>();
   return tok;
 }
 
 // ---------------------------------------------------------------------------
 // slice_kernel
 // ---------------------------------------------------------------------------
-size_t slice_smem_bytes(int kcap, int hcap, int bm_words) {
-  return sizeof(unsigned long long) * static_cast<size_t>(kcap + kCapB) +
-         sizeof(uint32_t) * static_cast<size_t>(bm_words) +
-         sizeof(int32_t) * 2 * static_cast<size_t>(hcap) +
+constexpr int kMaxStages = 16;       // bulk-copy ring depth limit (per launch: A.nstages)
+constexpr int kStageBytes = 8192;    // bytes per ring stage
+constexpr uint32_t kHashEmpty = 0xFFFFFFFFu;
+
+// Open-addressing table of the slice's history ids with their counts.  The
+// table has at least twice as many slots as ids, so probes end.
+__device__ __forceinline__ void hash_insert(uint32_t *hk, uint32_t *hn, uint32_t mask,
+                                            uint32_t shift, uint32_t t) {
+  uint32_t h = (t * 0x9E3779B1u) >> shift;
+  for (uint32_t i = 0; i <= mask; i++) {
+    const uint32_t prev = atomicCAS(&hk[h], kHashEmpty, t);
+    if (prev == kHashEmpty || prev == t) {
+      atomicAdd(&hn[h], 1u);
+      return;
+    }
+    h = (h + 1) & mask;
+  }
+}
+
+__device__ __forceinline__ int hash_count(const uint32_t *hk, const uint32_t *hn, uint32_t mask,
+                                          uint32_t shift, uint32_t t) {
+  uint32_t h = (t * 0x9E3779B1u) >> shift;
+  for (uint32_t i = 0; i <= mask; i++) {
+    const uint32_t k = hk[h];
+    if (k == t) return static_cast<int>(hn[h]);
+    if (k == kHashEmpty) return 0;
+    h = (h + 1) & mask;
+  }
+  return 0;
+}
+
+// 16 bytes of a staged chunk (shared memory) as VEC floats.
+template <typename T>
+struct Vec16S;
+template <>
+struct Vec16S<float> {
+  __device__ __forceinline__ static void load(const unsigned char *s, int vi, float *x) {
+    const float4 q = reinterpret_cast<const float4 *>(s)[vi];
+    x[0] = q.x;
+    x[1] = q.y;
+    x[2] = q.z;
+    x[3] = q.w;
+  }
+};
+template <>
+struct Vec16S<uint16_t> {
+  __device__ __forceinline__ static void load(const unsigned char *s, int vi, float *x) {
+    const uint4 q = reinterpret_cast<const uint4 *>(s)[vi];
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      x[2 * j] = __uint_as_float(w[j] << 16);
+      x[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  }
+};
+
+constexpr int kTQ = 4;          // keys kept per thread in registers
+constexpr int kTQK = 64;        // lists up to this long use the register queues
+
+// Shared memory of slice_kernel:
+//   ring   nstages x kStageBytes   (bulk-copy stages; reused for the merges)
+//   cbuf   max(the threads' queues, the block buffer) keys
+//   hash   2 x hts words
+//   fin    3 x kcap words          (list arithmetic)
+__host__ __device__ inline int slice_cbuf_keys(int kcap) {
+  const int queue_keys = kSliceThreads * kTQ;
+  const int block_keys = kcap + kCapB;
+  return queue_keys > block_keys ? queue_keys : block_keys;
+}
+
+size_t slice_smem_bytes(int kcap, int hts, int nstages) {
+  return static_cast<size_t>(nstages) * kStageBytes +
+         sizeof(unsigned long long) * static_cast<size_t>(slice_cbuf_keys(kcap)) +
+         sizeof(uint32_t) * 2 * static_cast<size_t>(hts) +
          (sizeof(float) * 2 + sizeof(int)) * static_cast<size_t>(kcap);
 }
 
+// Ring depth for a launch: the stages that fit beside the other shared
+// buffers within ~70 KB of dynamic shared memory (with the ~3.5 KB of static
+// shared memory and the 1 KB per-CTA reservation, three CTAs fit in an SM's
+// 228 KB), at least 4 (the finalizer merges up to 4096 keys in the ring).
+int slice_stages(int kcap, int hts) {
+  const size_t other = slice_smem_bytes(kcap, hts, 0);
+  const size_t budget = 70 * 1024;
+  int ns = other < budget ? static_cast<int>((budget - other) / kStageBytes) : 0;
+  return ns < 4 ? 4 : (ns > kMaxStages ? kMaxStages : ns);
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kSliceThreads)
+__global__ void __launch_bounds__(kSliceThreads, 3)
     slice_kernel(const SliceArgs A) {
   constexpr int NT = kSliceThreads;
+  constexpr int NW = NT / 32;
   constexpr int VEC = Vec16<T>::N;
-  constexpr int EPT = 16;
-  constexpr int UV = EPT / VEC;
+  constexpr int VPT = kStageBytes / 16 / NT;  // 16-byte vectors per thread per stage
+  constexpr int EPT = VPT * VEC;              // elements per thread per stage
+  constexpr int XPT = 16;                     // extra-round items per thread
   constexpr int MAXPER = (PZ_TOP_K_MAX + kCapB) / NT;
 
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   __shared__ SelShared sh;
-  __shared__ unsigned long long s_red[NT / 32];
-  __shared__ int s_nh, s_last, s_x0nan, s_tok;
+  __shared__ unsigned long long s_red[NW];
+  __shared__ int s_wn[NW];
+  __shared__ __align__(8) uint64_t s_bar[kMaxStages];
+  __shared__ int s_rel[kMaxStages];   // warps done with a ring slot
+  __shared__ int s_issued;
+  __shared__ unsigned long long s_tau;  // block admission bound
+  __shared__ unsigned long long s_max[NT];  // each thread's best key so far
+  __shared__ unsigned long long s_dk;   // largest discarded key of the block
+  __shared__ int s_x0nan, s_tok, s_timeout;
 
   const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.y, sl = blockIdx.x;
   const pz_sampler_config cfg = A.cfg[row];
   const RowPlan P = plan_row(cfg, A.V_global);
   const int a = sl * A.L;
   const int b = min(A.V, a + A.L);
-  const int cap = A.kcap + kCapB;
-  const int hwm = A.kcap + kCapB / 2;
 
-  unsigned long long *cand = reinterpret_cast<unsigned long long *>(smem);
-  uint32_t *bitmap = reinterpret_cast<uint32_t *>(cand + cap);
-  int32_t *hl = reinterpret_cast<int32_t *>(bitmap + A.bm_words);
-  int32_t *hc = hl + A.hcap;
-  float *fe = reinterpret_cast<float *>(hc + A.hcap);
+  unsigned char *ring = smem;
+  const int NS = A.nstages;
+  unsigned long long *cbuf = reinterpret_cast<unsigned long long *>(smem + NS * kStageBytes);
+  uint32_t *hk = reinterpret_cast<uint32_t *>(cbuf + slice_cbuf_keys(A.kcap));
+  uint32_t *hn = hk + A.hts;
+  float *fe = reinterpret_cast<float *>(hn + A.hts);
   float *fp = fe + A.kcap;
   int *ford = reinterpret_cast<int *>(fp + A.kcap);
+  const uint32_t hmask = static_cast<uint32_t>(A.hts - 1);
+  const uint32_t hshift = static_cast<uint32_t>(A.hshift);
 
   const T *rowp = static_cast<const T *>(A.logits) + static_cast<size_t>(row) * static_cast<size_t>(A.ld);
   const bool greedy = P.mode == kModeGreedy;
   // a list longer than this launch was sized for (hint broken): flag the row
   const bool bad_k = P.mode == kModeTopK && (P.keff > A.kmax || P.keff > A.kcap);
   const int k_sel = (P.mode == kModeTopK && !bad_k) ? P.keff : 1;
-  const bool use_buf = k_sel > 1;
+  // lists up to kTQK long: per-thread register queues of the TQ best keys,
+  // merged per CTA (exact unless a thread discarded a key that would have
+  // made the list, which is detected and redone); longer lists: one
+  // block-wide buffer.
+  const bool use_tq = k_sel > 1 && k_sel <= kTQK;
+  const bool use_block = k_sel > kTQK;
   const unsigned long long tau0 = (P.mode == kModeTopK) ? key_topk_floor() : 0ull;
   const uint32_t goff = static_cast<uint32_t>(A.v_offset);
+  const int cap = A.kcap + kCapB;         // block list buffer
+  const int hwm = A.kcap + kCapB / 2;
 
-  // ---- penalty history of this slice: sorted ids, counts, bitmap --------
   int H = 0;
   const int32_t *hrow = nullptr;
   if (A.hist != nullptr && A.hist_off != nullptr && P.pen_on) {
@@ -304,47 +422,9 @@ __global__ void __launch_bounds__(kSliceThreads)
     hrow = A.hist + h0;
   }
   const bool too_long = H > A.hcap;
-  const bool hist_on = H > 0 && !too_long;
-  if (tid == 0) {
-    s_nh = 0;
-    s_x0nan = 0;
-    sh.n = 0;
-    sh.tau = tau0;
-  }
-  if (hist_on)
-    for (int w = tid; w < A.bm_words; w += NT) bitmap[w] = 0u;
-  __syncthreads();
-  int nh = 0;
-  if (hist_on) {
-    for (int j = tid; j < H; j += NT) {
-      const long long t = static_cast<long long>(hrow[j]) - A.v_offset;
-      if (t >= a && t < b) hl[atomicAdd(&s_nh, 1)] = static_cast<int>(t);
-    }
-    __syncthreads();
-    nh = s_nh;
-    int np2 = 1;
-    while (np2 < nh) np2 <<= 1;
-    for (int i = nh + tid; i < np2; i += NT) hl[i] = INT_MAX;
-    block_sort_asc_i32<NT>(hl, np2);
-    for (int i = tid; i < nh; i += NT) {
-      const int t = hl[i];
-      if (i == nh - 1 || hl[i + 1] != t) {
-        int lo = 0, hi = i;
-        while (lo < hi) {
-          const int mid = (lo + hi) >> 1;
-          if (hl[mid] < t) lo = mid + 1; else hi = mid;
-        }
-        hc[i] = i - lo + 1;
-        const int o = t - a;
-        atomicOr(&bitmap[o >> 5], 1u << (o & 31));
-      } else {
-        hc[i] = 0;
-      }
-    }
-    __syncthreads();
-  }
+  const bool hist_on = H > 0 && !too_long && A.hts > 0;
 
-  // ---- stream the slice: 16-byte vectors, scalar head and tail ----------
+  // ---- aligned body streamed through the bulk-copy ring ------------------
   const uintptr_t addr = reinterpret_cast<uintptr_t>(rowp + a);
   int head = static_cast<int>(((16u - (addr & 15u)) & 15u) / sizeof(T));
   if (head > b - a) head = b - a;
@@ -352,65 +432,318 @@ __global__ void __launch_bounds__(kSliceThreads)
   const int nvec = (b - a_al) / VEC;
   const int b_al = a_al + nvec * VEC;
   const int tail = b - b_al;
-  const T *vbase = rowp + a_al;
+  const unsigned char *body = reinterpret_cast<const unsigned char *>(rowp + a_al);
+  const int body_bytes = nvec * 16;
+  const int nst = (body_bytes + kStageBytes - 1) / kStageBytes;
 
-  unsigned long long best = 0ull;
-  for (int v0 = 0; v0 < nvec; v0 += NT * UV) {
-    float xv[EPT];
-    uint32_t hb[UV];
-    uint32_t ok = 0;
-#pragma unroll
-    for (int u = 0; u < UV; u++) {
-      const int vi = v0 + u * NT + tid;
-      hb[u] = 0;
-      if (vi < nvec) {
-        Vec16<T>::load(vbase, vi, xv + u * VEC);
-        ok |= ((1u << VEC) - 1u) << (u * VEC);
-        if (hist_on) {
-          const int o = a_al + vi * VEC - a;
-          const uint32_t w0 = bitmap[o >> 5], w1 = bitmap[(o >> 5) + 1];
-          hb[u] = __funnelshift_r(w0, w1, o & 31) & ((1u << VEC) - 1u);
-        }
-      } else {
-#pragma unroll
-        for (int w = 0; w < VEC; w++) xv[u * VEC + w] = 0.0f;
-      }
+  auto issue = [&](int st) {
+    const int buf = st % NS;
+    const int off = st * kStageBytes;
+    const int bytes = min(kStageBytes, body_bytes - off);
+    // No proxy fence here: the slot's readers finished (syncwarp, block
+    // fence, release count) before the last of them issues the refill, and a
+    // fence.proxy.async per copy would wait for the copies already in flight.
+    mbar_expect_tx(&s_bar[buf], static_cast<uint32_t>(bytes));
+    bulk_load(ring + buf * kStageBytes, body + off, static_cast<uint32_t>(bytes), &s_bar[buf]);
+  };
+
+  if (tid == 0) {
+    for (int i = 0; i < NS; i++) {
+      mbar_init(&s_bar[i], 1);
+      s_rel[i] = 0;
     }
-    unsigned long long keys[EPT];
-    uint32_t valid = 0;
-#pragma unroll
-    for (int e = 0; e < EPT; e++) {
-      const int u = e / VEC, w = e % VEC;
-      keys[e] = 0ull;
-      if ((ok >> e) & 1u) {
-        if ((hb[u] >> w) & 1u) continue;
-        const int li = a_al + (v0 + u * NT + tid) * VEC + w;
-        const float v = greedy ? xv[e] : temper(xv[e], P);
-        if (v != v) {
-          if (li == 0 && goff == 0) s_x0nan = 1;
-          continue;
-        }
-        keys[e] = mkkey(v, static_cast<uint32_t>(li) + goff);
-        valid |= 1u << e;
-      }
-    }
-    if (use_buf) {
-      offer_round<NT, MAXPER, EPT>(cand, cap, hwm, k_sel, sh, keys, valid);
-    } else {
-#pragma unroll
-      for (int e = 0; e < EPT; e++)
-        if (((valid >> e) & 1u) && keys[e] > best) best = keys[e];
-    }
+    mbar_init_fence();
+    s_x0nan = 0;
+    s_timeout = 0;
+    s_tau = tau0;
+    s_dk = tau0;
+  }
+  s_max[tid] = tau0;
+  if (tid == 0) {
+    sh.n = 0;
+    sh.tau = tau0;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    s_issued = min(NS, nst);
+    for (int i = 0; i < min(NS, nst); i++) issue(i);
   }
 
-  // head, tail, and the penalised history ids, as extra rounds
-  const int n_extra = head + tail + (hist_on ? nh : 0);
-  for (int base = 0; base < n_extra; base += NT * EPT) {
-    unsigned long long keys[EPT];
-    uint32_t valid = 0;
+  // ---- the slice's history ids and counts (while the first copies fly) ---
+  if (hist_on) {
+    for (int i = tid; i < A.hts; i += NT) {
+      hk[i] = kHashEmpty;
+      hn[i] = 0u;
+    }
+    __syncthreads();
+    for (int j = tid; j < H; j += NT) {
+      const long long t = static_cast<long long>(hrow[j]) - A.v_offset;
+      if (t >= a && t < b) hash_insert(hk, hn, hmask, hshift, static_cast<uint32_t>(t));
+    }
+    __syncthreads();
+  }
+  auto in_hist = [&](int li) -> bool {
+    return hist_on && hash_count(hk, hn, hmask, hshift, static_cast<uint32_t>(li)) > 0;
+  };
+
+  // register queue of this thread's best keys (descending), the largest key
+  // it discarded, and their values for the cheap float tests
+  unsigned long long qk[kTQ];
 #pragma unroll
-    for (int e = 0; e < EPT; e++) {
-      keys[e] = 0ull;
+  for (int j = 0; j < kTQ; j++) qk[j] = tau0;
+  float q_lo = key_val(tau0);           // value of qk[kTQ-1]
+  unsigned long long dk = tau0;         // largest discarded key
+  float dv = key_val(tau0);
+  unsigned long long best = 0ull;       // argmax path
+  float best_f = -INFINITY;
+  float tau_f = key_val(tau0);          // block path
+  // Warp-uniform admission bound: a key that is certainly not above the
+  // slice's k-th best (queues) or its best (argmax).  Values below it are
+  // dropped with one compare.  Shared through s_tau with the other warps.
+  unsigned long long tau_w = tau0;
+  float tau_wf = tau0 == 0ull ? -INFINITY : key_val(tau0);
+  const int jq = (k_sel + kTQ - 1) / kTQ;   // lanes whose queues cover k keys
+  int st_fail = -1;
+  const float nanf_ = __int_as_float(0x7FC00000);
+
+  // Puts `key` (> qk[kTQ-1]) into the queue; the key pushed out becomes a
+  // discard.
+  auto q_insert = [&](unsigned long long key) {
+    unsigned long long ev = qk[kTQ - 1];
+#pragma unroll
+    for (int j = kTQ - 1; j > 0; j--) {
+      if (key > qk[j - 1]) {
+        qk[j] = qk[j - 1];
+      } else if (key > qk[j]) {
+        qk[j] = key;
+      }
+    }
+    if (key > qk[0]) qk[0] = key;
+    if (ev > dk) {
+      dk = ev;
+      dv = key_val(ev);
+    }
+    q_lo = key_val(qk[kTQ - 1]);
+  };
+  // Offers element (v, li) in this thread's index order (stream): a value
+  // equal to the queue's last one comes later, so it loses the tie.
+  auto offer_stream = [&](float v, int li) {
+    if (use_tq) {
+      if (v > q_lo) {
+        if (!in_hist(li)) q_insert(mkkey(v, static_cast<uint32_t>(li) + goff));
+      } else if (v >= dv) {
+        if (!in_hist(li)) {
+          const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
+          if (key > dk) {
+            dk = key;
+            dv = v;
+          }
+        }
+      }
+    } else if (v >= best_f && !in_hist(li)) {
+      const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
+      if (key > best) {
+        best = key;
+        best_f = v;
+      }
+    }
+  };
+  // Raises the warp bound to the jq-th largest of the lanes' smallest queue
+  // keys: those jq lanes hold jq * kTQ >= k distinct keys at or above it.
+  auto refresh_bound = [&]() {  // argmax path: the warp's best so far
+    const unsigned long long cand_b = warp_max_u64(best);
+    if (cand_b > tau_w) {
+      tau_w = cand_b;
+      tau_wf = key_val(cand_b);
+      if (lane == 0) atomicMax(&s_tau, cand_b);
+    }
+  };
+  // Offers a key out of index order (extra round): full key comparisons.
+  auto offer_key = [&](unsigned long long key) {
+    if (use_tq) {
+      if (key > qk[kTQ - 1]) {
+        q_insert(key);
+      } else if (key > dk) {
+        dk = key;
+        dv = key_val(key);
+      }
+    } else if (key > best) {
+      best = key;
+      best_f = key_val(key);
+    }
+  };
+
+  int st_done = 0;  // stages this thread consumed
+  for (int st = 0; st < nst; st++) {
+    if (*reinterpret_cast<volatile int *>(&s_timeout)) {
+      st_fail = st;
+      break;
+    }
+    const int buf = st % NS;
+    const bool ok = mbar_wait(&s_bar[buf], static_cast<uint32_t>((st / NS) & 1), kWaitBudget);
+    if (!ok) {
+      s_timeout = 1;
+      st_fail = st;
+      break;
+    }
+    st_done = st + 1;
+    const unsigned char *sb = ring + buf * kStageBytes;
+    const int v0 = st * (kStageBytes / 16);
+    const int nv = min(kStageBytes / 16, nvec - v0);
+    // fast pass: tempered values and their max; NaN marks an empty lane
+    float vv[EPT];
+    float vmax = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < VPT; u++) {
+      const int j = u * NT + tid;
+      float xv[VEC];
+      if (j < nv) {
+        Vec16S<T>::load(sb, j, xv);
+      } else {
+#pragma unroll
+        for (int w = 0; w < VEC; w++) xv[w] = nanf_;
+      }
+#pragma unroll
+      for (int w = 0; w < VEC; w++) vv[u * VEC + w] = xv[w];
+    }
+    if (!greedy) {
+      if (P.divide) {
+#pragma unroll
+        for (int e = 0; e < EPT; e++) vv[e] = __fdiv_rn(vv[e], P.T);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPT; e++) vv[e] = __fmul_rn(vv[e], P.inv_T);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < EPT; e++) vmax = fmaxf(vmax, vv[e]);
+    // This warp is done with the stage (vmax depends on every value it read,
+    // so the shared loads have completed): release the slot.  The last warp
+    // to release it refills it with stage st + NS; no one waits, and no
+    // fence is needed (a fence in a thread with bulk copies in flight would
+    // wait for them).
+    __syncwarp();
+    if (lane == 0 && atomicAdd(&s_rel[buf], vmax == vmax ? 1 : 1) == NW - 1) {
+      s_rel[buf] = 0;
+      if (st + NS < nst && !*reinterpret_cast<volatile int *>(&s_timeout)) {
+        issue(st + NS);
+        atomicMax(&s_issued, st + NS + 1);
+      }
+    }
+    if (use_block) {
+      // only a value >= the admission threshold can still enter the list
+      if (__syncthreads_or(vmax >= tau_f)) {
+        unsigned long long keys[EPT];
+        uint32_t valid = 0;
+#pragma unroll
+        for (int e = 0; e < EPT; e++) {
+          keys[e] = 0ull;
+          if (vv[e] >= tau_f) {
+            const int li = a_al + (v0 + (e / VEC) * NT + tid) * VEC + (e % VEC);
+            if (in_hist(li)) continue;
+            keys[e] = mkkey(vv[e], static_cast<uint32_t>(li) + goff);
+            valid |= 1u << e;
+          }
+        }
+        offer_round<NT, MAXPER, EPT>(cbuf, cap, hwm, k_sel, sh, keys, valid);
+        tau_f = key_val(sh.tau);
+      }
+    } else {
+      if (use_tq) {
+        // Per-thread exact queue: only values above this thread's own
+        // threshold (its 4th best, or its largest discard) need work.  The
+        // pending elements are handled one per iteration, so the warp loops
+        // over the largest per-lane count, not over every slot.
+        // values below the block bound cannot make the list
+        const float thr = fmaxf(fminf(q_lo, dv), tau_wf);
+        const unsigned long long top0 = qk[0];
+        uint32_t pend = 0;
+#pragma unroll
+        for (int e = 0; e < EPT; e++) pend |= (vv[e] >= thr) ? (1u << e) : 0u;
+        while (__any_sync(0xFFFFFFFFu, pend != 0)) {
+          if (pend) {
+            const int e = __ffs(pend) - 1;
+            pend &= pend - 1;
+            float v = vv[0];
+#pragma unroll
+            for (int j = 1; j < EPT; j++) v = (e == j) ? vv[j] : v;
+            const int li = a_al + (v0 + (e / VEC) * NT + tid) * VEC + (e % VEC);
+            if (!in_hist(li)) {
+              const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
+              if (key > tau_w) {
+                if (key > qk[kTQ - 1]) {
+                  q_insert(key);
+                } else if (key > dk) {
+                  dk = key;
+                  dv = v;
+                }
+              }
+            }
+          }
+        }
+        if (qk[0] != top0) s_max[tid] = qk[0];
+        if (warp == 0 && ((st + 2) & (st + 1)) == 0) {
+          // After stages 0, 1, 3, 7, ...: the k-th largest of the threads'
+          // best keys is a lower bound on the slice's k-th best (k distinct
+          // elements are at or above it); maxima only grow, so stale
+          // entries keep it valid.
+          unsigned long long mv[NW];
+#pragma unroll
+          for (int r = 0; r < NW; r++) mv[r] = *reinterpret_cast<volatile unsigned long long *>(&s_max[r * 32 + lane]);
+          const unsigned long long bnd = warp_jth_reg<NW>(mv, k_sel);
+          if (lane == 0 && bnd > tau0) atomicMax(&s_tau, bnd);
+        }
+      } else if (__any_sync(0xFFFFFFFFu, vmax >= tau_wf)) {
+        // argmax: one warp-uniform test per stage against the best so far
+        bool changed = false;
+        if (vmax >= tau_wf) {
+#pragma unroll
+          for (int e = 0; e < EPT; e++) {
+            if (!(vv[e] >= tau_wf)) continue;
+            const int li = a_al + (v0 + (e / VEC) * NT + tid) * VEC + (e % VEC);
+            if (in_hist(li)) continue;
+            const unsigned long long key = mkkey(vv[e], static_cast<uint32_t>(li) + goff);
+            if (key > best) {
+              best = key;
+              changed = true;
+            }
+          }
+        }
+        if (__any_sync(0xFFFFFFFFu, changed)) refresh_bound();
+      }
+      const unsigned long long sb_tau = *reinterpret_cast<volatile unsigned long long *>(&s_tau);
+      if (sb_tau > tau_w) {
+        tau_w = sb_tau;
+        tau_wf = key_val(sb_tau);
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0 && s_timeout) {
+    // a wait ran out: wait (bounded) for the copies still in flight
+    for (int s2 = st_done; s2 < s_issued; s2++)
+      mbar_wait(&s_bar[s2 % NS], static_cast<uint32_t>((s2 / NS) & 1), kDrainBudget);
+  }
+  if (s_timeout && st_fail < 0) st_fail = nst;
+  const bool timed_out = st_fail >= 0;
+
+  // ---- head, tail and the penalised history ids as extra rounds -----------
+  if (a == 0 && goff == 0 && tid == 0) {
+    float x = load_scalar<T>(rowp, 0);
+    const int c = hist_on ? hash_count(hk, hn, hmask, hshift, 0u) : 0;
+    if (c > 0) x = penalize(x, c, P);
+    const float v = greedy ? x : temper(x, P);
+    s_x0nan = (v != v) ? 1 : 0;
+  }
+  const int n_extra = head + tail + (hist_on ? A.hts : 0);
+  for (int base = 0; base < n_extra; base += NT * XPT) {
+    float xv[XPT];
+    int lis[XPT];
+    uint32_t have = 0;
+#pragma unroll
+    for (int e = 0; e < XPT; e++) {
+      xv[e] = nanf_;
+      lis[e] = 0;
       const int it = base + e * NT + tid;
       if (it >= n_extra) continue;
       int li, cnt = 0;
@@ -420,121 +753,210 @@ __global__ void __launch_bounds__(kSliceThreads)
         li = b_al + (it - head);
       } else {
         const int i = it - head - tail;
-        cnt = hc[i];
-        if (cnt == 0) continue;
-        li = hl[i];
+        if (hk[i] == kHashEmpty) continue;
+        li = static_cast<int>(hk[i]);
+        cnt = static_cast<int>(hn[i]);
       }
-      if (cnt == 0 && hist_on) {
-        const int o = li - a;
-        if ((bitmap[o >> 5] >> (o & 31)) & 1u) continue;
-      }
+      if (cnt == 0 && in_hist(li)) continue;
       float x = load_scalar<T>(rowp, li);
       if (cnt > 0) x = penalize(x, cnt, P);
-      const float v = greedy ? x : temper(x, P);
-      if (v != v) {
-        if (li == 0 && goff == 0) s_x0nan = 1;
-        continue;
-      }
-      keys[e] = mkkey(v, static_cast<uint32_t>(li) + goff);
-      valid |= 1u << e;
+      xv[e] = greedy ? x : temper(x, P);
+      lis[e] = li;
+      have |= 1u << e;
     }
-    if (use_buf) {
-      offer_round<NT, MAXPER, EPT>(cand, cap, hwm, k_sel, sh, keys, valid);
+    if (use_block) {
+      unsigned long long keys[XPT];
+      uint32_t valid = 0;
+#pragma unroll
+      for (int e = 0; e < XPT; e++) {
+        keys[e] = 0ull;
+        if (((have >> e) & 1u) && xv[e] == xv[e]) {
+          keys[e] = mkkey(xv[e], static_cast<uint32_t>(lis[e]) + goff);
+          valid |= 1u << e;
+        }
+      }
+      offer_round<NT, MAXPER, XPT>(cbuf, cap, hwm, k_sel, sh, keys, valid);
     } else {
 #pragma unroll
-      for (int e = 0; e < EPT; e++)
-        if (((valid >> e) & 1u) && keys[e] > best) best = keys[e];
+      for (int e = 0; e < XPT; e++)
+        if (((have >> e) & 1u) && xv[e] == xv[e])
+          offer_key(mkkey(xv[e], static_cast<uint32_t>(lis[e]) + goff));
     }
   }
 
-  // ---- this slice's list -> scratch ------------------------------------
-  int m;
-  unsigned long long *dst =
-      A.slice_keys + (static_cast<size_t>(row) * A.S + sl) * static_cast<size_t>(A.kcap);
-  if (use_buf) {
-    __syncthreads();
+  // ---- this slice's list -> scratch (one warp) ---------------------------
+  unsigned long long *ring_keys = reinterpret_cast<unsigned long long *>(ring);
+  __syncthreads();
+  if (use_block) {
     int n = sh.n < cap ? sh.n : cap;
     __syncthreads();
     if (n > k_sel) {
-      block_select<NT, MAXPER>(cand, n, k_sel, sh);
+      block_select<NT, MAXPER>(cbuf, n, k_sel, sh);
       n = k_sel;
     }
-    m = n;
-    for (int i = tid; i < m; i += NT) dst[i] = cand[i];
+    if (tid == 0) s_wn[0] = n;
+  } else if (use_tq) {
+    s_max[tid] = qk[0];
+#pragma unroll
+    for (int j = 0; j < kTQ; j++) cbuf[tid * kTQ + j] = qk[j];
+    const unsigned long long d = warp_max_u64(dk);
+    if (lane == 0) atomicMax(&s_dk, d);
   } else {
-    best = block_max_u64<NT>(best, s_red);
-    m = best > tau0 ? 1 : 0;
-    if (tid == 0 && m) dst[0] = best;
+    best = warp_max_u64(best);
+    if (lane == 0) s_red[warp] = best;
   }
   __syncthreads();
-  if (tid == 0) {
-    A.slice_cnt[static_cast<size_t>(row) * A.S + sl] = m;
-    if (a == 0) A.row_flags[row] = s_x0nan ? 1u : 0u;
+  bool exact_rescan = false;
+  if (use_tq) {
+    if (warp == 0) {
+      // A lower bound on the slice's k-th best key: the k-th largest of
+      // the threads' best keys.  Queue keys at or above it -> ring_keys,
+      // then the best k_sel of those.
+      unsigned long long v8[NW];
+#pragma unroll
+      for (int r = 0; r < NW; r++) v8[r] = s_max[r * 32 + lane];
+      const unsigned long long bnd = warp_jth_reg<NW>(v8, k_sel);
+      const unsigned long long lo = bnd > tau0 ? bnd - 1ull : tau0;
+      int n = 0;
+      for (int base = 0; base < NT * kTQ; base += 32) {
+        const unsigned long long key = cbuf[base + lane];
+        const bool r = key > lo;
+        const uint32_t bal = __ballot_sync(0xFFFFFFFFu, r);
+        if (r) ring_keys[n + __popc(bal & lanemask_lt())] = key;
+        n += __popc(bal);
+      }
+      __syncwarp();
+      unsigned long long kth = tau0;  // fewer than k real keys: any real discard counts
+      if (n >= k_sel) {
+        kth = warp_kth(ring_keys, n, k_sel);
+        n = warp_compact_ge(ring_keys, n, kth);
+      }
+      // exact unless some thread pushed out a key that beats the k-th
+      if (lane == 0) {
+        s_wn[0] = n;
+        s_tok = s_dk > kth ? 1 : 0;
+      }
+    }
+    __syncthreads();
+    exact_rescan = s_tok != 0;
   }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const unsigned int prev = atomicAdd(&A.row_arrive[row], 1u);
-    s_last = (prev == static_cast<unsigned int>(A.S - 1));
-  }
-  __syncthreads();
-  if (!s_last) return;
-
-  // ======================= last CTA of the row ==========================
-  __threadfence();
-  if (tid == 0) A.row_arrive[row] = 0u;
-  const int S = A.S;
-  const unsigned long long *sk = A.slice_keys + static_cast<size_t>(row) * S * static_cast<size_t>(A.kcap);
-  const int32_t *sc = A.slice_cnt + static_cast<size_t>(row) * S;
-  int n_sel = 0;
-  unsigned long long gbest = 0ull;
-  if (use_buf) {
+  if (exact_rescan) {
+    // rare: redo the slice exactly with the block-wide buffer (all threads)
     if (tid == 0) {
       sh.n = 0;
       sh.tau = tau0;
     }
     __syncthreads();
-    const int total = S * A.kcap;
-    for (int base = 0; base < total; base += NT * EPT) {
-      unsigned long long keys[EPT];
+    for (int base = a; base < b; base += NT * XPT) {
+      unsigned long long keys[XPT];
       uint32_t valid = 0;
 #pragma unroll
-      for (int e = 0; e < EPT; e++) {
+      for (int e = 0; e < XPT; e++) {
         keys[e] = 0ull;
-        const int it = base + e * NT + tid;
-        if (it < total) {
-          const int s2 = it / A.kcap, j = it - s2 * A.kcap;
-          if (j < __ldcg(sc + s2)) {
-            keys[e] = __ldcg(sk + it);
+        const int li = base + e * NT + tid;
+        if (li < b) {
+          float x = load_scalar<T>(rowp, li);
+          const int c = hist_on ? hash_count(hk, hn, hmask, hshift, static_cast<uint32_t>(li)) : 0;
+          if (c > 0) x = penalize(x, c, P);
+          const float v = temper(x, P);
+          if (v == v) {
+            keys[e] = mkkey(v, static_cast<uint32_t>(li) + goff);
             valid |= 1u << e;
           }
         }
       }
-      offer_round<NT, MAXPER, EPT>(cand, cap, hwm, k_sel, sh, keys, valid);
+      offer_round<NT, MAXPER, XPT>(cbuf, cap, hwm, k_sel, sh, keys, valid);
     }
     __syncthreads();
     int n = sh.n < cap ? sh.n : cap;
     __syncthreads();
     if (n > k_sel) {
-      block_select<NT, MAXPER>(cand, n, k_sel, sh);
+      block_select<NT, MAXPER>(cbuf, n, k_sel, sh);
       n = k_sel;
     }
+    if (tid == 0) s_wn[0] = n;
+    __syncthreads();
+  }
+  if (warp != 0) return;
+
+  int m = 0;
+  unsigned long long *dst =
+      A.slice_keys + (static_cast<size_t>(row) * A.S + sl) * static_cast<size_t>(A.kcap);
+  if (use_block || exact_rescan) {
+    m = s_wn[0];
+    for (int i = lane; i < m; i += 32) dst[i] = cbuf[i];
+  } else if (use_tq) {
+    m = s_wn[0];
+    for (int i = lane; i < m; i += 32) dst[i] = ring_keys[i];
+  } else {
+    unsigned long long bl = lane < NW ? s_red[lane] : 0ull;
+    bl = warp_max_u64(bl);
+    m = bl > tau0 ? 1 : 0;
+    if (lane == 0 && m) dst[0] = bl;
+  }
+  if (lane == 0) {
+    A.slice_cnt[static_cast<size_t>(row) * A.S + sl] = m | (timed_out ? (1 << 30) : 0);
+    if (a == 0) A.row_flags[row] = s_x0nan ? 1u : 0u;
+  }
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    const unsigned int prev = atomicAdd(&A.row_arrive[row], 1u);
+    last = (prev == static_cast<unsigned int>(A.S - 1));
+  }
+  last = __shfl_sync(0xFFFFFFFFu, last, 0);
+  if (!last) return;
+
+  // ================== last CTA of the row: warp 0 finishes ===============
+  __threadfence();
+  if (lane == 0) {
+    A.row_arrive[row] = 0u;
+    if (A.row_tau != nullptr) A.row_tau[row] = 0ull;
+  }
+  const int S = A.S;
+  const unsigned long long *sk = A.slice_keys + static_cast<size_t>(row) * S * static_cast<size_t>(A.kcap);
+  const int32_t *sc = A.slice_cnt + static_cast<size_t>(row) * S;
+  bool row_timed_out = timed_out;
+  int n_sel = 0;
+  unsigned long long gbest = 0ull;
+  unsigned long long *lst = ring_keys;  // merged list, sorted below
+  if (P.mode == kModeTopK && !bad_k && k_sel > 1) {
+    int n = 0;
+    for (int s2 = 0; s2 < S; s2++) {
+      const int raw = __ldcg(sc + s2);
+      row_timed_out |= ((raw >> 30) & 1) != 0;
+      const int c = raw & 0xFFFF;
+      for (int i = lane; i < c; i += 32) lst[n + i] = __ldcg(sk + static_cast<size_t>(s2) * A.kcap + i);
+      n += c;
+    }
+    __syncwarp();
+    if (n > k_sel) {
+      const unsigned long long kth = warp_kth(lst, n, k_sel);
+      n = warp_compact_ge(lst, n, kth);
+    }
     n_sel = n;
-    for (int i = n_sel + tid; i < A.kcap; i += NT) cand[i] = 0ull;
-    block_sort_desc<NT>(cand, A.kcap);
+    for (int i = n_sel + lane; i < A.kcap; i += 32) lst[i] = 0ull;
+    warp_sort_desc(lst, A.kcap);
   } else {
     unsigned long long bl = 0ull;
-    for (int s2 = tid; s2 < S; s2 += NT)
-      if (__ldcg(sc + s2) > 0) {
+    for (int s2 = lane; s2 < S; s2 += 32) {
+      const int raw = __ldcg(sc + s2);
+      if ((raw >> 30) & 1) bl = ~0ull;  // marker below
+      if ((raw & 0xFFFF) > 0) {
         const unsigned long long k = __ldcg(sk + static_cast<size_t>(s2) * A.kcap);
-        bl = k > bl ? k : bl;
+        if (bl != ~0ull) bl = k > bl ? k : bl;
       }
-    gbest = block_max_u64<NT>(bl, s_red);
+    }
+    const bool any_to = __any_sync(0xFFFFFFFFu, bl == ~0ull);
+    row_timed_out |= any_to;
+    if (bl == ~0ull) bl = 0ull;
+    gbest = warp_max_u64(bl);
     if (P.mode == kModeTopK) {  // k_eff == 1: the single best admitted key
       n_sel = gbest > tau0 ? 1 : 0;
-      if (tid == 0) cand[0] = gbest;
-      for (int i = 1 + tid; i < A.kcap; i += NT) cand[i] = 0ull;
-      __syncthreads();
+      if (lane == 0) lst[0] = gbest;
+      for (int i = 1 + lane; i < A.kcap; i += 32) lst[i] = 0ull;
+      __syncwarp();
     }
   }
   const bool x0nan = (__ldcg(A.row_flags + row) & 1u) != 0u;
@@ -544,17 +966,18 @@ __global__ void __launch_bounds__(kSliceThreads)
     // allgather (merge_kernel).
     unsigned long long *ek = A.emit_keys + static_cast<size_t>(row) * (A.kcap + 1);
     int cnt;
-    if (use_buf) {
+    if (P.mode == kModeTopK && !bad_k) {
       cnt = n_sel;
-      for (int i = tid; i < cnt; i += NT) ek[i] = cand[i];
+      for (int i = lane; i < cnt; i += 32) ek[i] = lst[i];
     } else {
       cnt = gbest > tau0 ? 1 : 0;
-      if (tid == 0 && cnt) ek[0] = gbest;
+      if (lane == 0 && cnt) ek[0] = gbest;
     }
-    if (tid == 0)
+    if (lane == 0)
       ek[A.kcap] = static_cast<unsigned long long>(cnt | (x0nan ? (1 << 30) : 0) |
                                                    (too_long ? (1 << 29) : 0) |
-                                                   (bad_k ? (1 << 28) : 0));
+                                                   (bad_k ? (1 << 28) : 0) |
+                                                   (row_timed_out ? (1 << 27) : 0));
     return;
   }
 
@@ -563,7 +986,10 @@ __global__ void __launch_bounds__(kSliceThreads)
   int status = too_long ? PZ_ROW_HISTORY_TOO_LONG : PZ_ROW_OK;
   bool pending = false;
   const bool want_cand = A.cand_ids != nullptr || A.cand_probs != nullptr;
-  if (too_long) {
+  if (row_timed_out) {
+    tok = -1;
+    status = PZ_ROW_TIMEOUT;
+  } else if (too_long) {
     tok = -1;                                             // penalties could not be applied
   } else if (bad_k) {
     tok = -1;
@@ -573,8 +999,17 @@ __global__ void __launch_bounds__(kSliceThreads)
   } else if (P.mode == kModeTopK) {
     int32_t *cids = A.cand_ids ? A.cand_ids + static_cast<size_t>(row) * A.cand_stride : nullptr;
     float *cprobs = A.cand_probs ? A.cand_probs + static_cast<size_t>(row) * A.cand_stride : nullptr;
-    tok = sample_list<NT>(cand, n_sel, P, rs, fe, fp, ford, &s_tok,
+    int t = INT_MIN;
+    if (P.keff <= 64) {
+      // warp-parallel, rounding exactly like the reference's loops
+      t = warp_sample_list<2>(lst, n_sel, P, rs, want_cand ? cprobs : nullptr);
+      if (t != INT_MIN && want_cand && cids != nullptr)
+        for (int i = lane; i < P.keff; i += 32) cids[i] = i < n_sel ? key_idx(lst[i]) : -1;
+    }
+    if (t == INT_MIN)
+      t = sample_list<32>(lst, n_sel, P, rs, fe, fp, ford, &s_tok,
                           want_cand ? cids : nullptr, want_cand ? cprobs : nullptr);
+    tok = t;
   } else if (P.mode == kModeTopPFull && A.V_global > PZ_TOP_P_MAX_VOCAB) {
     tok = x0nan ? 0 : key_idx(gbest);                     // top_p.c:33-34
   } else if (P.mode == kModeTopPFull && x0nan) {
@@ -584,21 +1019,21 @@ __global__ void __launch_bounds__(kSliceThreads)
     status = PZ_ROW_HINT_VIOLATED;
   } else {
     pending = true;
-    if (tid == 0) {
+    if (lane == 0) {
       A.row_best[row] = gbest;
       A.full_rows[atomicAdd(A.n_full, 1)] = row;
     }
   }
-  if (tid == 0) {
+  if (lane == 0) {
     if (!pending) {
       A.out[row] = tok;
       A.rng[row] = rs;
     }
-    if (A.n_cand) A.n_cand[row] = (P.mode == kModeTopK) ? P.keff : 0;
+    if (A.n_cand) A.n_cand[row] = (P.mode == kModeTopK && !bad_k && !too_long && !row_timed_out) ? P.keff : 0;
     if (A.row_status) A.row_status[row] = status;
   }
-  if (want_cand && P.mode != kModeTopK) {
-    for (int i = tid; i < A.cand_stride; i += NT) {
+  if (want_cand && (P.mode != kModeTopK || bad_k || too_long || row_timed_out)) {
+    for (int i = lane; i < A.cand_stride; i += 32) {
       if (A.cand_ids) A.cand_ids[static_cast<size_t>(row) * A.cand_stride + i] = -1;
       if (A.cand_probs) A.cand_probs[static_cast<size_t>(row) * A.cand_stride + i] = 0.0f;
     }
@@ -619,7 +1054,7 @@ size_t full_smem_bytes(int V, int hcap) {
 // a segment elements keep their order, so equal keys keep input order.
 // Returns true when the result is in (k1, v1).
 template <int NT>
-__device__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32_t *k1,
+__device__ __noinline__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32_t *k1,
                                  uint32_t *v1, int n, uint32_t *whist,
                                  uint32_t *tot, int *s_flag) {
   constexpr int NW = NT / 32;
@@ -690,7 +1125,7 @@ __device__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32_t *k1,
 template <typename T>
 __global__ void __launch_bounds__(kFullThreads, 1) full_kernel(const FullArgs A) {
   constexpr int NT = kFullThreads;
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   __shared__ SeqShared ssh;
   __shared__ int s_red[NT / 32];
   __shared__ int s_nh, s_flag;
@@ -836,7 +1271,7 @@ __global__ void __launch_bounds__(kSliceThreads) merge_kernel(const MergeArgs A)
   constexpr int NT = kSliceThreads;
   constexpr int EPT = 16;
   constexpr int MAXPER = (PZ_TOP_K_MAX + kCapB) / NT;
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   __shared__ SelShared sh;
   __shared__ unsigned long long s_red[NT / 32];
   __shared__ int s_tok, s_flags;
@@ -863,8 +1298,8 @@ __global__ void __launch_bounds__(kSliceThreads) merge_kernel(const MergeArgs A)
   auto gcount = [&](int g) -> int {
     return static_cast<int>(A.gathered[(static_cast<size_t>(g) * A.B + row) * stride + A.kcap]);
   };
-  auto gn = [&](int g) -> int { return min(gcount(g) & ((1 << 28) - 1), A.kcap); };
-  if (tid < A.G) atomicOr(&s_flags, gcount(tid) & (7 << 28));
+  auto gn = [&](int g) -> int { return min(gcount(g) & ((1 << 27) - 1), A.kcap); };
+  if (tid < A.G) atomicOr(&s_flags, gcount(tid) & (15 << 27));
   int n_sel = 0;
   unsigned long long gbest = 0ull;
   if (use_buf) {
@@ -917,11 +1352,15 @@ __global__ void __launch_bounds__(kSliceThreads) merge_kernel(const MergeArgs A)
   const bool x0nan = (s_flags >> 30) & 1;
   const bool too_long = (s_flags >> 29) & 1;
   const bool bad_k = ((s_flags >> 28) & 1) || (P.mode == kModeTopK && !k_fits);
+  const bool timed_out = (s_flags >> 27) & 1;
   unsigned long long rs = A.rng[row];
   int tok = -1;
   int status = too_long ? PZ_ROW_HISTORY_TOO_LONG : PZ_ROW_OK;
   const bool want_cand = A.cand_ids != nullptr || A.cand_probs != nullptr;
-  if (too_long) {
+  if (timed_out) {
+    tok = -1;
+    status = PZ_ROW_TIMEOUT;
+  } else if (too_long) {
     tok = -1;
   } else if (bad_k) {
     tok = -1;
@@ -965,9 +1404,18 @@ __global__ void rng_seed_kernel(unsigned long long *s, int B,
 // ---------------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------------
+// Opt-in dynamic shared memory: the device's per-block maximum minus the
+// largest static shared footprint of these kernels (< 4 KB).
+int max_dynamic_smem() {
+  int dev = 0, optin = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  return optin - 4096;
+}
+
 cudaError_t set_kernel_attributes() {
   cudaError_t e;
-  const int big = 227 * 1024;
+  const int big = max_dynamic_smem();
   e = cudaFuncSetAttribute(slice_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(slice_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);

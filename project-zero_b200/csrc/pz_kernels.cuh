@@ -36,8 +36,10 @@ struct SliceArgs {
   int L;                // columns per CTA (multiple of 8)
   int kcap;             // power of two >= largest k_eff in the launch
   int kmax;             // declared largest k_eff (rows above it are rejected)
-  int hcap;             // power of two >= longest history (0: no history SMEM)
-  int bm_words;         // bitmap words per CTA
+  int hcap;             // longest history a row may have (0: no history)
+  int hts;              // history hash slots per CTA (power of two >= 2*hcap, or 0)
+  int hshift;           // 32 - log2(hts)
+  int nstages;          // bulk-copy ring depth
   int mode_emit;        // 1: write the merged local list (vocab sharding), no draw
   int no_full_vocab;
   // scratch
@@ -45,6 +47,7 @@ struct SliceArgs {
   int32_t *slice_cnt;              // [B*S]
   uint32_t *row_arrive;            // [B]
   uint32_t *row_flags;             // [B]
+  unsigned long long *row_tau;     // [B] shared list threshold (0 between calls)
   unsigned long long *row_best;    // [B]
   int32_t *full_rows;              // [B]
   int32_t *n_full;                 // [1]
@@ -99,7 +102,8 @@ struct MergeArgs {               // vocab-sharded merge after the allgather
 // Launchers (pz_kernels.cu).  Return cudaGetLastError() after the launch.
 cudaError_t launch_slice(const SliceArgs &a, int dtype, size_t smem,
                          cudaStream_t st);
-size_t slice_smem_bytes(int kcap, int hcap, int bm_words);
+size_t slice_smem_bytes(int kcap, int hts, int nstages);
+int slice_stages(int kcap, int hts);
 cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem,
                         cudaStream_t st);
 size_t full_smem_bytes(int V, int hcap);
@@ -110,5 +114,6 @@ cudaError_t launch_rng_seed(unsigned long long *s, int B,
                             unsigned long long base,
                             const unsigned long long *seeds, cudaStream_t st);
 cudaError_t set_kernel_attributes();
+int max_dynamic_smem();
 
 }  // namespace pz

@@ -32,12 +32,43 @@ struct SelShared {
 // sh.tau to the smallest kept key.  Requires k < n <= MAXPER * NT.
 // All threads of the block must call it.
 template <int NT, int MAXPER>
-__device__ void block_select(unsigned long long *cand, int n, int k,
+__device__ __noinline__ void block_select(unsigned long long *cand, int n, int k,
                             SelShared &sh) {
   const int tid = threadIdx.x;
+  const uint32_t lane = lane_id();
+  // Bytes shared by every key need no pass: start at the first byte where
+  // the smallest and largest keys differ (keys are unique, n >= 2).
+  unsigned long long mn = ~0ull, mx = 0ull;
+  for (int i = tid; i < n; i += NT) {
+    const unsigned long long key = cand[i];
+    mn = key < mn ? key : mn;
+    mx = key > mx ? key : mx;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long a = __shfl_xor_sync(0xFFFFFFFFu, mn, o);
+    const unsigned long long b = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+    mn = a < mn ? a : mn;
+    mx = b > mx ? b : mx;
+  }
   if (tid == 0) {
-    sh.prefix = 0;
-    sh.mask = 0;
+    sh.prefix = ~0ull;  // running min
+    sh.mask = 0ull;     // running max
+  }
+  __syncthreads();
+  if (lane == 0) {
+    atomicMin(&sh.prefix, mn);
+    atomicMax(&sh.mask, mx);
+  }
+  __syncthreads();
+  const unsigned long long gmin = sh.prefix, gmax = sh.mask;
+  const int lead = __clzll(static_cast<long long>(gmin ^ gmax));  // < 64
+  const int top_shift = 56 - 8 * (lead >> 3);
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned long long common = top_shift == 56 ? 0ull : (~0ull << (top_shift + 8));
+    sh.prefix = gmin & common;
+    sh.mask = common;
     sh.need = k;
     sh.done = 0;
     sh.kth = ~0ull;
@@ -46,14 +77,22 @@ __device__ void block_select(unsigned long long *cand, int n, int k,
     sh.above = 0;
   }
   __syncthreads();
-  for (int shift = 56; shift >= 0; shift -= 8) {
+  const int n_up = (n + NT - 1) / NT * NT;
+  for (int shift = top_shift; shift >= 0; shift -= 8) {
     for (int i = tid; i < 256; i += NT) sh.hist[i] = 0;
     __syncthreads();
     const unsigned long long prefix = sh.prefix, mask = sh.mask;
-    for (int i = tid; i < n; i += NT) {
-      const unsigned long long key = cand[i];
-      if ((key & mask) == prefix)
-        atomicAdd(&sh.hist[(key >> shift) & 0xFFu], 1u);
+    for (int i = tid; i < n_up; i += NT) {
+      bool act = false;
+      uint32_t d = 256u + lane;
+      if (i < n) {
+        const unsigned long long key = cand[i];
+        act = (key & mask) == prefix;
+        if (act) d = static_cast<uint32_t>((key >> shift) & 0xFFu);
+      }
+      const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
+      if (act && lane == static_cast<uint32_t>(__ffs(peers) - 1))
+        atomicAdd(&sh.hist[d], static_cast<uint32_t>(__popc(peers)));
     }
     __syncthreads();
     if (tid < kWarp) {
@@ -108,7 +147,6 @@ __device__ void block_select(unsigned long long *cand, int n, int k,
   }
   if (mymin != ~0ull) atomicMin(&sh.kth, mymin);
   __syncthreads();
-  const uint32_t lane = lane_id();
 #pragma unroll
   for (int j = 0; j < MAXPER; j++) {
     const uint32_t b = __ballot_sync(0xFFFFFFFFu, sel[j]);
@@ -201,7 +239,7 @@ __device__ void offer_round(unsigned long long *cand, int cap, int hwm, int k,
 // Bitonic sort of cand[0..npow2) descending (npow2 a power of two, padding
 // keys 0 sort last).  Block-wide call.
 template <int NT>
-__device__ void block_sort_desc(unsigned long long *cand, int npow2) {
+__device__ __noinline__ void block_sort_desc(unsigned long long *cand, int npow2) {
   for (int size = 2; size <= npow2; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       __syncthreads();

@@ -29,7 +29,8 @@ import os
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libpz_sampling.so")
+# PZ_SAMPLING_LIB may point at another build of the same library.
+LIB_PATH = os.environ.get("PZ_SAMPLING_LIB") or os.path.join(HERE, "libpz_sampling.so")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
@@ -96,6 +97,7 @@ def _sig(name, res, args):
 _sig("pz_status_str", ctypes.c_char_p, [ctypes.c_int])
 _sig("pz_version", ctypes.c_char_p, [])
 _sig("pz_last_error", ctypes.c_int, [])
+_sig("pz_last_error_detail", ctypes.c_char_p, [])
 _sig("pz_sample_argmax", ctypes.c_int, [_f32p, ctypes.c_int])
 _sig("pz_apply_temperature", None, [_f32p, ctypes.c_int, ctypes.c_float])
 _sig("pz_sample_top_p", ctypes.c_int, [_f32p, ctypes.c_int, ctypes.c_float, _u64p])
@@ -122,7 +124,9 @@ _sig("pz_sample_batch_vocab_sharded", ctypes.c_int,
 class PZError(RuntimeError):
     def __init__(self, status, what=""):
         self.status = status
-        super().__init__(f"{what}: {_lib.pz_status_str(status).decode()} (status {status})")
+        detail = _lib.pz_last_error_detail().decode()
+        super().__init__(f"{what}: {_lib.pz_status_str(status).decode()} (status {status})"
+                         + (f" [{detail}]" if detail else ""))
 
 
 def _check(status, what):

@@ -180,3 +180,25 @@ def test_vocab_sharded_single_rank(cuda, pz, golden):
     assert out.cpu().tolist() == case["tokens"]
     assert [int(v) for v in rng.cpu().numpy().view(np.uint64)] == case["rng_out"]
     s.close()
+
+
+def test_register_queue_overflow_falls_back_exactly(cuda, pz, oracle_lib):
+    """The per-thread queues keep 4 keys; when one thread's share of a slice
+    holds more of the list than that (large values at positions that all map
+    to the same thread), the kernel must detect it and redo the slice
+    exactly."""
+    rs = np.random.default_rng(5)
+    for dtype, period in [("f32", 1024), ("bf16", 2048)]:
+        B, V = 4, 65536
+        x = (rs.standard_normal((B, V)) * 0.5).astype(np.float32)
+        for r in range(B):
+            for i in range(60):
+                x[r, (i * period + (i % 4)) % V] = np.float32(8.0 + 0.01 * i + r)
+        logits = synth.to_bf16_bits(x) if dtype == "bf16" else x
+        for k, p in [(50, 0.9), (8, 1.0), (64, 0.5)]:
+            cfg = cases.configs(B, temperature=0.9, top_k=k, top_p=p)
+            d = dict(logits=logits, cfg=cfg, rng=np.arange(7, 7 + B, dtype=np.uint64), hist=None,
+                     hist_off=None)
+            g = run_gpu(cuda, pz, d, max_top_k=64, no_full_vocab=True)
+            mism, _, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+            assert mism == 0, (dtype, k)
