@@ -340,6 +340,8 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     return fail(PZ_ERR_CUDA);
   cudaError_t ce = pz::launch_slice(a, dtype, smem, st);
   if (ce != cudaSuccess) return fail_cuda(ce);
+  ce = pz::launch_finalize(a, st);
+  if (ce != cudaSuccess) return fail_cuda(ce);
   if (full_pass) {
     FullArgs f{};
     f.logits = logits;

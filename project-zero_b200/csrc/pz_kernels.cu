@@ -898,22 +898,45 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     A.slice_cnt[static_cast<size_t>(row) * A.S + sl] = m | (timed_out ? (1 << 30) : 0);
     if (a == 0) A.row_flags[row] = s_x0nan ? 1u : 0u;
   }
-  __threadfence();
-  __syncwarp();
-  int last = 0;
-  if (lane == 0) {
-    const unsigned int prev = atomicAdd(&A.row_arrive[row], 1u);
-    last = (prev == static_cast<unsigned int>(A.S - 1));
-  }
-  last = __shfl_sync(0xFFFFFFFFu, last, 0);
-  if (!last) return;
+}
 
-  // ================== last CTA of the row: warp 0 finishes ===============
-  __threadfence();
-  if (lane == 0) {
-    A.row_arrive[row] = 0u;
-    if (A.row_tau != nullptr) A.row_tau[row] = 0ull;
-  }
+// ---------------------------------------------------------------------------
+// finalize_kernel: one warp per row merges the row's slice lists into the
+// exact top-k (or argmax) and draws (reference list arithmetic), hands
+// full-vocabulary rows to full_kernel, or publishes the list (vocab
+// sharding).  Runs after slice_kernel on the same stream.
+// ---------------------------------------------------------------------------
+__host__ __device__ size_t finalize_smem_per_warp(int S, int kcap) {
+  const int merge = S * kcap > kcap ? S * kcap : kcap;
+  const size_t bytes = sizeof(unsigned long long) * static_cast<size_t>(merge) +
+                       (sizeof(float) * 2 + sizeof(int)) * static_cast<size_t>(kcap) + 16;
+  return (bytes + 15) / 16 * 16;  // each warp's region starts 16-byte aligned
+}
+
+__global__ void __launch_bounds__(128) finalize_kernel(const SliceArgs A, int warps_per_cta) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int row = blockIdx.x * warps_per_cta + warp;
+  if (row >= A.B) return;
+  const size_t per_warp = finalize_smem_per_warp(A.S, A.kcap);
+  unsigned char *base = smem + per_warp * warp;
+  const int merge_keys = A.S * A.kcap > A.kcap ? A.S * A.kcap : A.kcap;
+  unsigned long long *ring_keys = reinterpret_cast<unsigned long long *>(base);
+  float *fe = reinterpret_cast<float *>(ring_keys + merge_keys);
+  float *fp = fe + A.kcap;
+  int *ford = reinterpret_cast<int *>(fp + A.kcap);
+  int *s_tokp = ford + A.kcap;
+  int &s_tok = *s_tokp;
+
+  const pz_sampler_config cfg = A.cfg[row];
+  const RowPlan P = plan_row(cfg, A.V_global);
+  const bool bad_k = P.mode == kModeTopK && (P.keff > A.kmax || P.keff > A.kcap);
+  const int k_sel = (P.mode == kModeTopK && !bad_k) ? P.keff : 1;
+  const unsigned long long tau0 = (P.mode == kModeTopK) ? key_topk_floor() : 0ull;
+  int H = 0;
+  if (A.hist != nullptr && A.hist_off != nullptr && P.pen_on) H = A.hist_off[row + 1] - A.hist_off[row];
+  const bool too_long = H > A.hcap;
+  const bool timed_out = false;
   const int S = A.S;
   const unsigned long long *sk = A.slice_keys + static_cast<size_t>(row) * S * static_cast<size_t>(A.kcap);
   const int32_t *sc = A.slice_cnt + static_cast<size_t>(row) * S;
@@ -1424,6 +1447,8 @@ cudaError_t set_kernel_attributes() {
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(full_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   return e;
 }
@@ -1442,6 +1467,14 @@ cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem, cud
     full_kernel<float><<<grid, kFullThreads, smem, st>>>(a);
   else
     full_kernel<uint16_t><<<grid, kFullThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_finalize(const SliceArgs &a, cudaStream_t st) {
+  const size_t per_warp = finalize_smem_per_warp(a.S, a.kcap);
+  int w = 4;
+  while (w > 1 && per_warp * w > 96 * 1024) w >>= 1;
+  finalize_kernel<<<(a.B + w - 1) / w, 32 * w, per_warp * w, st>>>(a, w);
   return cudaGetLastError();
 }
 

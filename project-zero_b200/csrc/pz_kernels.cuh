@@ -104,6 +104,8 @@ cudaError_t launch_slice(const SliceArgs &a, int dtype, size_t smem,
                          cudaStream_t st);
 size_t slice_smem_bytes(int kcap, int hts, int nstages);
 int slice_stages(int kcap, int hts);
+cudaError_t launch_finalize(const SliceArgs &a, cudaStream_t st);
+__host__ __device__ size_t finalize_smem_per_warp(int S, int kcap);
 cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem,
                         cudaStream_t st);
 size_t full_smem_bytes(int V, int hcap);
