@@ -225,6 +225,39 @@ pz_status pz_sample_batch(pz_sampler_ctx *ctx, const void *logits,
                           const pz_batch_hints *hints,
                           const pz_batch_outputs *outputs, void *stream);
 
+/* Context-free, allocation-free form of pz_sample_batch.  No counterpart in
+ * the reference (whose sampler is a single-row CPU routine with no scratch):
+ * it exists for callers that may not allocate device memory at sampling
+ * time.  Its scratch is one fixed device array per device (about 2.1 MiB)
+ * sized for the limits below.
+ *   - Runs on the caller's CURRENT device.  The first call on a device does
+ *     the set-up (looks up the array's address and sets kernel attributes);
+ *     make that first call before any stream capture.  Later calls allocate
+ *     nothing and only launch kernels.
+ *   - B > PZ_STATIC_MAX_BATCH or V > PZ_STATIC_MAX_VOCAB: PZ_ERR_UNSUPPORTED
+ *     with the reason in pz_last_error_detail().  Rows whose top_k is 0 or
+ *     above PZ_STATIC_MAX_TOP_K (they would need a full-vocabulary pass or a
+ *     longer list) get token -1 and PZ_ROW_HINT_VIOLATED; rows with more
+ *     than PZ_STATIC_MAX_HISTORY history ids get PZ_ROW_HISTORY_TOO_LONG.
+ *   - outputs->cand_stride, when candidates are asked for, is at least
+ *     PZ_STATIC_MAX_TOP_K.
+ *   - Every call on a device shares the one array: calls that overlap in
+ *     time (two streams, two host threads without ordering) race and give
+ *     wrong tokens.  Order them on one stream or with events.
+ * Results are identical to pz_sample_batch's for the rows it accepts. */
+#define PZ_STATIC_MAX_BATCH 1024
+#define PZ_STATIC_MAX_VOCAB 1048576
+#define PZ_STATIC_MAX_TOP_K 64
+#define PZ_STATIC_MAX_HISTORY 1024
+pz_status pz_sample_batch_static(const void *logits, pz_dtype dtype, int B,
+                                 int V, int64_t ld,
+                                 const pz_sampler_config *cfg,
+                                 const int32_t *hist, const int32_t *hist_off,
+                                 unsigned long long *rng_state,
+                                 int32_t *out_tokens,
+                                 const pz_batch_outputs *outputs,
+                                 void *stream);
+
 /* Seeds B RNG states on the device: state[r] = seed_base + r (0 -> 1, as
  * rng_seed does), or state[r] = seeds[r] when `seeds` (device) is non-NULL. */
 pz_status pz_rng_seed_batch(unsigned long long *rng_state, int B,

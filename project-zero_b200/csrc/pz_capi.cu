@@ -6,6 +6,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -379,6 +380,120 @@ pz_status pz_sample_batch(pz_sampler_ctx *ctx, const void *logits,
                           const pz_batch_outputs *outputs, void *stream) {
   return sample_impl(ctx, logits, dtype, B, V, ld, 0, V, cfg, hist, hist_off,
                      rng_state, out_tokens, hints, outputs, stream, false);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// pz_sample_batch_static: the batched sampler with its scratch carved out of
+// one fixed device array (per device, zero at module load) instead of a
+// context's allocations.  Layout (bytes):
+//   slice lists  kStaticSlices x PZ_STATIC_MAX_TOP_K u64   (B*S <= kStaticSlices)
+//   slice counts kStaticSlices int32
+//   row words    row_tau, row_best (u64), row_arrive, row_flags, full_rows
+//                (32-bit), PZ_STATIC_MAX_BATCH each, then the n_full counter.
+// Every word this path reads is written earlier in the same call (slice
+// counts and lists by every slice CTA, row flags by slice 0), so nothing has
+// to be cleared between calls; the full-vocabulary counter, the one word that
+// must start at zero, is never touched because such rows are refused.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kStaticSlices = 4096;
+constexpr size_t kStaticOffCnt = sizeof(unsigned long long) * kStaticSlices * PZ_STATIC_MAX_TOP_K;
+constexpr size_t kStaticOffTau = kStaticOffCnt + sizeof(int32_t) * kStaticSlices;
+constexpr size_t kStaticOffBest = kStaticOffTau + sizeof(unsigned long long) * PZ_STATIC_MAX_BATCH;
+constexpr size_t kStaticOffArrive = kStaticOffBest + sizeof(unsigned long long) * PZ_STATIC_MAX_BATCH;
+constexpr size_t kStaticOffFlags = kStaticOffArrive + sizeof(uint32_t) * PZ_STATIC_MAX_BATCH;
+constexpr size_t kStaticOffFull = kStaticOffFlags + sizeof(uint32_t) * PZ_STATIC_MAX_BATCH;
+constexpr size_t kStaticOffNFull = kStaticOffFull + sizeof(int32_t) * PZ_STATIC_MAX_BATCH;
+constexpr size_t kStaticBytes = kStaticOffNFull + 256;
+static_assert(kStaticOffTau % 8 == 0 && kStaticOffArrive % 8 == 0, "u64 rows must stay aligned");
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticBytes];
+
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_mu;
+std::atomic<unsigned char *> g_static_base[kStaticMaxDevices];
+int g_static_sms[kStaticMaxDevices];
+
+pz_status fail_detail(pz_status s, const char *msg) {
+  g_last_error = s;
+  std::snprintf(g_detail, sizeof g_detail, "%s", msg);
+  return s;
+}
+
+// The array's address on device `dev` (the current device), looked up once.
+pz_status static_scratch(int dev, unsigned char **base, int *num_sms) {
+  unsigned char *p = g_static_base[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    p = g_static_base[dev].load(std::memory_order_relaxed);
+    if (p == nullptr) {
+      void *q = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&q, g_static_scratch);
+      if (e != cudaSuccess) return fail_cuda(e);
+      e = pz::set_kernel_attributes();
+      if (e != cudaSuccess) return fail_cuda(e);
+      int sms = 0;
+      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return fail_cuda(e);
+      g_static_sms[dev] = sms;
+      p = static_cast<unsigned char *>(q);
+      g_static_base[dev].store(p, std::memory_order_release);
+    }
+  }
+  *base = p;
+  *num_sms = g_static_sms[dev];
+  return PZ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+pz_status pz_sample_batch_static(const void *logits, pz_dtype dtype, int B,
+                                 int V, int64_t ld,
+                                 const pz_sampler_config *cfg,
+                                 const int32_t *hist, const int32_t *hist_off,
+                                 unsigned long long *rng_state,
+                                 int32_t *out_tokens,
+                                 const pz_batch_outputs *outputs,
+                                 void *stream) {
+  if (B > PZ_STATIC_MAX_BATCH || V > PZ_STATIC_MAX_VOCAB) {
+    char msg[160];
+    std::snprintf(msg, sizeof msg,
+                  "pz_sample_batch_static: B=%d V=%d beyond the static scratch's limits "
+                  "(B <= %d, V <= %d)", B, V, PZ_STATIC_MAX_BATCH, PZ_STATIC_MAX_VOCAB);
+    return fail_detail(PZ_ERR_UNSUPPORTED, msg);
+  }
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(PZ_ERR_NO_DEVICE);
+  if (dev < 0 || dev >= kStaticMaxDevices) return fail(PZ_ERR_UNSUPPORTED);
+  unsigned char *base = nullptr;
+  int sms = 0;
+  const pz_status s = static_scratch(dev, &base, &sms);
+  if (s != PZ_OK) return s;
+  // A context that owns nothing: its scratch pointers name the static array.
+  pz_sampler_ctx view;
+  view.device = dev;
+  view.num_sms = sms;
+  view.lim = pz_ctx_limits{PZ_STATIC_MAX_BATCH, PZ_STATIC_MAX_VOCAB, PZ_STATIC_MAX_TOP_K,
+                           PZ_STATIC_MAX_HISTORY};
+  view.kcap_max = PZ_STATIC_MAX_TOP_K;
+  view.hcap_max = PZ_STATIC_MAX_HISTORY;
+  view.slices_cap = kStaticSlices;
+  view.slice_keys = reinterpret_cast<unsigned long long *>(base);
+  view.slice_cnt = reinterpret_cast<int32_t *>(base + kStaticOffCnt);
+  view.row_tau = reinterpret_cast<unsigned long long *>(base + kStaticOffTau);
+  view.row_best = reinterpret_cast<unsigned long long *>(base + kStaticOffBest);
+  view.row_arrive = reinterpret_cast<uint32_t *>(base + kStaticOffArrive);
+  view.row_flags = reinterpret_cast<uint32_t *>(base + kStaticOffFlags);
+  view.full_rows = reinterpret_cast<int32_t *>(base + kStaticOffFull);
+  view.n_full = reinterpret_cast<int32_t *>(base + kStaticOffNFull);
+  const pz_batch_hints h{PZ_STATIC_MAX_TOP_K, PZ_STATIC_MAX_HISTORY, 1, 0};
+  return sample_impl(&view, logits, dtype, B, V, ld, 0, V, cfg, hist, hist_off, rng_state,
+                     out_tokens, &h, outputs, stream, false);
 }
 
 pz_status pz_rng_seed_batch(unsigned long long *rng_state, int B,

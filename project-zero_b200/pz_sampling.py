@@ -39,6 +39,7 @@ if not os.path.exists(LIB_PATH):
 _lib = ctypes.CDLL(LIB_PATH)
 
 PZ_OK = 0
+PZ_ERR_UNSUPPORTED = 6
 PZ_DTYPE_F32, PZ_DTYPE_BF16 = 0, 1
 PZ_CFG_TEMP_DIVIDE = 0x1
 PZ_ROW_OK, PZ_ROW_HISTORY_TOO_LONG, PZ_ROW_HINT_VIOLATED = 0, 1, 2
@@ -112,6 +113,9 @@ _sig("pz_sample_batch", ctypes.c_int,
      [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp,
       ctypes.POINTER(BatchHints), ctypes.POINTER(BatchOutputs), _vp])
 _sig("pz_rng_seed_batch", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_ulonglong, _vp, _vp])
+_sig("pz_sample_batch_static", ctypes.c_int,
+     [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp,
+      ctypes.POINTER(BatchOutputs), _vp])
 _sig("pz_row_shard", None, [ctypes.c_int, ctypes.c_int, ctypes.c_int,
                             ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)])
 _sig("pz_nccl_get_unique_id", ctypes.c_int, [_vp, ctypes.c_size_t])
@@ -327,6 +331,29 @@ class Sampler:
             _stream_handle(stream))
         _check(st, "pz_sample_batch_vocab_sharded")
         return out
+
+
+STATIC_MAX_BATCH = 1024
+STATIC_MAX_VOCAB = 1048576
+STATIC_MAX_TOP_K = 64
+STATIC_MAX_HISTORY = 1024
+
+
+def sample_static(logits, cfg, rng_state, out, hist=None, hist_off=None, *, cand_ids=None,
+                  cand_probs=None, n_cand=None, row_status=None, stream=None):
+    """pz_sample_batch_static: Sampler.sample without a context, on the
+    current CUDA device, with the library's fixed per-device scratch (no
+    allocation; B <= 1024, top_k 1..64, history <= 1024 ids per row).  The
+    first call on a device does the set-up.  Calls on one device must not
+    overlap in time: they share that scratch."""
+    B, V = logits.shape
+    outs = Sampler._outputs(cand_ids, cand_probs, n_cand, row_status)
+    st = _lib.pz_sample_batch_static(
+        _ptr(logits), Sampler._dtype_code(logits), B, V, logits.stride(0), _ptr(cfg), _ptr(hist),
+        _ptr(hist_off), _ptr(rng_state), _ptr(out),
+        ctypes.byref(outs) if outs is not None else None, _stream_handle(stream))
+    _check(st, "pz_sample_batch_static")
+    return out
 
 
 def seed_states(rng_state, seed_base=0, seeds=None, stream=None):
