@@ -420,7 +420,7 @@ def run_ours(args):
             "hbm_frac_of_peak_whole_step": (bpr * B / (total_ms / args.steps / 1000.0) / 1e9) / peak,
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": ke},
-            "gpu_launches": args.steps,
+            "gpu_launches": 2 * args.steps,  # slice_kernel + finalize_kernel per step
             "clocks": clk,
             "cpu_baseline": cpu,
         }

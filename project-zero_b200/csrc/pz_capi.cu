@@ -238,18 +238,18 @@ void pz_row_shard(int B, int world, int rank, int *begin, int *count) {
   if (count) *count = base + (rank < rem ? 1 : 0);
 }
 
-// Slices per row.  Enough CTAs for ~6.5 waves of the GPU at the kernel's
-// occupancy (fewer slices means less per-CTA setup, more slices means a
-// smaller last-wave tail), slices of at least 2048 columns, B*S within the
-// context's scratch, and S lists of the launch's list length fitting the
-// finalizer's merge area (4096 keys).
+// Slices per row: just enough CTAs to fill the GPU once at the kernel's
+// occupancy (every slice pays a setup and an end-of-slice merge, and with
+// one slice per row the row is decided inside slice_kernel), slices of at
+// least 2048 columns, B*S within the context's scratch, and S lists of the
+// launch's list length fitting the finalizer's merge area (4096 keys).
 static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
                           size_t smem, int *S_out, int *L_out) {
   const size_t per_sm = 228 * 1024;
   int occ = static_cast<int>(per_sm / (smem + 2048));
   occ = std::max(1, std::min(occ, 3));
-  const int target = static_cast<int>(c->num_sms * occ * 6.5);
-  int S = (target + B - 1) / B;
+  const int slots = c->num_sms * occ;
+  int S = (slots + B - 1) / B;
   // PZ_SLICES_PER_ROW: tuning override of the slice count
   static const int forced = [] {
     const char *e = std::getenv("PZ_SLICES_PER_ROW");

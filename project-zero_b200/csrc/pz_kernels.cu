@@ -14,6 +14,8 @@
 //                 and CDF walk of generate.c:158-167.
 //   merge_kernel  vocab sharding: merges the G gathered per-rank lists and
 //                 draws.
+#include <cuda_bf16.h>
+
 #include <climits>
 
 #include "pz_device.cuh"
@@ -264,12 +266,108 @@ __device__ __noinline__ int sample_list(const unsigned long long *lk, int n_sel,
   return tok;
 }
 
+// The decision for one row from its merged list (one warp): the draw (or
+// argmax), its outputs, a full-vocabulary hand-off to full_kernel, or the
+// published list (vocab sharding).  lst: sorted descending, n_sel real keys
+// then zeros up to kcap (top-k rows); gbest: the best key (other rows).
+// fe, fp, ford, s_tok: the warp's shared scratch of kcap entries each.
+__device__ __forceinline__ void finalize_row(const SliceArgs &A, int row, const RowPlan &P, bool bad_k,
+                                          bool too_long, bool row_timed_out, bool x0nan,
+                                          const unsigned long long *lst, int n_sel,
+                                          unsigned long long gbest, float *fe, float *fp, int *ford,
+                                          int *s_tokp) {
+  const int lane = threadIdx.x & 31;
+  int &s_tok = *s_tokp;
+  const unsigned long long tau0 = (P.mode == kModeTopK) ? key_topk_floor() : 0ull;
+  if (A.mode_emit) {
+    // vocab sharding: publish the local list; the draw happens after the
+    // allgather (merge_kernel).
+    unsigned long long *ek = A.emit_keys + static_cast<size_t>(row) * (A.kcap + 1);
+    int cnt;
+    if (P.mode == kModeTopK && !bad_k) {
+      cnt = n_sel;
+      for (int i = lane; i < cnt; i += 32) ek[i] = lst[i];
+    } else {
+      cnt = gbest > tau0 ? 1 : 0;
+      if (lane == 0 && cnt) ek[0] = gbest;
+    }
+    if (lane == 0)
+      ek[A.kcap] = static_cast<unsigned long long>(cnt | (x0nan ? (1 << 30) : 0) |
+                                                   (too_long ? (1 << 29) : 0) |
+                                                   (bad_k ? (1 << 28) : 0) |
+                                                   (row_timed_out ? (1 << 27) : 0));
+    return;
+  }
+
+  unsigned long long rs = A.rng[row];
+  int tok = -1;
+  int status = too_long ? PZ_ROW_HISTORY_TOO_LONG : PZ_ROW_OK;
+  bool pending = false;
+  const bool want_cand = A.cand_ids != nullptr || A.cand_probs != nullptr;
+  if (row_timed_out) {
+    tok = -1;
+    status = PZ_ROW_TIMEOUT;
+  } else if (too_long) {
+    tok = -1;                                             // penalties could not be applied
+  } else if (bad_k) {
+    tok = -1;
+    status = PZ_ROW_HINT_VIOLATED;
+  } else if (P.mode == kModeGreedy) {
+    tok = x0nan ? 0 : (gbest ? key_idx(gbest) : 0);       // argmax.c:3-13
+  } else if (P.mode == kModeTopK) {
+    int32_t *cids = A.cand_ids ? A.cand_ids + static_cast<size_t>(row) * A.cand_stride : nullptr;
+    float *cprobs = A.cand_probs ? A.cand_probs + static_cast<size_t>(row) * A.cand_stride : nullptr;
+    int t = INT_MIN;
+    if (P.keff <= 64) {
+      // element-wise steps across the warp, the sequential sums on one lane
+      t = warp_sample_small(lst, n_sel, P, rs, fe, fp, want_cand ? cprobs : nullptr);
+      if (t != INT_MIN && want_cand && cids != nullptr)
+        for (int i = lane; i < P.keff; i += 32) cids[i] = i < n_sel ? key_idx(lst[i]) : -1;
+    }
+    if (t == INT_MIN)
+      t = sample_list<32>(lst, n_sel, P, rs, fe, fp, ford, &s_tok,
+                          want_cand ? cids : nullptr, want_cand ? cprobs : nullptr);
+    tok = t;
+  } else if (P.mode == kModeTopPFull && A.V_global > PZ_TOP_P_MAX_VOCAB) {
+    tok = x0nan ? 0 : key_idx(gbest);                     // top_p.c:33-34
+  } else if (P.mode == kModeTopPFull && x0nan) {
+    tok = 0;                                              // NaN max: n == 0 -> argmax
+  } else if (A.no_full_vocab) {
+    tok = -1;
+    status = PZ_ROW_HINT_VIOLATED;
+  } else {
+    pending = true;
+    if (lane == 0) {
+      A.row_best[row] = gbest;
+      A.full_rows[atomicAdd(A.n_full, 1)] = row;
+    }
+  }
+  if (lane == 0) {
+    if (!pending) {
+      A.out[row] = tok;
+      A.rng[row] = rs;
+    }
+    if (A.n_cand) A.n_cand[row] = (P.mode == kModeTopK && !bad_k && !too_long && !row_timed_out) ? P.keff : 0;
+    if (A.row_status) A.row_status[row] = status;
+  }
+  if (want_cand && (P.mode != kModeTopK || bad_k || too_long || row_timed_out)) {
+    for (int i = lane; i < A.cand_stride; i += 32) {
+      if (A.cand_ids) A.cand_ids[static_cast<size_t>(row) * A.cand_stride + i] = -1;
+      if (A.cand_probs) A.cand_probs[static_cast<size_t>(row) * A.cand_stride + i] = 0.0f;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // slice_kernel
 // ---------------------------------------------------------------------------
-constexpr int kMaxStages = 16;       // bulk-copy ring depth limit (per launch: A.nstages)
-constexpr int kStageBytes = 8192;    // bytes per ring stage
+constexpr int kChunkBytes = 2048;    // one bulk copy: a warp's chunk of the slice
+constexpr int kSlots = 3;            // ring slots per warp (copies in flight per warp)
+constexpr int kSliceWarps = kSliceThreads / 32;
+constexpr int kLaneVecs = kChunkBytes / 16 / 32;  // 16-byte vectors per lane per chunk
 constexpr uint32_t kHashEmpty = 0xFFFFFFFFu;
+constexpr uint32_t kOrdNegInf = 0x007FFFFFu;      // f2ord(-inf)
+static_assert(kLaneVecs == 4, "the chunk loop is written for four vectors per lane");
 
 // Open-addressing table of the slice's history ids with their counts.  The
 // table has at least twice as many slots as ids, so probes end.
@@ -324,60 +422,186 @@ struct Vec16S<uint16_t> {
   }
 };
 
+// A lane's 16-byte vector of a chunk held in registers: its largest value
+// (NaN ignored, as fmaxf does) and element w.  `nan` fills the vectors past
+// the end of a short chunk.
+template <typename T>
+struct LaneVec;
+template <>
+struct LaneVec<float> {
+  static constexpr int N = 4;
+  static constexpr uint32_t nan = 0x7FC00000u;
+  __device__ __forceinline__ static float vmax(const uint4 &q) {
+    return fmaxf(fmaxf(__uint_as_float(q.x), __uint_as_float(q.y)),
+                 fmaxf(__uint_as_float(q.z), __uint_as_float(q.w)));
+  }
+  __device__ __forceinline__ static float elem(const uint4 &q, int w) {
+    return __uint_as_float(w == 0 ? q.x : w == 1 ? q.y : w == 2 ? q.z : q.w);
+  }
+  __device__ __forceinline__ static float smem(const unsigned char *s, int i) {
+    return reinterpret_cast<const float *>(s)[i];
+  }
+};
+template <>
+struct LaneVec<uint16_t> {
+  static constexpr int N = 8;
+  static constexpr uint32_t nan = 0x7FC07FC0u;
+  __device__ __forceinline__ static __nv_bfloat162 as2(uint32_t u) {
+    __nv_bfloat162 r;
+    memcpy(&r, &u, sizeof r);
+    return r;
+  }
+  __device__ __forceinline__ static float vmax(const uint4 &q) {
+    const __nv_bfloat162 m2 = __hmax2(__hmax2(as2(q.x), as2(q.y)), __hmax2(as2(q.z), as2(q.w)));
+    uint32_t m;
+    memcpy(&m, &m2, sizeof m);
+    return fmaxf(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
+  }
+  __device__ __forceinline__ static float elem(const uint4 &q, int w) {
+    const uint32_t u = (w >> 1) == 0 ? q.x : (w >> 1) == 1 ? q.y : (w >> 1) == 2 ? q.z : q.w;
+    return __uint_as_float((w & 1) ? (u & 0xFFFF0000u) : (u << 16));
+  }
+  __device__ __forceinline__ static float smem(const unsigned char *s, int i) {
+    return bf16_to_f32(reinterpret_cast<const uint16_t *>(s)[i]);
+  }
+};
+
+// A value v_b with at least k of the warp's 32*R values at or above it
+// (duplicates count): the k-th largest, resolved to `bits` bits below the
+// highest bit in which the values differ (fully resolved: exact).
+template <int R>
+__device__ __forceinline__ uint32_t warp_kth_u32(const uint32_t (&v)[R], int k, int bits) {
+  uint32_t lo = 0xFFFFFFFFu, hi = 0u;
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    lo = min(lo, v[r]);
+    hi = max(hi, v[r]);
+  }
+  lo = __reduce_min_sync(0xFFFFFFFFu, lo);
+  hi = __reduce_max_sync(0xFFFFFFFFu, hi);
+  if (lo == hi) return lo;
+  int b = 31 - __clz(static_cast<int>(lo ^ hi));
+  uint32_t mask = b == 31 ? 0u : (0xFFFFFFFFu << (b + 1));
+  uint32_t prefix = hi & mask;
+  int need = k;
+  const int stop = b - bits;
+  for (; b >= 0 && b > stop; b--) {
+    const uint32_t bit = 1u << b;
+    int cm = 0, c1 = 0;
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const bool m = (v[r] & mask) == prefix;
+      cm += m ? 1 : 0;
+      c1 += (m && (v[r] & bit)) ? 1 : 0;
+    }
+    cm = __reduce_add_sync(0xFFFFFFFFu, cm);
+    if (cm == need) break;  // every value under the prefix is in: the k-th is their minimum
+    c1 = __reduce_add_sync(0xFFFFFFFFu, c1);
+    if (c1 >= need) {
+      prefix |= bit;
+    } else {
+      need -= c1;
+    }
+    mask |= bit;
+  }
+  uint32_t m = 0xFFFFFFFFu;
+#pragma unroll
+  for (int r = 0; r < R; r++)
+    if ((v[r] & mask) == prefix) m = min(m, v[r]);
+  return __reduce_min_sync(0xFFFFFFFFu, m);
+}
+
+// Barrier `id` (not 0, which __syncthreads uses) over the first `count`
+// threads' warps; count a multiple of 32.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// The float just below x (x > -inf).
+__device__ __forceinline__ float prev_float(float x) {
+  if (x == 0.0f) return __int_as_float(static_cast<int>(0x80000001u));
+  const int b = __float_as_int(x);
+  return __int_as_float(x > 0.0f ? b - 1 : b + 1);
+}
+
+// A raw value r such that every x < r tempers below t (temperature is
+// monotone): start near the preimage t*T and step down until the float
+// below r tempers below t.  -inf when t is -inf (or on the way out).
+__device__ __noinline__ float raw_floor(float t, const RowPlan P) {
+  if (!(t > -INFINITY)) return -INFINITY;
+  float r = __fmul_rn(t, P.T);
+  for (int it = 0; it < 6 && r > -INFINITY; it++) {
+    const float pr = prev_float(r);
+    if (temper(pr, P) < t) return r;
+    r = pr;
+  }
+  return -INFINITY;
+}
+
+// Out of line so the streaming loops stay short.
+__device__ __noinline__ uint32_t kth_of_4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, int k,
+                                          int bits) {
+  const uint32_t v[4] = {a, b, c, d};
+  return warp_kth_u32<4>(v, k, bits);
+}
+__device__ __noinline__ uint32_t kth_of_maxima(const uint32_t *s_maxv, int k, int bits) {
+  const int lane = threadIdx.x & 31;
+  uint32_t v[kSliceWarps];
+#pragma unroll
+  for (int r = 0; r < kSliceWarps; r++) v[r] = *reinterpret_cast<const volatile uint32_t *>(&s_maxv[r * 32 + lane]);
+  return warp_kth_u32<kSliceWarps>(v, k, bits);
+}
+
 constexpr int kTQ = 4;          // keys kept per thread in registers
 constexpr int kTQK = 64;        // lists up to this long use the register queues
 
 // Shared memory of slice_kernel:
-//   ring   nstages x kStageBytes   (bulk-copy stages; reused for the merges)
-//   cbuf   max(the threads' queues, the block buffer) keys
+//   ring   NW x nslots x kChunkBytes  (per-warp bulk-copy rings; after the
+//          stream: the queues, the survivors and the rare exact rescan)
+//   cbuf   block buffer keys           (lists longer than kTQK only)
 //   hash   2 x hts words
-//   fin    3 x kcap words          (list arithmetic)
 __host__ __device__ inline int slice_cbuf_keys(int kcap) {
-  const int queue_keys = kSliceThreads * kTQ;
-  const int block_keys = kcap + kCapB;
-  return queue_keys > block_keys ? queue_keys : block_keys;
+  return kcap > kTQK ? kcap + kCapB : 0;
 }
 
-size_t slice_smem_bytes(int kcap, int hts, int nstages) {
-  return static_cast<size_t>(nstages) * kStageBytes +
+size_t slice_smem_bytes(int kcap, int hts, int nslots) {
+  return static_cast<size_t>(nslots) * kSliceWarps * kChunkBytes +
          sizeof(unsigned long long) * static_cast<size_t>(slice_cbuf_keys(kcap)) +
-         sizeof(uint32_t) * 2 * static_cast<size_t>(hts) +
-         (sizeof(float) * 2 + sizeof(int)) * static_cast<size_t>(kcap);
+         sizeof(uint32_t) * 2 * static_cast<size_t>(hts);
 }
 
-// Ring depth for a launch: the stages that fit beside the other shared
-// buffers within ~70 KB of dynamic shared memory (with the ~3.5 KB of static
-// shared memory and the 1 KB per-CTA reservation, three CTAs fit in an SM's
-// 228 KB), at least 4 (the finalizer merges up to 4096 keys in the ring).
-int slice_stages(int kcap, int hts) {
-  const size_t other = slice_smem_bytes(kcap, hts, 0);
-  const size_t budget = 70 * 1024;
-  int ns = other < budget ? static_cast<int>((budget - other) / kStageBytes) : 0;
-  return ns < 4 ? 4 : (ns > kMaxStages ? kMaxStages : ns);
-}
+// Ring slots per warp: kSlots chunks of 2 KB in flight per warp (48 KB per
+// CTA; with the history table, three CTAs fit in an SM's 228 KB).  The
+// end-of-slice merge needs 16 KB of the ring and the rescan buffer
+// kTQK + kCapB keys, both well inside it.
+int slice_stages(int, int) { return kSlots; }
 
+// One CTA per (row, slice of L columns).  The slice's 16-byte-aligned body
+// is cut into chunks of kChunkBytes; warp w streams chunks w, w + NW, ...
+// through its own ring of bulk copies (its lane 0 issues them and refills a
+// slot as soon as the warp has read it), so warps never wait for one
+// another while streaming.  Per chunk a lane reads four 16-byte vectors and
+// takes their maximum; temperature is monotone, so the tempered maximum
+// decides with one compare whether any of the lane's values can still
+// matter.  Only those values are tempered, keyed and offered.
 template <typename T>
 __global__ void __launch_bounds__(kSliceThreads, 3)
     slice_kernel(const SliceArgs A) {
   constexpr int NT = kSliceThreads;
-  constexpr int NW = NT / 32;
-  constexpr int VEC = Vec16<T>::N;
-  constexpr int VPT = kStageBytes / 16 / NT;  // 16-byte vectors per thread per stage
-  constexpr int EPT = VPT * VEC;              // elements per thread per stage
+  constexpr int NW = kSliceWarps;
+  constexpr int VEC = LaneVec<T>::N;          // elements per 16-byte vector
+  constexpr int HPT = 2 * VEC;                // block path: elements per offer
   constexpr int XPT = 16;                     // extra-round items per thread
   constexpr int MAXPER = (PZ_TOP_K_MAX + kCapB) / NT;
 
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ SelShared sh;
   __shared__ unsigned long long s_red[NW];
-  __shared__ int s_wn[NW];
-  __shared__ __align__(8) uint64_t s_bar[kMaxStages];
-  __shared__ int s_rel[kMaxStages];   // warps done with a ring slot
-  __shared__ int s_issued;
-  __shared__ unsigned long long s_tau;  // block admission bound
-  __shared__ unsigned long long s_max[NT];  // each thread's best key so far
+  __shared__ uint32_t s_maxv[NT];       // ordered value of each thread's best key
+  __shared__ uint32_t s_tauv;           // ordered value: the block's admission bound
+  __shared__ uint32_t s_b0;             // first bound, combined over the warps
   __shared__ unsigned long long s_dk;   // largest discarded key of the block
-  __shared__ int s_x0nan, s_tok, s_timeout;
+  __shared__ int s_x0nan, s_timeout, s_cnt, s_n, s_rescan;
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
@@ -387,14 +611,12 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   const int a = sl * A.L;
   const int b = min(A.V, a + A.L);
 
+  constexpr int NS = kSlots;
   unsigned char *ring = smem;
-  const int NS = A.nstages;
-  unsigned long long *cbuf = reinterpret_cast<unsigned long long *>(smem + NS * kStageBytes);
+  unsigned long long *cbuf =
+      reinterpret_cast<unsigned long long *>(smem + static_cast<size_t>(NW) * NS * kChunkBytes);
   uint32_t *hk = reinterpret_cast<uint32_t *>(cbuf + slice_cbuf_keys(A.kcap));
   uint32_t *hn = hk + A.hts;
-  float *fe = reinterpret_cast<float *>(hn + A.hts);
-  float *fp = fe + A.kcap;
-  int *ford = reinterpret_cast<int *>(fp + A.kcap);
   const uint32_t hmask = static_cast<uint32_t>(A.hts - 1);
   const uint32_t hshift = static_cast<uint32_t>(A.hshift);
 
@@ -403,13 +625,14 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   // a list longer than this launch was sized for (hint broken): flag the row
   const bool bad_k = P.mode == kModeTopK && (P.keff > A.kmax || P.keff > A.kcap);
   const int k_sel = (P.mode == kModeTopK && !bad_k) ? P.keff : 1;
-  // lists up to kTQK long: per-thread register queues of the TQ best keys,
+  // lists up to kTQK long: per-thread register queues of the kTQ best keys,
   // merged per CTA (exact unless a thread discarded a key that would have
   // made the list, which is detected and redone); longer lists: one
   // block-wide buffer.
   const bool use_tq = k_sel > 1 && k_sel <= kTQK;
   const bool use_block = k_sel > kTQK;
   const unsigned long long tau0 = (P.mode == kModeTopK) ? key_topk_floor() : 0ull;
+  const float tau0_f = tau0 == 0ull ? -INFINITY : key_val(tau0);
   const uint32_t goff = static_cast<uint32_t>(A.v_offset);
   const int cap = A.kcap + kCapB;         // block list buffer
   const int hwm = A.kcap + kCapB / 2;
@@ -424,7 +647,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   const bool too_long = H > A.hcap;
   const bool hist_on = H > 0 && !too_long && A.hts > 0;
 
-  // ---- aligned body streamed through the bulk-copy ring ------------------
+  // ---- aligned body, cut into chunks --------------------------------------
   const uintptr_t addr = reinterpret_cast<uintptr_t>(rowp + a);
   int head = static_cast<int>(((16u - (addr & 15u)) & 15u) / sizeof(T));
   if (head > b - a) head = b - a;
@@ -434,39 +657,53 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   const int tail = b - b_al;
   const unsigned char *body = reinterpret_cast<const unsigned char *>(rowp + a_al);
   const int body_bytes = nvec * 16;
-  const int nst = (body_bytes + kStageBytes - 1) / kStageBytes;
+  const int nchunks = (body_bytes + kChunkBytes - 1) / kChunkBytes;
+  const int nw = nchunks > warp ? (nchunks - warp + NW - 1) / NW : 0;  // this warp's chunks
+  unsigned char *wring = ring + static_cast<size_t>(warp) * NS * kChunkBytes;
 
-  auto issue = [&](int st) {
-    const int buf = st % NS;
-    const int off = st * kStageBytes;
-    const int bytes = min(kStageBytes, body_bytes - off);
-    // No proxy fence here: the slot's readers finished (syncwarp, block
-    // fence, release count) before the last of them issues the refill, and a
-    // fence.proxy.async per copy would wait for the copies already in flight.
-    mbar_expect_tx(&s_bar[buf], static_cast<uint32_t>(bytes));
-    bulk_load(ring + buf * kStageBytes, body + off, static_cast<uint32_t>(bytes), &s_bar[buf]);
+  // Warp-local chunk i (global chunk warp + NW*i) into ring slot `slot`:
+  // each lane copies the four vectors it will read (u*32 + lane); in the
+  // slice's last, short chunk the lanes past its end store NaN instead, so
+  // the readers need no bounds tests.
+  const unsigned char *lsrc = body + static_cast<size_t>(warp) * kChunkBytes + lane * 16;
+  unsigned char *ldst = wring + lane * 16;
+  auto issue = [&](int i, int slot) {
+    const int c = warp + NW * i;
+    const unsigned char *src = lsrc + static_cast<size_t>(i) * (NW * kChunkBytes);
+    unsigned char *dst = ldst + slot * kChunkBytes;
+    if (c != nchunks - 1) {
+#pragma unroll
+      for (int u = 0; u < kLaneVecs; u++) cp_async16(dst + u * 512, src + u * 512);
+    } else {
+      const int cv = (body_bytes - c * kChunkBytes) >> 4;
+#pragma unroll
+      for (int u = 0; u < kLaneVecs; u++) {
+        if (u * 32 + lane < cv)
+          cp_async16(dst + u * 512, src + u * 512);
+        else
+          *reinterpret_cast<uint4 *>(dst + u * 512) =
+              make_uint4(LaneVec<T>::nan, LaneVec<T>::nan, LaneVec<T>::nan, LaneVec<T>::nan);
+      }
+    }
   };
 
   if (tid == 0) {
-    for (int i = 0; i < NS; i++) {
-      mbar_init(&s_bar[i], 1);
-      s_rel[i] = 0;
-    }
-    mbar_init_fence();
     s_x0nan = 0;
     s_timeout = 0;
-    s_tau = tau0;
+    s_cnt = 0;
+    s_tauv = f2ord(tau0_f);
+    s_b0 = 0xFFFFFFFFu;
     s_dk = tau0;
-  }
-  s_max[tid] = tau0;
-  if (tid == 0) {
     sh.n = 0;
     sh.tau = tau0;
   }
+  s_maxv[tid] = kOrdNegInf;
   __syncthreads();
-  if (tid == 0) {
-    s_issued = min(NS, nst);
-    for (int i = 0; i < min(NS, nst); i++) issue(i);
+  // one copy group per chunk slot, empty past the end, so that "chunk i has
+  // landed" is always "at most NS - 1 groups pending"
+  for (int i = 0; i < NS; i++) {
+    if (i < nw) issue(i, i);
+    cp_async_commit();
   }
 
   // ---- the slice's history ids and counts (while the first copies fly) ---
@@ -491,24 +728,18 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   unsigned long long qk[kTQ];
 #pragma unroll
   for (int j = 0; j < kTQ; j++) qk[j] = tau0;
-  float q_lo = key_val(tau0);           // value of qk[kTQ-1]
+  float q_lo = tau0_f;                  // value of qk[kTQ-1]
   unsigned long long dk = tau0;         // largest discarded key
-  float dv = key_val(tau0);
+  float dv = tau0_f;
   unsigned long long best = 0ull;       // argmax path
   float best_f = -INFINITY;
-  float tau_f = key_val(tau0);          // block path
-  // Warp-uniform admission bound: a key that is certainly not above the
-  // slice's k-th best (queues) or its best (argmax).  Values below it are
-  // dropped with one compare.  Shared through s_tau with the other warps.
-  unsigned long long tau_w = tau0;
-  float tau_wf = tau0 == 0ull ? -INFINITY : key_val(tau0);
-  const int jq = (k_sel + kTQ - 1) / kTQ;   // lanes whose queues cover k keys
-  int st_fail = -1;
+  // Admission bound: a value below it cannot make the slice's list (at
+  // least k_sel elements of the slice are at or above it).  Shared by the
+  // warps through s_tauv.
+  float tau_wf = tau0_f;
   const float nanf_ = __int_as_float(0x7FC00000);
 
-  // Puts `key` (> qk[kTQ-1]) into the queue; the key pushed out becomes a
-  // discard.
-  auto q_insert = [&](unsigned long long key) {
+  auto q_insert = [&](unsigned long long key) {  // key > qk[kTQ-1]
     unsigned long long ev = qk[kTQ - 1];
 #pragma unroll
     for (int j = kTQ - 1; j > 0; j--) {
@@ -525,40 +756,6 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     }
     q_lo = key_val(qk[kTQ - 1]);
   };
-  // Offers element (v, li) in this thread's index order (stream): a value
-  // equal to the queue's last one comes later, so it loses the tie.
-  auto offer_stream = [&](float v, int li) {
-    if (use_tq) {
-      if (v > q_lo) {
-        if (!in_hist(li)) q_insert(mkkey(v, static_cast<uint32_t>(li) + goff));
-      } else if (v >= dv) {
-        if (!in_hist(li)) {
-          const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
-          if (key > dk) {
-            dk = key;
-            dv = v;
-          }
-        }
-      }
-    } else if (v >= best_f && !in_hist(li)) {
-      const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
-      if (key > best) {
-        best = key;
-        best_f = v;
-      }
-    }
-  };
-  // Raises the warp bound to the jq-th largest of the lanes' smallest queue
-  // keys: those jq lanes hold jq * kTQ >= k distinct keys at or above it.
-  auto refresh_bound = [&]() {  // argmax path: the warp's best so far
-    const unsigned long long cand_b = warp_max_u64(best);
-    if (cand_b > tau_w) {
-      tau_w = cand_b;
-      tau_wf = key_val(cand_b);
-      if (lane == 0) atomicMax(&s_tau, cand_b);
-    }
-  };
-  // Offers a key out of index order (extra round): full key comparisons.
   auto offer_key = [&](unsigned long long key) {
     if (use_tq) {
       if (key > qk[kTQ - 1]) {
@@ -573,161 +770,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     }
   };
 
-  int st_done = 0;  // stages this thread consumed
-  for (int st = 0; st < nst; st++) {
-    if (*reinterpret_cast<volatile int *>(&s_timeout)) {
-      st_fail = st;
-      break;
-    }
-    const int buf = st % NS;
-    const bool ok = mbar_wait(&s_bar[buf], static_cast<uint32_t>((st / NS) & 1), kWaitBudget);
-    if (!ok) {
-      s_timeout = 1;
-      st_fail = st;
-      break;
-    }
-    st_done = st + 1;
-    const unsigned char *sb = ring + buf * kStageBytes;
-    const int v0 = st * (kStageBytes / 16);
-    const int nv = min(kStageBytes / 16, nvec - v0);
-    // fast pass: tempered values and their max; NaN marks an empty lane
-    float vv[EPT];
-    float vmax = -INFINITY;
-#pragma unroll
-    for (int u = 0; u < VPT; u++) {
-      const int j = u * NT + tid;
-      float xv[VEC];
-      if (j < nv) {
-        Vec16S<T>::load(sb, j, xv);
-      } else {
-#pragma unroll
-        for (int w = 0; w < VEC; w++) xv[w] = nanf_;
-      }
-#pragma unroll
-      for (int w = 0; w < VEC; w++) vv[u * VEC + w] = xv[w];
-    }
-    if (!greedy) {
-      if (P.divide) {
-#pragma unroll
-        for (int e = 0; e < EPT; e++) vv[e] = __fdiv_rn(vv[e], P.T);
-      } else {
-#pragma unroll
-        for (int e = 0; e < EPT; e++) vv[e] = __fmul_rn(vv[e], P.inv_T);
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < EPT; e++) vmax = fmaxf(vmax, vv[e]);
-    // This warp is done with the stage (vmax depends on every value it read,
-    // so the shared loads have completed): release the slot.  The last warp
-    // to release it refills it with stage st + NS; no one waits, and no
-    // fence is needed (a fence in a thread with bulk copies in flight would
-    // wait for them).
-    __syncwarp();
-    if (lane == 0 && atomicAdd(&s_rel[buf], vmax == vmax ? 1 : 1) == NW - 1) {
-      s_rel[buf] = 0;
-      if (st + NS < nst && !*reinterpret_cast<volatile int *>(&s_timeout)) {
-        issue(st + NS);
-        atomicMax(&s_issued, st + NS + 1);
-      }
-    }
-    if (use_block) {
-      // only a value >= the admission threshold can still enter the list
-      if (__syncthreads_or(vmax >= tau_f)) {
-        unsigned long long keys[EPT];
-        uint32_t valid = 0;
-#pragma unroll
-        for (int e = 0; e < EPT; e++) {
-          keys[e] = 0ull;
-          if (vv[e] >= tau_f) {
-            const int li = a_al + (v0 + (e / VEC) * NT + tid) * VEC + (e % VEC);
-            if (in_hist(li)) continue;
-            keys[e] = mkkey(vv[e], static_cast<uint32_t>(li) + goff);
-            valid |= 1u << e;
-          }
-        }
-        offer_round<NT, MAXPER, EPT>(cbuf, cap, hwm, k_sel, sh, keys, valid);
-        tau_f = key_val(sh.tau);
-      }
-    } else {
-      if (use_tq) {
-        // Per-thread exact queue: only values above this thread's own
-        // threshold (its 4th best, or its largest discard) need work.  The
-        // pending elements are handled one per iteration, so the warp loops
-        // over the largest per-lane count, not over every slot.
-        // values below the block bound cannot make the list
-        const float thr = fmaxf(fminf(q_lo, dv), tau_wf);
-        const unsigned long long top0 = qk[0];
-        uint32_t pend = 0;
-#pragma unroll
-        for (int e = 0; e < EPT; e++) pend |= (vv[e] >= thr) ? (1u << e) : 0u;
-        while (__any_sync(0xFFFFFFFFu, pend != 0)) {
-          if (pend) {
-            const int e = __ffs(pend) - 1;
-            pend &= pend - 1;
-            float v = vv[0];
-#pragma unroll
-            for (int j = 1; j < EPT; j++) v = (e == j) ? vv[j] : v;
-            const int li = a_al + (v0 + (e / VEC) * NT + tid) * VEC + (e % VEC);
-            if (!in_hist(li)) {
-              const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
-              if (key > tau_w) {
-                if (key > qk[kTQ - 1]) {
-                  q_insert(key);
-                } else if (key > dk) {
-                  dk = key;
-                  dv = v;
-                }
-              }
-            }
-          }
-        }
-        if (qk[0] != top0) s_max[tid] = qk[0];
-        if (warp == 0 && ((st + 2) & (st + 1)) == 0) {
-          // After stages 0, 1, 3, 7, ...: the k-th largest of the threads'
-          // best keys is a lower bound on the slice's k-th best (k distinct
-          // elements are at or above it); maxima only grow, so stale
-          // entries keep it valid.
-          unsigned long long mv[NW];
-#pragma unroll
-          for (int r = 0; r < NW; r++) mv[r] = *reinterpret_cast<volatile unsigned long long *>(&s_max[r * 32 + lane]);
-          const unsigned long long bnd = warp_jth_reg<NW>(mv, k_sel);
-          if (lane == 0 && bnd > tau0) atomicMax(&s_tau, bnd);
-        }
-      } else if (__any_sync(0xFFFFFFFFu, vmax >= tau_wf)) {
-        // argmax: one warp-uniform test per stage against the best so far
-        bool changed = false;
-        if (vmax >= tau_wf) {
-#pragma unroll
-          for (int e = 0; e < EPT; e++) {
-            if (!(vv[e] >= tau_wf)) continue;
-            const int li = a_al + (v0 + (e / VEC) * NT + tid) * VEC + (e % VEC);
-            if (in_hist(li)) continue;
-            const unsigned long long key = mkkey(vv[e], static_cast<uint32_t>(li) + goff);
-            if (key > best) {
-              best = key;
-              changed = true;
-            }
-          }
-        }
-        if (__any_sync(0xFFFFFFFFu, changed)) refresh_bound();
-      }
-      const unsigned long long sb_tau = *reinterpret_cast<volatile unsigned long long *>(&s_tau);
-      if (sb_tau > tau_w) {
-        tau_w = sb_tau;
-        tau_wf = key_val(sb_tau);
-      }
-    }
-  }
-  __syncthreads();
-  if (tid == 0 && s_timeout) {
-    // a wait ran out: wait (bounded) for the copies still in flight
-    for (int s2 = st_done; s2 < s_issued; s2++)
-      mbar_wait(&s_bar[s2 % NS], static_cast<uint32_t>((s2 / NS) & 1), kDrainBudget);
-  }
-  if (s_timeout && st_fail < 0) st_fail = nst;
-  const bool timed_out = st_fail >= 0;
-
-  // ---- head, tail and the penalised history ids as extra rounds -----------
+  // ---- head, tail and the penalised history ids: exact keys, first --------
   if (a == 0 && goff == 0 && tid == 0) {
     float x = load_scalar<T>(rowp, 0);
     const int c = hist_on ? hash_count(hk, hn, hmask, hshift, 0u) : 0;
@@ -738,31 +781,46 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   const int n_extra = head + tail + (hist_on ? A.hts : 0);
   for (int base = 0; base < n_extra; base += NT * XPT) {
     float xv[XPT];
-    int lis[XPT];
+    int lis[XPT], cnts[XPT];
     uint32_t have = 0;
+    // the items' columns first (column a stands in for an empty item), then
+    // every load at once, then the values
 #pragma unroll
     for (int e = 0; e < XPT; e++) {
-      xv[e] = nanf_;
-      lis[e] = 0;
       const int it = base + e * NT + tid;
-      if (it >= n_extra) continue;
-      int li, cnt = 0;
+      int li = a, cnt = 0;
+      bool h = false;
       if (it < head) {
         li = a + it;
+        h = true;
       } else if (it < head + tail) {
         li = b_al + (it - head);
-      } else {
+        h = true;
+      } else if (it < n_extra) {
         const int i = it - head - tail;
-        if (hk[i] == kHashEmpty) continue;
-        li = static_cast<int>(hk[i]);
-        cnt = static_cast<int>(hn[i]);
+        const uint32_t t = hk[i];
+        if (t != kHashEmpty) {
+          li = static_cast<int>(t);
+          cnt = static_cast<int>(hn[i]);
+          h = true;
+        }
       }
-      if (cnt == 0 && in_hist(li)) continue;
-      float x = load_scalar<T>(rowp, li);
-      if (cnt > 0) x = penalize(x, cnt, P);
-      xv[e] = greedy ? x : temper(x, P);
       lis[e] = li;
-      have |= 1u << e;
+      cnts[e] = cnt;
+      have |= h ? (1u << e) : 0u;
+    }
+#pragma unroll
+    for (int e = 0; e < XPT; e++) xv[e] = load_scalar<T>(rowp, lis[e]);
+#pragma unroll
+    for (int e = 0; e < XPT; e++) {
+      if (!((have >> e) & 1u)) continue;
+      if (cnts[e] == 0 && in_hist(lis[e])) {
+        have &= ~(1u << e);
+        continue;
+      }
+      float x = xv[e];
+      if (cnts[e] > 0) x = penalize(x, cnts[e], P);
+      xv[e] = greedy ? x : temper(x, P);
     }
     if (use_block) {
       unsigned long long keys[XPT];
@@ -783,10 +841,267 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
           offer_key(mkkey(xv[e], static_cast<uint32_t>(lis[e]) + goff));
     }
   }
+  if (use_tq && qk[0] > tau0) s_maxv[tid] = f2ord(key_val(qk[0]));
+  if (!use_tq && !use_block) {
+    const uint32_t bo = __reduce_max_sync(0xFFFFFFFFu, best != 0ull ? f2ord(best_f) : kOrdNegInf);
+    if (lane == 0) atomicMax(&s_tauv, bo);
+  }
 
-  // ---- this slice's list -> scratch (one warp) ---------------------------
-  unsigned long long *ring_keys = reinterpret_cast<unsigned long long *>(ring);
+  // ---- the stream ----------------------------------------------------------
+  // Temperature of the stream: a multiplication by `scale` (1 for greedy
+  // rows), which is monotone, so the tempered chunk maximum is the maximum
+  // of the tempered values; with PZ_CFG_TEMP_DIVIDE a division, tested
+  // through a raw threshold instead.
+  const bool mulT = greedy || !P.divide;
+  const float scale = greedy ? 1.0f : P.inv_T;
+  if (use_tq) {
+    // Per lane: thr, the tempered value below which nothing can change this
+    // thread's state (below the block bound, or below a key it already
+    // discarded); rthr (division only), a raw value below which every value
+    // tempers below thr.
+    uint32_t seen_tau = *reinterpret_cast<volatile uint32_t *>(&s_tauv);
+    tau_wf = fmaxf(tau_wf, ord2f(seen_tau));
+    float thr = fmaxf(fminf(q_lo, dv), tau_wf);
+    float rthr = mulT ? 0.0f : raw_floor(thr, P);
+    auto retune = [&]() {
+      const float t = fmaxf(fminf(q_lo, dv), tau_wf);
+      if (t != thr) {
+        thr = t;
+        if (!mulT) rthr = raw_floor(t, P);
+      }
+    };
+    // warp w refreshes the block bound once, after its chunk refresh_at
+    const int refresh_at = warp < 4 ? 2 + warp : 2 * warp;
+    int slot = 0;
+    for (int i = 0; i < nw; i++) {
+      cp_async_wait<NS - 1>();
+      const unsigned char *sb = wring + slot * kChunkBytes;
+      const unsigned char *lsb = ldst + slot * kChunkBytes;
+      uint4 q[kLaneVecs];
+      float mv[kLaneVecs];
+#pragma unroll
+      for (int u = 0; u < kLaneVecs; u++) {
+        q[u] = *reinterpret_cast<const uint4 *>(lsb + u * 512);
+        mv[u] = LaneVec<T>::vmax(q[u]);
+      }
+      const float m = fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3]));
+      const int e0 = a_al + (warp + NW * i) * (kChunkBytes / static_cast<int>(sizeof(T)));
+      if (i == 0) {
+        // A first bound from the first chunk of every warp: each of the np
+        // warps that have chunks offers the jq-th largest of its 128 vector
+        // maxima (distinct elements; a maximum that is a history id does
+        // not count, its penalised value is not known here), and the
+        // smallest offer has np * jq >= k elements at or above it.
+        uint32_t vm[kLaneVecs];
+#pragma unroll
+        for (int u = 0; u < kLaneVecs; u++) {
+          vm[u] = kOrdNegInf;
+          if (mv[u] == mv[u]) {
+            bool ok = true;
+            if (hist_on) {
+              int w0 = VEC - 1;
+#pragma unroll
+              for (int w = VEC - 2; w >= 0; w--)
+                if (LaneVec<T>::elem(q[u], w) == mv[u]) w0 = w;
+              ok = !in_hist(e0 + (u * 32 + lane) * VEC + w0);
+            }
+            if (ok) vm[u] = f2ord(temper(mv[u], P));
+          }
+        }
+        const int np = min(NW, nchunks);
+        const uint32_t bj = kth_of_4(vm[0], vm[1], vm[2], vm[3], (k_sel + np - 1) / np, 12);
+        if (lane == 0) atomicMin(&s_b0, bj);
+        named_bar_sync(1, np * 32);  // the warps with chunks (warps 0 .. np-1)
+        const uint32_t b0 = *reinterpret_cast<volatile uint32_t *>(&s_b0);
+        tau_wf = fmaxf(tau_wf, ord2f(b0));
+        if (warp == 0 && lane == 0) atomicMax(&s_tauv, b0);
+        retune();
+      }
+      const bool hot = mulT ? !(__fmul_rn(m, scale) < thr) : !(m < rthr);
+      if (__any_sync(0xFFFFFFFFu, hot)) {
+        uint32_t pend = 0;
+        if (hot) {
+          if (mulT) {
+#pragma unroll
+            for (int u = 0; u < kLaneVecs; u++) {
+              if (__fmul_rn(mv[u], scale) < thr) continue;
+#pragma unroll
+              for (int w = 0; w < VEC; w++)
+                if (__fmul_rn(LaneVec<T>::elem(q[u], w), scale) >= thr) pend |= 1u << (u * VEC + w);
+            }
+          } else {
+#pragma unroll
+            for (int u = 0; u < kLaneVecs; u++) {
+              if (mv[u] < rthr) continue;
+#pragma unroll
+              for (int w = 0; w < VEC; w++)
+                if (LaneVec<T>::elem(q[u], w) >= rthr) pend |= 1u << (u * VEC + w);
+            }
+          }
+        }
+        const unsigned long long top0 = qk[0];
+        while (pend) {
+          const int e = __ffs(pend) - 1;
+          pend &= pend - 1;
+          const int pos = ((e / VEC) * 32 + lane) * VEC + (e % VEC);  // element within the chunk
+          const int li = e0 + pos;
+          if (in_hist(li)) continue;
+          const float v = temper(LaneVec<T>::smem(sb, pos), P);
+          const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
+          if (key > qk[kTQ - 1]) {
+            q_insert(key);
+          } else if (key > dk) {
+            dk = key;
+            dv = v;
+          }
+        }
+        if (qk[0] != top0) s_maxv[tid] = f2ord(key_val(qk[0]));
+        retune();
+      }
+      if (i == refresh_at) {
+        // the k-th largest of the threads' best values: k distinct elements
+        // are at or above it; maxima only grow, so stale entries keep it valid
+        const uint32_t bnd = kth_of_maxima(s_maxv, k_sel, 12);
+        if (lane == 0) atomicMax(&s_tauv, bnd);
+      }
+      // this lane has read its vectors of the slot (every value fed the
+      // maximum): refill them
+      if (i + NS < nw) issue(i + NS, slot);
+      cp_async_commit();
+      const uint32_t tb = *reinterpret_cast<volatile uint32_t *>(&s_tauv);
+      if (tb != seen_tau) {
+        seen_tau = tb;
+        tau_wf = fmaxf(tau_wf, ord2f(tb));
+        retune();
+      }
+      slot = slot + 1 == NS ? 0 : slot + 1;
+    }
+  } else if (!use_block) {
+    // argmax: the threshold is the block's best value so far (warp-uniform);
+    // only a lane's maximum and its ties can beat it
+    uint32_t seen_tau = *reinterpret_cast<volatile uint32_t *>(&s_tauv);
+    tau_wf = fmaxf(tau_wf, ord2f(seen_tau));
+    float rthr = mulT ? 0.0f : raw_floor(tau_wf, P);
+    int slot = 0;
+    for (int i = 0; i < nw; i++) {
+      cp_async_wait<NS - 1>();
+      const unsigned char *sb = wring + slot * kChunkBytes;
+      const unsigned char *lsb = ldst + slot * kChunkBytes;
+      uint4 q[kLaneVecs];
+      float mv[kLaneVecs];
+#pragma unroll
+      for (int u = 0; u < kLaneVecs; u++) {
+        q[u] = *reinterpret_cast<const uint4 *>(lsb + u * 512);
+        mv[u] = LaneVec<T>::vmax(q[u]);
+      }
+      const float m = fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3]));
+      const bool hot = mulT ? !(__fmul_rn(m, scale) < tau_wf) : !(m < rthr);
+      if (__any_sync(0xFFFFFFFFu, hot)) {
+        const int e0 = a_al + (warp + NW * i) * (kChunkBytes / static_cast<int>(sizeof(T)));
+        uint32_t pend = 0;
+        if (hot) {
+          // the lane's maximum and its ties; every element at or above the
+          // threshold when the maximum may be a (penalised) history id
+          const float te = hist_on ? (mulT ? tau_wf : rthr) : (mulT ? fmaxf(tau_wf, __fmul_rn(m, scale)) : fmaxf(rthr, m));
+#pragma unroll
+          for (int u = 0; u < kLaneVecs; u++) {
+            if ((mulT ? __fmul_rn(mv[u], scale) : mv[u]) < te) continue;
+#pragma unroll
+            for (int w = 0; w < VEC; w++) {
+              const float x = LaneVec<T>::elem(q[u], w);
+              if ((mulT ? __fmul_rn(x, scale) : x) >= te) pend |= 1u << (u * VEC + w);
+            }
+          }
+        }
+        while (pend) {
+          const int e = __ffs(pend) - 1;
+          pend &= pend - 1;
+          const int pos = ((e / VEC) * 32 + lane) * VEC + (e % VEC);
+          const int li = e0 + pos;
+          if (in_hist(li)) continue;
+          const float x = LaneVec<T>::smem(sb, pos);
+          const float v = greedy ? x : temper(x, P);
+          const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
+          if (key > best) {
+            best = key;
+            best_f = v;
+          }
+        }
+        const uint32_t bo = __reduce_max_sync(0xFFFFFFFFu, best != 0ull ? f2ord(best_f) : kOrdNegInf);
+        if (lane == 0 && bo > *reinterpret_cast<volatile uint32_t *>(&s_tauv)) atomicMax(&s_tauv, bo);
+      }
+      if (i + NS < nw) issue(i + NS, slot);
+      cp_async_commit();
+      const uint32_t tb = *reinterpret_cast<volatile uint32_t *>(&s_tauv);
+      if (tb != seen_tau) {
+        seen_tau = tb;
+        const float tf = ord2f(tb);
+        if (tf > tau_wf) {
+          tau_wf = tf;
+          if (!mulT) rthr = raw_floor(tf, P);
+        }
+      }
+      slot = slot + 1 == NS ? 0 : slot + 1;
+    }
+  } else {
+    // long lists: one block-wide buffer, all warps in step (round r: chunk
+    // warp + NW*r of every warp)
+    float tau_f = tau0_f;
+    const int R = (nchunks + NW - 1) / NW;
+    for (int r = 0; r < R; r++) {
+      const bool mine = r < nw;
+      cp_async_wait<NS - 1>();
+      const unsigned char *sb = wring + (r % NS) * kChunkBytes;
+      const int c = warp + NW * r;
+      const int cv = mine ? kChunkBytes / 16 : 0;  // a short last chunk is NaN-filled
+      const int e0 = a_al + c * (kChunkBytes / static_cast<int>(sizeof(T)));
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        float xv[HPT];
+#pragma unroll
+        for (int uu = 0; uu < 2; uu++) {
+          const int j = (2 * h + uu) * 32 + lane;
+          if (j < cv) {
+            Vec16S<T>::load(sb, j, xv + uu * VEC);
+          } else {
+#pragma unroll
+            for (int w = 0; w < VEC; w++) xv[uu * VEC + w] = nanf_;
+          }
+        }
+        float vmax = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < HPT; e++) {
+          xv[e] = temper(xv[e], P);
+          vmax = fmaxf(vmax, xv[e]);
+        }
+        if (__syncthreads_or(vmax >= tau_f)) {
+          unsigned long long keys[HPT];
+          uint32_t valid = 0;
+#pragma unroll
+          for (int e = 0; e < HPT; e++) {
+            keys[e] = 0ull;
+            if (xv[e] >= tau_f) {
+              const int li = e0 + ((2 * h + e / VEC) * 32 + lane) * VEC + (e % VEC);
+              if (in_hist(li)) continue;
+              keys[e] = mkkey(xv[e], static_cast<uint32_t>(li) + goff);
+              valid |= 1u << e;
+            }
+          }
+          offer_round<NT, MAXPER, HPT>(cbuf, cap, hwm, k_sel, sh, keys, valid);
+          tau_f = key_val(sh.tau);
+        }
+      }
+      if (r + NS < nw) issue(r + NS, r % NS);
+      cp_async_commit();
+    }
+  }
+  cp_async_wait<0>();
   __syncthreads();
+  const bool timed_out = s_timeout != 0;
+
+  // ---- this slice's list -> scratch ---------------------------------------
+  unsigned long long *lst = reinterpret_cast<unsigned long long *>(ring);  // survivors
+  unsigned long long *rb = use_block ? cbuf : lst;                         // block buffer
   if (use_block) {
     int n = sh.n < cap ? sh.n : cap;
     __syncthreads();
@@ -794,11 +1109,9 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       block_select<NT, MAXPER>(cbuf, n, k_sel, sh);
       n = k_sel;
     }
-    if (tid == 0) s_wn[0] = n;
+    if (tid == 0) s_n = n;
   } else if (use_tq) {
-    s_max[tid] = qk[0];
-#pragma unroll
-    for (int j = 0; j < kTQ; j++) cbuf[tid * kTQ + j] = qk[j];
+    s_maxv[tid] = qk[0] > tau0 ? f2ord(key_val(qk[0])) : kOrdNegInf;
     const unsigned long long d = warp_max_u64(dk);
     if (lane == 0) atomicMax(&s_dk, d);
   } else {
@@ -808,40 +1121,40 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   __syncthreads();
   bool exact_rescan = false;
   if (use_tq) {
-    if (warp == 0) {
-      // A lower bound on the slice's k-th best key: the k-th largest of
-      // the threads' best keys.  Queue keys at or above it -> ring_keys,
-      // then the best k_sel of those.
-      unsigned long long v8[NW];
+    // keys whose value is at or above the k-th largest thread maximum (at
+    // least k_sel of them), then the best k_sel of those
+    uint32_t v8[NW];
 #pragma unroll
-      for (int r = 0; r < NW; r++) v8[r] = s_max[r * 32 + lane];
-      const unsigned long long bnd = warp_jth_reg<NW>(v8, k_sel);
-      const unsigned long long lo = bnd > tau0 ? bnd - 1ull : tau0;
-      int n = 0;
-      for (int base = 0; base < NT * kTQ; base += 32) {
-        const unsigned long long key = cbuf[base + lane];
-        const bool r = key > lo;
-        const uint32_t bal = __ballot_sync(0xFFFFFFFFu, r);
-        if (r) ring_keys[n + __popc(bal & lanemask_lt())] = key;
-        n += __popc(bal);
-      }
-      __syncwarp();
+    for (int r = 0; r < NW; r++) v8[r] = s_maxv[r * 32 + lane];
+    const uint32_t bnd = warp_kth_u32<NW>(v8, k_sel, 32);
+#pragma unroll
+    for (int j = 0; j < kTQ; j++) {
+      const bool keep = qk[j] > tau0 && f2ord(key_val(qk[j])) >= bnd;
+      const uint32_t bal = __ballot_sync(0xFFFFFFFFu, keep);
+      int base = 0;
+      if (lane == 0 && bal) base = atomicAdd(&s_cnt, __popc(bal));
+      base = __shfl_sync(0xFFFFFFFFu, base, 0);
+      if (keep) lst[base + __popc(bal & lanemask_lt())] = qk[j];
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int n = s_cnt;
       unsigned long long kth = tau0;  // fewer than k real keys: any real discard counts
       if (n >= k_sel) {
-        kth = warp_kth(ring_keys, n, k_sel);
-        n = warp_compact_ge(ring_keys, n, kth);
+        kth = warp_kth(lst, n, k_sel);
+        n = warp_compact_ge(lst, n, kth);
       }
       // exact unless some thread pushed out a key that beats the k-th
       if (lane == 0) {
-        s_wn[0] = n;
-        s_tok = s_dk > kth ? 1 : 0;
+        s_n = n;
+        s_rescan = s_dk > kth ? 1 : 0;
       }
     }
     __syncthreads();
-    exact_rescan = s_tok != 0;
+    exact_rescan = s_rescan != 0;
   }
   if (exact_rescan) {
-    // rare: redo the slice exactly with the block-wide buffer (all threads)
+    // rare: redo the slice exactly with a block-wide buffer (all threads)
     if (tid == 0) {
       sh.n = 0;
       sh.tau = tau0;
@@ -865,16 +1178,16 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
           }
         }
       }
-      offer_round<NT, MAXPER, XPT>(cbuf, cap, hwm, k_sel, sh, keys, valid);
+      offer_round<NT, MAXPER, XPT>(rb, cap, hwm, k_sel, sh, keys, valid);
     }
     __syncthreads();
     int n = sh.n < cap ? sh.n : cap;
     __syncthreads();
     if (n > k_sel) {
-      block_select<NT, MAXPER>(cbuf, n, k_sel, sh);
+      block_select<NT, MAXPER>(rb, n, k_sel, sh);
       n = k_sel;
     }
-    if (tid == 0) s_wn[0] = n;
+    if (tid == 0) s_n = n;
     __syncthreads();
   }
   if (warp != 0) return;
@@ -883,11 +1196,11 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   unsigned long long *dst =
       A.slice_keys + (static_cast<size_t>(row) * A.S + sl) * static_cast<size_t>(A.kcap);
   if (use_block || exact_rescan) {
-    m = s_wn[0];
-    for (int i = lane; i < m; i += 32) dst[i] = cbuf[i];
+    m = s_n;
+    for (int i = lane; i < m; i += 32) dst[i] = rb[i];
   } else if (use_tq) {
-    m = s_wn[0];
-    for (int i = lane; i < m; i += 32) dst[i] = ring_keys[i];
+    m = s_n;
+    for (int i = lane; i < m; i += 32) dst[i] = lst[i];
   } else {
     unsigned long long bl = lane < NW ? s_red[lane] : 0ull;
     bl = warp_max_u64(bl);
@@ -959,8 +1272,14 @@ __global__ void __launch_bounds__(128) finalize_kernel(const SliceArgs A, int wa
       n = warp_compact_ge(lst, n, kth);
     }
     n_sel = n;
-    for (int i = n_sel + lane; i < A.kcap; i += 32) lst[i] = 0ull;
-    warp_sort_desc(lst, A.kcap);
+    if (A.kcap <= 64) {
+      warp_rank_sort_desc(lst, n_sel);
+      for (int i = n_sel + lane; i < A.kcap; i += 32) lst[i] = 0ull;
+      __syncwarp();
+    } else {
+      for (int i = n_sel + lane; i < A.kcap; i += 32) lst[i] = 0ull;
+      warp_sort_desc(lst, A.kcap);
+    }
   } else {
     unsigned long long bl = 0ull;
     for (int s2 = lane; s2 < S; s2 += 32) {
@@ -983,84 +1302,7 @@ __global__ void __launch_bounds__(128) finalize_kernel(const SliceArgs A, int wa
     }
   }
   const bool x0nan = (__ldcg(A.row_flags + row) & 1u) != 0u;
-
-  if (A.mode_emit) {
-    // vocab sharding: publish the local list; the draw happens after the
-    // allgather (merge_kernel).
-    unsigned long long *ek = A.emit_keys + static_cast<size_t>(row) * (A.kcap + 1);
-    int cnt;
-    if (P.mode == kModeTopK && !bad_k) {
-      cnt = n_sel;
-      for (int i = lane; i < cnt; i += 32) ek[i] = lst[i];
-    } else {
-      cnt = gbest > tau0 ? 1 : 0;
-      if (lane == 0 && cnt) ek[0] = gbest;
-    }
-    if (lane == 0)
-      ek[A.kcap] = static_cast<unsigned long long>(cnt | (x0nan ? (1 << 30) : 0) |
-                                                   (too_long ? (1 << 29) : 0) |
-                                                   (bad_k ? (1 << 28) : 0) |
-                                                   (row_timed_out ? (1 << 27) : 0));
-    return;
-  }
-
-  unsigned long long rs = A.rng[row];
-  int tok = -1;
-  int status = too_long ? PZ_ROW_HISTORY_TOO_LONG : PZ_ROW_OK;
-  bool pending = false;
-  const bool want_cand = A.cand_ids != nullptr || A.cand_probs != nullptr;
-  if (row_timed_out) {
-    tok = -1;
-    status = PZ_ROW_TIMEOUT;
-  } else if (too_long) {
-    tok = -1;                                             // penalties could not be applied
-  } else if (bad_k) {
-    tok = -1;
-    status = PZ_ROW_HINT_VIOLATED;
-  } else if (P.mode == kModeGreedy) {
-    tok = x0nan ? 0 : (gbest ? key_idx(gbest) : 0);       // argmax.c:3-13
-  } else if (P.mode == kModeTopK) {
-    int32_t *cids = A.cand_ids ? A.cand_ids + static_cast<size_t>(row) * A.cand_stride : nullptr;
-    float *cprobs = A.cand_probs ? A.cand_probs + static_cast<size_t>(row) * A.cand_stride : nullptr;
-    int t = INT_MIN;
-    if (P.keff <= 64) {
-      // warp-parallel, rounding exactly like the reference's loops
-      t = warp_sample_list<2>(lst, n_sel, P, rs, want_cand ? cprobs : nullptr);
-      if (t != INT_MIN && want_cand && cids != nullptr)
-        for (int i = lane; i < P.keff; i += 32) cids[i] = i < n_sel ? key_idx(lst[i]) : -1;
-    }
-    if (t == INT_MIN)
-      t = sample_list<32>(lst, n_sel, P, rs, fe, fp, ford, &s_tok,
-                          want_cand ? cids : nullptr, want_cand ? cprobs : nullptr);
-    tok = t;
-  } else if (P.mode == kModeTopPFull && A.V_global > PZ_TOP_P_MAX_VOCAB) {
-    tok = x0nan ? 0 : key_idx(gbest);                     // top_p.c:33-34
-  } else if (P.mode == kModeTopPFull && x0nan) {
-    tok = 0;                                              // NaN max: n == 0 -> argmax
-  } else if (A.no_full_vocab) {
-    tok = -1;
-    status = PZ_ROW_HINT_VIOLATED;
-  } else {
-    pending = true;
-    if (lane == 0) {
-      A.row_best[row] = gbest;
-      A.full_rows[atomicAdd(A.n_full, 1)] = row;
-    }
-  }
-  if (lane == 0) {
-    if (!pending) {
-      A.out[row] = tok;
-      A.rng[row] = rs;
-    }
-    if (A.n_cand) A.n_cand[row] = (P.mode == kModeTopK && !bad_k && !too_long && !row_timed_out) ? P.keff : 0;
-    if (A.row_status) A.row_status[row] = status;
-  }
-  if (want_cand && (P.mode != kModeTopK || bad_k || too_long || row_timed_out)) {
-    for (int i = lane; i < A.cand_stride; i += 32) {
-      if (A.cand_ids) A.cand_ids[static_cast<size_t>(row) * A.cand_stride + i] = -1;
-      if (A.cand_probs) A.cand_probs[static_cast<size_t>(row) * A.cand_stride + i] = 0.0f;
-    }
-  }
+  finalize_row(A, row, P, bad_k, too_long, row_timed_out, x0nan, lst, n_sel, gbest, fe, fp, ford, s_tokp);
 }
 
 // ---------------------------------------------------------------------------

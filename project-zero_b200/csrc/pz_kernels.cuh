@@ -39,7 +39,7 @@ struct SliceArgs {
   int hcap;             // longest history a row may have (0: no history)
   int hts;              // history hash slots per CTA (power of two >= 2*hcap, or 0)
   int hshift;           // 32 - log2(hts)
-  int nstages;          // bulk-copy ring depth
+  int nstages;          // bulk-copy ring slots per warp
   int mode_emit;        // 1: write the merged local list (vocab sharding), no draw
   int no_full_vocab;
   // scratch

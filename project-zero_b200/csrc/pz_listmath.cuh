@@ -207,3 +207,149 @@ __device__ int warp_sample_list(const unsigned long long *lk, int n_sel, const R
 }
 
 }  // namespace pz
+
+namespace pz {
+
+// Sorts lk[0..n) (distinct keys, n <= 64) descending in place, one warp:
+// each key's position is the number of keys above it.
+__device__ __forceinline__ void warp_rank_sort_desc(unsigned long long *lk, int n) {
+  const int lane = static_cast<int>(lane_id());
+  const unsigned long long k0 = lane < n ? lk[lane] : 0ull;
+  const unsigned long long k1 = lane + 32 < n ? lk[lane + 32] : 0ull;
+  int r0 = 0, r1 = 0;
+  for (int j = 0; j < n; j++) {
+    const unsigned long long o = lk[j];
+    r0 += o > k0 ? 1 : 0;
+    r1 += o > k1 ? 1 : 0;
+  }
+  __syncwarp();
+  if (lane < n) lk[r0] = k0;
+  if (lane + 32 < n) lk[r1] = k1;
+  __syncwarp();
+}
+
+// The reference's list sampling over a sorted list of keff <= 64 entries
+// (lk[0..n_sel) keys, the rest the reference's empty slots (-1e30, -1)),
+// one warp: element-wise steps in parallel, each sequential float sum on
+// lane 0 in the reference's order, searches by ballot.  p_on: reference
+// src/sampling/top_p.c:37-105 on the list; else: src/sampling/top_k.c:50-72.
+// `rs` advances by one draw unless the nucleus is empty.  e, c: shared
+// scratch of 64 floats each.  Writes the list's probabilities to
+// pr_out[0..keff) when pr_out is not null.  Returns INT_MIN if the
+// probabilities are not in list order (the caller then uses the general
+// path with its stable sort).
+__device__ __noinline__ int warp_sample_small(const unsigned long long *lk, int n_sel, const RowPlan P,
+                                              unsigned long long &rs, float *e, float *c,
+                                              float *pr_out) {
+  const int lane = static_cast<int>(lane_id());
+  const int keff = P.keff;
+  const int i0 = lane, i1 = lane + 32;
+  const float v0 = i0 < n_sel ? key_val(lk[i0]) : -1e30f;
+  const float v1 = i1 < n_sel ? key_val(lk[i1]) : -1e30f;
+  const float mx = __shfl_sync(0xFFFFFFFFu, v0, 0);
+  auto idv = [&](int i) -> int { return i < n_sel ? key_idx(lk[i]) : -1; };
+  // lane 0's sequential sum of x[0..n) (unrolled so the loads run ahead)
+  auto seq_sum = [&](const float *x, int n) -> float {
+    float s = 0.0f;
+    if (lane == 0) {
+      int j = 0;
+      for (; j + 4 <= n; j += 4) {
+        const float a = x[j], b = x[j + 1], d = x[j + 2], f = x[j + 3];
+        s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, a), b), d), f);
+      }
+      for (; j < n; j++) s = __fadd_rn(s, x[j]);
+    }
+    return __shfl_sync(0xFFFFFFFFu, s, 0);
+  };
+  // lane 0's running sums of x[0..n) into out[]; returns the first j with
+  // out[j] >= stop (or n)
+  auto seq_cum = [&](const float *x, int n, float *out, float stop) -> int {
+    int hit = n;
+    if (lane == 0) {
+      float s = 0.0f;
+      for (int j = 0; j < n; j++) {
+        s = __fadd_rn(s, x[j]);
+        out[j] = s;
+        if (s >= stop) {
+          hit = j;
+          break;
+        }
+      }
+    }
+    __syncwarp();
+    return __shfl_sync(0xFFFFFFFFu, hit, 0);
+  };
+  // first j < n with r < cdf[j], or -1
+  auto first_below = [&](const float *cdf, int n, float r) -> int {
+    for (int base = 0; base < n; base += 32) {
+      const int j = base + lane;
+      const uint32_t b = __ballot_sync(0xFFFFFFFFu, j < n && r < cdf[j]);
+      if (b) return base + __ffs(b) - 1;
+    }
+    return -1;
+  };
+  int tok;
+  if (P.p_on) {
+    const float thr = __fsub_rn(mx, 20.0f);                             // top_p.c:53
+    const bool c0 = i0 < keff && v0 >= thr, c1 = i1 < keff && v1 >= thr;
+    if (c0) e[i0] = cr_expf(__fsub_rn(v0, mx));                         // :58-59
+    if (c1) e[i1] = cr_expf(__fsub_rn(v1, mx));
+    // the list is sorted, so the kept entries are a prefix
+    const uint32_t k0 = __ballot_sync(0xFFFFFFFFu, c0), k1 = __ballot_sync(0xFFFFFFFFu, c1);
+    const int n = (~k0 != 0u) ? __ffs(~k0) - 1 : 32 + ((~k1 != 0u) ? __ffs(~k1) - 1 : 32);
+    const int nk = n < keff ? n : keff;
+    if (nk == 0) {                                                      // :68-69
+      if (pr_out)
+        for (int i = lane; i < keff; i += 32) pr_out[i] = 0.0f;
+      return idv(0);
+    }
+    __syncwarp();
+    const float sum = seq_sum(e, nk);                                   // :62
+    const float inv = __fdiv_rn(1.0f, sum);                             // :72
+    const float p0 = i0 < nk ? __fmul_rn(e[i0], inv) : 0.0f;            // :73-74
+    const float p1 = i1 < nk ? __fmul_rn(e[i1], inv) : 0.0f;
+    // stable sort by probability (:77) is the identity when they descend
+    const float nx0 = __shfl_down_sync(0xFFFFFFFFu, p0, 1);
+    const float nx1 = __shfl_down_sync(0xFFFFFFFFu, p1, 1);
+    const float p1first = __shfl_sync(0xFFFFFFFFu, p1, 0);
+    const bool up0 = i0 + 1 < nk && (lane < 31 ? nx0 : p1first) > p0;
+    const bool up1 = i1 + 1 < nk && lane < 31 && nx1 > p1;
+    if (__any_sync(0xFFFFFFFFu, up0 || up1)) return INT_MIN;
+    __syncwarp();
+    if (i0 < nk) e[i0] = p0;  // e now holds the probabilities
+    if (i1 < nk) e[i1] = p1;
+    __syncwarp();
+    const int hit = seq_cum(e, nk, c, P.p);                             // :80-88
+    const int cutoff = hit < nk ? hit + 1 : nk;
+    const float trunc = c[cutoff - 1];                                  // :91-93
+    const float r = __fmul_rn(rng_next(rs), trunc);                     // :96
+    const int w = first_below(c, cutoff, r);                            // :98-105
+    tok = idv(w >= 0 ? w : 0);
+    if (pr_out) {
+      if (i0 < keff) pr_out[i0] = p0;
+      if (i1 < keff) pr_out[i1] = p1;
+    }
+  } else {
+    if (i0 < keff) e[i0] = cr_expf(__fsub_rn(v0, mx));                  // top_k.c:54
+    if (i1 < keff) e[i1] = cr_expf(__fsub_rn(v1, mx));
+    __syncwarp();
+    const float sum = seq_sum(e, keff);                                 // :55
+    const float p0 = i0 < keff ? __fdiv_rn(e[i0], sum) : 0.0f;          // :57-59
+    const float p1 = i1 < keff ? __fdiv_rn(e[i1], sum) : 0.0f;
+    __syncwarp();
+    if (i0 < keff) e[i0] = p0;
+    if (i1 < keff) e[i1] = p1;
+    __syncwarp();
+    seq_cum(e, keff, c, INFINITY);
+    const float r = rng_next(rs);                                       // :62
+    const int w = first_below(c, keff, r);                              // :63-70
+    tok = idv(w >= 0 ? w : 0);                                          // :72
+    if (pr_out) {
+      if (i0 < keff) pr_out[i0] = p0;
+      if (i1 < keff) pr_out[i1] = p1;
+    }
+  }
+  return tok;
+}
+
+}  // namespace pz

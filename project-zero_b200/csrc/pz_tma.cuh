@@ -80,3 +80,40 @@ constexpr long long kWaitBudget = 4000000000ll;
 constexpr long long kDrainBudget = 200000000ll;
 
 }  // namespace pz
+
+namespace pz {
+
+// ---------------------------------------------------------------------------
+// Per-thread asynchronous copies (cp.async, 16 bytes each) from global into
+// shared memory.  A thread waits only for its own copies (wait_group), so a
+// warp that reads back exactly the vectors its lanes copied needs no barrier
+// and no spin-wait.  These travel the load path of ordinary global loads
+// (about a microsecond of latency under full load), where a bulk copy
+// completes only when all of its bytes have landed.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Waits until at most n (0..7) of this thread's copy groups are pending.
+__device__ __forceinline__ void cp_async_wait_n(int n) {
+  switch (n) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    case 3: cp_async_wait<3>(); break;
+    case 4: cp_async_wait<4>(); break;
+    case 5: cp_async_wait<5>(); break;
+    case 6: cp_async_wait<6>(); break;
+    default: cp_async_wait<7>(); break;
+  }
+}
+
+}  // namespace pz

@@ -202,3 +202,30 @@ def test_register_queue_overflow_falls_back_exactly(cuda, pz, oracle_lib):
             g = run_gpu(cuda, pz, d, max_top_k=64, no_full_vocab=True)
             mism, _, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
             assert mism == 0, (dtype, k)
+
+
+def test_penalised_maximum_gives_way(cuda, pz, oracle_lib):
+    """A row's largest logits are history ids whose penalty pushes them below
+    their neighbours in the same 16-byte vector: the neighbours must win
+    (greedy) or enter the list (top-k)."""
+    rs = np.random.default_rng(11)
+    B, V = 8, 8192
+    for dtype in ("f32", "bf16"):
+        x = (rs.standard_normal((B, V)) * 0.5).astype(np.float32)
+        hist, off = [], [0]
+        for r in range(B):
+            p = 64 * (r + 1) + (r % 3)
+            x[r, p], x[r, p + 1], x[r, 4000 + r] = 20.0, 10.0, 9.0
+            ids = [p, 4000 + r] if r % 2 else [p]
+            hist += ids
+            off.append(len(hist))
+        logits = synth.to_bf16_bits(x) if dtype == "bf16" else x
+        for temp, k, p_ in [(0.0, 0, 1.0), (0.8, 3, 0.9), (0.8, 1, 1.0)]:
+            cfg = cases.configs(B, temperature=temp, top_k=k, top_p=p_, rep=100.0)
+            d = dict(logits=logits, cfg=cfg, rng=np.arange(3, 3 + B, dtype=np.uint64),
+                     hist=np.array(hist, dtype=np.int32), hist_off=np.array(off, dtype=np.int32))
+            g = run_gpu(cuda, pz, d, max_top_k=8, max_history=8)
+            tok, *_ = oracle_lib.sample_batch(d["logits"], d["cfg"], d["rng"], d["hist"], d["hist_off"])
+            assert (g["tokens"] == tok).all(), (dtype, temp, k)
+            mism, _, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+            assert mism == 0, (dtype, temp, k)
