@@ -511,6 +511,10 @@ __device__ __forceinline__ uint32_t warp_kth_u32(const uint32_t (&v)[R], int k, 
   return __reduce_min_sync(0xFFFFFFFFu, m);
 }
 
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // Barrier `id` (not 0, which __syncthreads uses) over the first `count`
 // threads' warps; count a multiple of 32.
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
@@ -539,11 +543,6 @@ __device__ __noinline__ float raw_floor(float t, const RowPlan P) {
 }
 
 // Out of line so the streaming loops stay short.
-__device__ __noinline__ uint32_t kth_of_4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, int k,
-                                          int bits) {
-  const uint32_t v[4] = {a, b, c, d};
-  return warp_kth_u32<4>(v, k, bits);
-}
 __device__ __noinline__ uint32_t kth_of_maxima(const uint32_t *s_maxv, int k, int bits) {
   const int lane = threadIdx.x & 31;
   uint32_t v[kSliceWarps];
@@ -551,13 +550,18 @@ __device__ __noinline__ uint32_t kth_of_maxima(const uint32_t *s_maxv, int k, in
   for (int r = 0; r < kSliceWarps; r++) v[r] = *reinterpret_cast<const volatile uint32_t *>(&s_maxv[r * 32 + lane]);
   return warp_kth_u32<kSliceWarps>(v, k, bits);
 }
+__device__ __noinline__ uint32_t kth_of_4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, int k,
+                                          int bits) {
+  const uint32_t v[4] = {a, b, c, d};
+  return warp_kth_u32<4>(v, k, bits);
+}
 
 constexpr int kTQ = 4;          // keys kept per thread in registers
 constexpr int kTQK = 64;        // lists up to this long use the register queues
 
 // Shared memory of slice_kernel:
-//   ring   NW x nslots x kChunkBytes  (per-warp bulk-copy rings; after the
-//          stream: the queues, the survivors and the rare exact rescan)
+//   ring   NW x nslots x kChunkBytes  (per-warp copy rings; after the
+//          stream: the queues' survivors and the rare exact rescan)
 //   cbuf   block buffer keys           (lists longer than kTQK only)
 //   hash   2 x hts words
 __host__ __device__ inline int slice_cbuf_keys(int kcap) {
@@ -591,7 +595,8 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   constexpr int NW = kSliceWarps;
   constexpr int VEC = LaneVec<T>::N;          // elements per 16-byte vector
   constexpr int HPT = 2 * VEC;                // block path: elements per offer
-  constexpr int XPT = 16;                     // extra-round items per thread
+  constexpr int XPT = 16;                     // rescan items per thread per round
+  constexpr int XPE = 4;                      // extra-round items per thread per round
   constexpr int MAXPER = (PZ_TOP_K_MAX + kCapB) / NT;
 
   extern __shared__ __align__(128) unsigned char smem[];
@@ -601,13 +606,12 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   __shared__ uint32_t s_tauv;           // ordered value: the block's admission bound
   __shared__ uint32_t s_b0;             // first bound, combined over the warps
   __shared__ unsigned long long s_dk;   // largest discarded key of the block
-  __shared__ int s_x0nan, s_timeout, s_cnt, s_n, s_rescan;
+  __shared__ unsigned long long s_dk2;  // the slice's k-th best key
+  __shared__ int s_x0nan, s_timeout, s_cnt, s_n;
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int row = blockIdx.y, sl = blockIdx.x;
-  const pz_sampler_config cfg = A.cfg[row];
-  const RowPlan P = plan_row(cfg, A.V_global);
   const int a = sl * A.L;
   const int b = min(A.V, a + A.L);
 
@@ -619,35 +623,9 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   uint32_t *hn = hk + A.hts;
   const uint32_t hmask = static_cast<uint32_t>(A.hts - 1);
   const uint32_t hshift = static_cast<uint32_t>(A.hshift);
-
   const T *rowp = static_cast<const T *>(A.logits) + static_cast<size_t>(row) * static_cast<size_t>(A.ld);
-  const bool greedy = P.mode == kModeGreedy;
-  // a list longer than this launch was sized for (hint broken): flag the row
-  const bool bad_k = P.mode == kModeTopK && (P.keff > A.kmax || P.keff > A.kcap);
-  const int k_sel = (P.mode == kModeTopK && !bad_k) ? P.keff : 1;
-  // lists up to kTQK long: per-thread register queues of the kTQ best keys,
-  // merged per CTA (exact unless a thread discarded a key that would have
-  // made the list, which is detected and redone); longer lists: one
-  // block-wide buffer.
-  const bool use_tq = k_sel > 1 && k_sel <= kTQK;
-  const bool use_block = k_sel > kTQK;
-  const unsigned long long tau0 = (P.mode == kModeTopK) ? key_topk_floor() : 0ull;
-  const float tau0_f = tau0 == 0ull ? -INFINITY : key_val(tau0);
-  const uint32_t goff = static_cast<uint32_t>(A.v_offset);
-  const int cap = A.kcap + kCapB;         // block list buffer
-  const int hwm = A.kcap + kCapB / 2;
 
-  int H = 0;
-  const int32_t *hrow = nullptr;
-  if (A.hist != nullptr && A.hist_off != nullptr && P.pen_on) {
-    const int h0 = A.hist_off[row];
-    H = A.hist_off[row + 1] - h0;
-    hrow = A.hist + h0;
-  }
-  const bool too_long = H > A.hcap;
-  const bool hist_on = H > 0 && !too_long && A.hts > 0;
-
-  // ---- aligned body, cut into chunks --------------------------------------
+  // ---- aligned body, cut into chunks; the first copies go out first -------
   const uintptr_t addr = reinterpret_cast<uintptr_t>(rowp + a);
   int head = static_cast<int>(((16u - (addr & 15u)) & 15u) / sizeof(T));
   if (head > b - a) head = b - a;
@@ -686,6 +664,42 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       }
     }
   };
+  // one copy group per chunk slot, empty past the end, so that "chunk i has
+  // landed" is always "at most NS - 1 groups pending"
+  for (int i = 0; i < NS; i++) {
+    if (i < nw) issue(i, i);
+    cp_async_commit();
+  }
+
+  // ---- the row's settings and history extent (loaded together) ------------
+  const pz_sampler_config cfg = A.cfg[row];
+  int h0 = 0, h1 = 0;
+  if (A.hist != nullptr && A.hist_off != nullptr) {
+    h0 = A.hist_off[row];
+    h1 = A.hist_off[row + 1];
+  }
+  const float x0raw = (a == 0 && A.v_offset == 0 && tid == 0) ? load_scalar<T>(rowp, 0) : 0.0f;
+  const RowPlan P = plan_row(cfg, A.V_global);
+  const bool greedy = P.mode == kModeGreedy;
+  // a list longer than this launch was sized for (hint broken): flag the row
+  const bool bad_k = P.mode == kModeTopK && (P.keff > A.kmax || P.keff > A.kcap);
+  const int k_sel = (P.mode == kModeTopK && !bad_k) ? P.keff : 1;
+  // lists up to kTQK long: per-thread register queues of the kTQ best keys,
+  // merged per CTA (exact unless a thread discarded a key that would have
+  // made the list, which is detected and redone); longer lists: one
+  // block-wide buffer.
+  const bool use_tq = k_sel > 1 && k_sel <= kTQK;
+  const bool use_block = k_sel > kTQK;
+  const unsigned long long tau0 = (P.mode == kModeTopK) ? key_topk_floor() : 0ull;
+  const float tau0_f = tau0 == 0ull ? -INFINITY : key_val(tau0);
+  const uint32_t goff = static_cast<uint32_t>(A.v_offset);
+  const int cap = A.kcap + kCapB;         // block list buffer
+  const int hwm = A.kcap + kCapB / 2;
+
+  const int H = P.pen_on ? h1 - h0 : 0;
+  const int32_t *hrow = A.hist + h0;
+  const bool too_long = H > A.hcap;
+  const bool hist_on = H > 0 && !too_long && A.hts > 0;
 
   if (tid == 0) {
     s_x0nan = 0;
@@ -699,12 +713,6 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   }
   s_maxv[tid] = kOrdNegInf;
   __syncthreads();
-  // one copy group per chunk slot, empty past the end, so that "chunk i has
-  // landed" is always "at most NS - 1 groups pending"
-  for (int i = 0; i < NS; i++) {
-    if (i < nw) issue(i, i);
-    cp_async_commit();
-  }
 
   // ---- the slice's history ids and counts (while the first copies fly) ---
   if (hist_on) {
@@ -712,10 +720,23 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       hk[i] = kHashEmpty;
       hn[i] = 0u;
     }
-    __syncthreads();
-    for (int j = tid; j < H; j += NT) {
-      const long long t = static_cast<long long>(hrow[j]) - A.v_offset;
-      if (t >= a && t < b) hash_insert(hk, hn, hmask, hshift, static_cast<uint32_t>(t));
+    // ids in batches (all loads of a batch in flight together); the logits
+    // they name are fetched into L2 now for the extra round below
+    constexpr int IPT = 4;
+    for (int base = 0; base < H; base += NT * IPT) {
+      long long t[IPT];
+#pragma unroll
+      for (int u = 0; u < IPT; u++) {
+        const int j = base + u * NT + tid;
+        t[u] = j < H ? static_cast<long long>(hrow[j]) - A.v_offset : -1;
+      }
+#pragma unroll
+      for (int u = 0; u < IPT; u++)
+        if (t[u] >= a && t[u] < b) prefetch_l2(rowp + t[u]);
+      if (base == 0) __syncthreads();  // the table is initialised
+#pragma unroll
+      for (int u = 0; u < IPT; u++)
+        if (t[u] >= a && t[u] < b) hash_insert(hk, hn, hmask, hshift, static_cast<uint32_t>(t[u]));
     }
     __syncthreads();
   }
@@ -772,21 +793,21 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
 
   // ---- head, tail and the penalised history ids: exact keys, first --------
   if (a == 0 && goff == 0 && tid == 0) {
-    float x = load_scalar<T>(rowp, 0);
+    float x = x0raw;
     const int c = hist_on ? hash_count(hk, hn, hmask, hshift, 0u) : 0;
     if (c > 0) x = penalize(x, c, P);
     const float v = greedy ? x : temper(x, P);
     s_x0nan = (v != v) ? 1 : 0;
   }
   const int n_extra = head + tail + (hist_on ? A.hts : 0);
-  for (int base = 0; base < n_extra; base += NT * XPT) {
-    float xv[XPT];
-    int lis[XPT], cnts[XPT];
+  for (int base = 0; base < n_extra; base += NT * XPE) {
+    float xv[XPE];
+    int lis[XPE], cnts[XPE];
     uint32_t have = 0;
     // the items' columns first (column a stands in for an empty item), then
     // every load at once, then the values
 #pragma unroll
-    for (int e = 0; e < XPT; e++) {
+    for (int e = 0; e < XPE; e++) {
       const int it = base + e * NT + tid;
       int li = a, cnt = 0;
       bool h = false;
@@ -810,9 +831,9 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       have |= h ? (1u << e) : 0u;
     }
 #pragma unroll
-    for (int e = 0; e < XPT; e++) xv[e] = load_scalar<T>(rowp, lis[e]);
+    for (int e = 0; e < XPE; e++) xv[e] = load_scalar<T>(rowp, lis[e]);
 #pragma unroll
-    for (int e = 0; e < XPT; e++) {
+    for (int e = 0; e < XPE; e++) {
       if (!((have >> e) & 1u)) continue;
       if (cnts[e] == 0 && in_hist(lis[e])) {
         have &= ~(1u << e);
@@ -823,20 +844,20 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       xv[e] = greedy ? x : temper(x, P);
     }
     if (use_block) {
-      unsigned long long keys[XPT];
+      unsigned long long keys[XPE];
       uint32_t valid = 0;
 #pragma unroll
-      for (int e = 0; e < XPT; e++) {
+      for (int e = 0; e < XPE; e++) {
         keys[e] = 0ull;
         if (((have >> e) & 1u) && xv[e] == xv[e]) {
           keys[e] = mkkey(xv[e], static_cast<uint32_t>(lis[e]) + goff);
           valid |= 1u << e;
         }
       }
-      offer_round<NT, MAXPER, XPT>(cbuf, cap, hwm, k_sel, sh, keys, valid);
+      offer_round<NT, MAXPER, XPE>(cbuf, cap, hwm, k_sel, sh, keys, valid);
     } else {
 #pragma unroll
-      for (int e = 0; e < XPT; e++)
+      for (int e = 0; e < XPE; e++)
         if (((have >> e) & 1u) && xv[e] == xv[e])
           offer_key(mkkey(xv[e], static_cast<uint32_t>(lis[e]) + goff));
     }
@@ -1120,6 +1141,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   }
   __syncthreads();
   bool exact_rescan = false;
+  int n_tq = 0;  // list length (queue path)
   if (use_tq) {
     // keys whose value is at or above the k-th largest thread maximum (at
     // least k_sel of them), then the best k_sel of those
@@ -1137,21 +1159,37 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       if (keep) lst[base + __popc(bal & lanemask_lt())] = qk[j];
     }
     __syncthreads();
-    if (warp == 0) {
-      int n = s_cnt;
-      unsigned long long kth = tau0;  // fewer than k real keys: any real discard counts
-      if (n >= k_sel) {
-        kth = warp_kth(lst, n, k_sel);
-        n = warp_compact_ge(lst, n, kth);
-      }
-      // exact unless some thread pushed out a key that beats the k-th
-      if (lane == 0) {
-        s_n = n;
-        s_rescan = s_dk > kth ? 1 : 0;
+    // Each survivor's rank is the number of survivors above it (keys are
+    // distinct); the best k_sel go straight to their place in sorted order.
+    const int n = s_cnt;
+    int rk[kTQ];
+    bool kept[kTQ];
+    bool any = false;
+#pragma unroll
+    for (int j = 0; j < kTQ; j++) {
+      rk[j] = 0;
+      kept[j] = qk[j] > tau0 && f2ord(key_val(qk[j])) >= bnd;
+      any |= kept[j];
+    }
+    if (any) {
+      for (int i = 0; i < n; i++) {
+        const unsigned long long o = lst[i];
+#pragma unroll
+        for (int j = 0; j < kTQ; j++) rk[j] += o > qk[j] ? 1 : 0;
       }
     }
+    __syncthreads();  // every survivor was ranked before the list is rewritten
+#pragma unroll
+    for (int j = 0; j < kTQ; j++) {
+      if (kept[j] && rk[j] < k_sel) lst[rk[j]] = qk[j];
+      if (kept[j] && rk[j] == k_sel - 1) s_dk2 = qk[j];
+    }
     __syncthreads();
-    exact_rescan = s_rescan != 0;
+    // fewer than k real keys: any real discard counts
+    const unsigned long long kth = n >= k_sel ? s_dk2 : tau0;
+    // exact unless some thread pushed out a key that beats the k-th
+    exact_rescan = s_dk > kth;
+    n_tq = n < k_sel ? n : k_sel;
   }
   if (exact_rescan) {
     // rare: redo the slice exactly with a block-wide buffer (all threads)
@@ -1199,7 +1237,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     m = s_n;
     for (int i = lane; i < m; i += 32) dst[i] = rb[i];
   } else if (use_tq) {
-    m = s_n;
+    m = n_tq;
     for (int i = lane; i < m; i += 32) dst[i] = lst[i];
   } else {
     unsigned long long bl = lane < NW ? s_red[lane] : 0ull;
@@ -1239,7 +1277,6 @@ __global__ void __launch_bounds__(128) finalize_kernel(const SliceArgs A, int wa
   float *fp = fe + A.kcap;
   int *ford = reinterpret_cast<int *>(fp + A.kcap);
   int *s_tokp = ford + A.kcap;
-  int &s_tok = *s_tokp;
 
   const pz_sampler_config cfg = A.cfg[row];
   const RowPlan P = plan_row(cfg, A.V_global);
