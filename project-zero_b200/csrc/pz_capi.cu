@@ -128,6 +128,9 @@ struct pz_sampler_ctx {
   int world = 1, rank = 0;
   unsigned long long *emit = nullptr;
   unsigned long long *gathered = nullptr;
+  // kernel timing: three events per call (start, after slice_kernel, end)
+  std::vector<cudaEvent_t> prof;
+  int prof_used = 0;
 
   template <typename T>
   bool alloc(T **p, size_t count) {
@@ -146,6 +149,8 @@ struct pz_sampler_ctx {
   void release() {
     for (void *q : allocs) cudaFree(q);
     allocs.clear();
+    for (cudaEvent_t e : prof) cudaEventDestroy(e);
+    prof.clear();
   }
 };
 
@@ -339,8 +344,15 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   const bool full_pass = !emit && !no_full;
   if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t), st) != cudaSuccess)
     return fail(PZ_ERR_CUDA);
+  cudaEvent_t *ev = nullptr;
+  if (ctx->prof_used * 3 + 3 <= static_cast<int>(ctx->prof.size())) {
+    ev = &ctx->prof[ctx->prof_used * 3];
+    ctx->prof_used++;
+    cudaEventRecord(ev[0], st);
+  }
   cudaError_t ce = pz::launch_slice(a, dtype, smem, st);
   if (ce != cudaSuccess) return fail_cuda(ce);
+  if (ev) cudaEventRecord(ev[1], st);
   ce = pz::launch_finalize(a, st);
   if (ce != cudaSuccess) return fail_cuda(ce);
   if (full_pass) {
@@ -368,6 +380,7 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     ce = pz::launch_full(f, dtype, grid, fsmem, st);
     if (ce != cudaSuccess) return fail_cuda(ce);
   }
+  if (ev) cudaEventRecord(ev[2], st);
   return PZ_OK;
 }
 
@@ -494,6 +507,47 @@ pz_status pz_sample_batch_static(const void *logits, pz_dtype dtype, int B,
   const pz_batch_hints h{PZ_STATIC_MAX_TOP_K, PZ_STATIC_MAX_HISTORY, 1, 0};
   return sample_impl(&view, logits, dtype, B, V, ld, 0, V, cfg, hist, hist_off, rng_state,
                      out_tokens, &h, outputs, stream, false);
+}
+
+pz_status pz_ctx_profile(pz_sampler_ctx *ctx, int n_calls) {
+  if (!ctx || n_calls < 0) return fail(PZ_ERR_INVALID_ARGS);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(PZ_ERR_CUDA);
+  for (cudaEvent_t e : ctx->prof) cudaEventDestroy(e);
+  ctx->prof.clear();
+  ctx->prof_used = 0;
+  for (int i = 0; i < 3 * n_calls; i++) {
+    cudaEvent_t e;
+    const cudaError_t ce = cudaEventCreate(&e);
+    if (ce != cudaSuccess) return fail_cuda(ce);
+    ctx->prof.push_back(e);
+  }
+  return PZ_OK;
+}
+
+pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms, double *rest_ms,
+                              int *calls) {
+  if (!ctx) return fail(PZ_ERR_INVALID_ARGS);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(PZ_ERR_CUDA);
+  double s1 = 0.0, s2 = 0.0;
+  for (int i = 0; i < ctx->prof_used; i++) {
+    cudaEvent_t *ev = &ctx->prof[i * 3];
+    cudaError_t ce = cudaEventSynchronize(ev[2]);
+    if (ce != cudaSuccess) return fail_cuda(ce);
+    float t1 = 0.0f, t2 = 0.0f;
+    ce = cudaEventElapsedTime(&t1, ev[0], ev[1]);
+    if (ce != cudaSuccess) return fail_cuda(ce);
+    ce = cudaEventElapsedTime(&t2, ev[1], ev[2]);
+    if (ce != cudaSuccess) return fail_cuda(ce);
+    s1 += t1;
+    s2 += t2;
+  }
+  if (slice_ms) *slice_ms = s1;
+  if (rest_ms) *rest_ms = s2;
+  if (calls) *calls = ctx->prof_used;
+  ctx->prof_used = 0;
+  return PZ_OK;
 }
 
 pz_status pz_rng_seed_batch(unsigned long long *rng_state, int B,

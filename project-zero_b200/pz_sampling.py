@@ -113,6 +113,9 @@ _sig("pz_sample_batch", ctypes.c_int,
      [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp,
       ctypes.POINTER(BatchHints), ctypes.POINTER(BatchOutputs), _vp])
 _sig("pz_rng_seed_batch", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_ulonglong, _vp, _vp])
+_sig("pz_ctx_profile", ctypes.c_int, [_vp, ctypes.c_int])
+_sig("pz_ctx_profile_read", ctypes.c_int,
+     [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int)])
 _sig("pz_sample_batch_static", ctypes.c_int,
      [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp,
       ctypes.POINTER(BatchOutputs), _vp])
@@ -306,6 +309,19 @@ class Sampler:
             _stream_handle(stream))
         _check(st, "pz_sample_batch")
         return out
+
+    def profile(self, n_calls):
+        """Times the kernels of the next n_calls sampling calls with CUDA
+        events (0 turns timing off)."""
+        _check(_lib.pz_ctx_profile(self._h, int(n_calls)), "pz_ctx_profile")
+
+    def profile_read(self):
+        """(slice_kernel ms, rest ms, calls) summed over the timed calls since
+        the last read."""
+        a, b, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
+        _check(_lib.pz_ctx_profile_read(self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(n)),
+               "pz_ctx_profile_read")
+        return a.value, b.value, n.value
 
     # ---- vocab sharding --------------------------------------------------
     @staticmethod
