@@ -720,9 +720,11 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       hk[i] = kHashEmpty;
       hn[i] = 0u;
     }
-    // ids in batches (all loads of a batch in flight together); the logits
-    // they name are fetched into L2 now for the extra round below
+    // ids in batches (all loads of a batch in flight together); argmax rows
+    // take the history round right after this, so the logits the ids name
+    // are fetched into L2 now
     constexpr int IPT = 4;
+    const bool pre = !use_tq && !use_block;
     for (int base = 0; base < H; base += NT * IPT) {
       long long t[IPT];
 #pragma unroll
@@ -730,9 +732,11 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
         const int j = base + u * NT + tid;
         t[u] = j < H ? static_cast<long long>(hrow[j]) - A.v_offset : -1;
       }
+      if (pre) {
 #pragma unroll
-      for (int u = 0; u < IPT; u++)
-        if (t[u] >= a && t[u] < b) prefetch_l2(rowp + t[u]);
+        for (int u = 0; u < IPT; u++)
+          if (t[u] >= a && t[u] < b) prefetch_l2(rowp + t[u]);
+      }
       if (base == 0) __syncthreads();  // the table is initialised
 #pragma unroll
       for (int u = 0; u < IPT; u++)
@@ -791,7 +795,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     }
   };
 
-  // ---- head, tail and the penalised history ids: exact keys, first --------
+  // ---- row 0's first logit (the NaN rule of argmax.c:3-13) ---------------
   if (a == 0 && goff == 0 && tid == 0) {
     float x = x0raw;
     const int c = hist_on ? hash_count(hk, hn, hmask, hshift, 0u) : 0;
@@ -799,71 +803,78 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     const float v = greedy ? x : temper(x, P);
     s_x0nan = (v != v) ? 1 : 0;
   }
-  const int n_extra = head + tail + (hist_on ? A.hts : 0);
-  for (int base = 0; base < n_extra; base += NT * XPE) {
-    float xv[XPE];
-    int lis[XPE], cnts[XPE];
-    uint32_t have = 0;
-    // the items' columns first (column a stands in for an empty item), then
-    // every load at once, then the values
-#pragma unroll
-    for (int e = 0; e < XPE; e++) {
-      const int it = base + e * NT + tid;
-      int li = a, cnt = 0;
-      bool h = false;
-      if (it < head) {
-        li = a + it;
-        h = true;
-      } else if (it < head + tail) {
-        li = b_al + (it - head);
-        h = true;
-      } else if (it < n_extra) {
-        const int i = it - head - tail;
-        const uint32_t t = hk[i];
-        if (t != kHashEmpty) {
-          li = static_cast<int>(t);
-          cnt = static_cast<int>(hn[i]);
-          h = true;
-        }
-      }
-      lis[e] = li;
-      cnts[e] = cnt;
-      have |= h ? (1u << e) : 0u;
-    }
-#pragma unroll
-    for (int e = 0; e < XPE; e++) xv[e] = load_scalar<T>(rowp, lis[e]);
-#pragma unroll
-    for (int e = 0; e < XPE; e++) {
-      if (!((have >> e) & 1u)) continue;
-      if (cnts[e] == 0 && in_hist(lis[e])) {
-        have &= ~(1u << e);
-        continue;
-      }
-      float x = xv[e];
-      if (cnts[e] > 0) x = penalize(x, cnts[e], P);
-      xv[e] = greedy ? x : temper(x, P);
-    }
-    if (use_block) {
-      unsigned long long keys[XPE];
-      uint32_t valid = 0;
-#pragma unroll
+
+  // ---- head, tail and the penalised history ids: exact keys ---------------
+  // Argmax rows take them before the stream (the best of them is a strong
+  // first bound); list rows after it (the tight bound rejects most of them).
+  auto history_round = [&]() {
+    const int n_extra = head + tail + (hist_on ? A.hts : 0);
+    for (int base = 0; base < n_extra; base += NT * XPE) {
+      float xv[XPE];
+      int lis[XPE], cnts[XPE];
+      uint32_t have = 0;
+      // the items' columns first (column a stands in for an empty item), then
+      // every load at once, then the values
+  #pragma unroll
       for (int e = 0; e < XPE; e++) {
-        keys[e] = 0ull;
-        if (((have >> e) & 1u) && xv[e] == xv[e]) {
-          keys[e] = mkkey(xv[e], static_cast<uint32_t>(lis[e]) + goff);
-          valid |= 1u << e;
+        const int it = base + e * NT + tid;
+        int li = a, cnt = 0;
+        bool h = false;
+        if (it < head) {
+          li = a + it;
+          h = true;
+        } else if (it < head + tail) {
+          li = b_al + (it - head);
+          h = true;
+        } else if (it < n_extra) {
+          const int i = it - head - tail;
+          const uint32_t t = hk[i];
+          if (t != kHashEmpty) {
+            li = static_cast<int>(t);
+            cnt = static_cast<int>(hn[i]);
+            h = true;
+          }
         }
+        lis[e] = li;
+        cnts[e] = cnt;
+        have |= h ? (1u << e) : 0u;
       }
-      offer_round<NT, MAXPER, XPE>(cbuf, cap, hwm, k_sel, sh, keys, valid);
-    } else {
-#pragma unroll
-      for (int e = 0; e < XPE; e++)
-        if (((have >> e) & 1u) && xv[e] == xv[e])
-          offer_key(mkkey(xv[e], static_cast<uint32_t>(lis[e]) + goff));
+  #pragma unroll
+      for (int e = 0; e < XPE; e++) xv[e] = load_scalar<T>(rowp, lis[e]);
+  #pragma unroll
+      for (int e = 0; e < XPE; e++) {
+        if (!((have >> e) & 1u)) continue;
+        if (cnts[e] == 0 && in_hist(lis[e])) {
+          have &= ~(1u << e);
+          continue;
+        }
+        float x = xv[e];
+        if (cnts[e] > 0) x = penalize(x, cnts[e], P);
+        xv[e] = greedy ? x : temper(x, P);
+      }
+      if (use_block) {
+        unsigned long long keys[XPE];
+        uint32_t valid = 0;
+  #pragma unroll
+        for (int e = 0; e < XPE; e++) {
+          keys[e] = 0ull;
+          if (((have >> e) & 1u) && xv[e] == xv[e]) {
+            keys[e] = mkkey(xv[e], static_cast<uint32_t>(lis[e]) + goff);
+            valid |= 1u << e;
+          }
+        }
+        offer_round<NT, MAXPER, XPE>(cbuf, cap, hwm, k_sel, sh, keys, valid);
+      } else {
+        // after the stream the bound is tight: most values stop here
+  #pragma unroll
+        for (int e = 0; e < XPE; e++)
+          if (((have >> e) & 1u) && xv[e] >= tau_wf)
+            offer_key(mkkey(xv[e], static_cast<uint32_t>(lis[e]) + goff));
+      }
     }
-  }
-  if (use_tq && qk[0] > tau0) s_maxv[tid] = f2ord(key_val(qk[0]));
+  };
   if (!use_tq && !use_block) {
+    history_round();
     const uint32_t bo = __reduce_max_sync(0xFFFFFFFFu, best != 0ull ? f2ord(best_f) : kOrdNegInf);
     if (lane == 0) atomicMax(&s_tauv, bo);
   }
@@ -930,7 +941,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
           }
         }
         const int np = min(NW, nchunks);
-        const uint32_t bj = kth_of_4(vm[0], vm[1], vm[2], vm[3], (k_sel + np - 1) / np, 12);
+        const uint32_t bj = kth_of_4(vm[0], vm[1], vm[2], vm[3], (k_sel + np - 1) / np, 32);
         if (lane == 0) atomicMin(&s_b0, bj);
         named_bar_sync(1, np * 32);  // the warps with chunks (warps 0 .. np-1)
         const uint32_t b0 = *reinterpret_cast<volatile uint32_t *>(&s_b0);
@@ -982,7 +993,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       if (i == refresh_at) {
         // the k-th largest of the threads' best values: k distinct elements
         // are at or above it; maxima only grow, so stale entries keep it valid
-        const uint32_t bnd = kth_of_maxima(s_maxv, k_sel, 12);
+        const uint32_t bnd = kth_of_maxima(s_maxv, k_sel, 32);
         if (lane == 0) atomicMax(&s_tauv, bnd);
       }
       // this lane has read its vectors of the slot (every value fed the
@@ -1117,6 +1128,9 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     }
   }
   cp_async_wait<0>();
+
+  // list rows: the history round after the stream, where the bounds are tight
+  if (use_tq || use_block) history_round();
   __syncthreads();
   const bool timed_out = s_timeout != 0;
 
