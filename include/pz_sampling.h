@@ -264,10 +264,11 @@ pz_status pz_sample_batch_static(const void *logits, pz_dtype dtype, int B,
  * call's stream.  pz_ctx_profile_read waits for the recorded calls and
  * returns the summed milliseconds of the streaming kernel (slice_kernel) and
  * of the rest of each call (the row finaliser and any full-vocabulary
- * pass), and the number of calls timed; it then starts a new count. */
+ * pass), the number of calls timed and the number of kernels they
+ * launched; it then starts a new count. */
 pz_status pz_ctx_profile(pz_sampler_ctx *ctx, int n_calls);
 pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms,
-                              double *rest_ms, int *calls);
+                              double *rest_ms, int *calls, int *kernels);
 
 /* Seeds B RNG states on the device: state[r] = seed_base + r (0 -> 1, as
  * rng_seed does), or state[r] = seeds[r] when `seeds` (device) is non-NULL. */

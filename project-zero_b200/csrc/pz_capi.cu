@@ -131,6 +131,7 @@ struct pz_sampler_ctx {
   // kernel timing: three events per call (start, after slice_kernel, end)
   std::vector<cudaEvent_t> prof;
   int prof_used = 0;
+  int prof_kernels = 0;
 
   template <typename T>
   bool alloc(T **p, size_t count) {
@@ -353,8 +354,12 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   cudaError_t ce = pz::launch_slice(a, dtype, smem, st);
   if (ce != cudaSuccess) return fail_cuda(ce);
   if (ev) cudaEventRecord(ev[1], st);
-  ce = pz::launch_finalize(a, st);
-  if (ce != cudaSuccess) return fail_cuda(ce);
+  int kernels = 1;
+  if (a.S > 1) {  // with one slice per row, slice_kernel decides the rows itself
+    ce = pz::launch_finalize(a, st);
+    if (ce != cudaSuccess) return fail_cuda(ce);
+    kernels++;
+  }
   if (full_pass) {
     FullArgs f{};
     f.logits = logits;
@@ -379,8 +384,12 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     const int grid = std::min(ctx->full_grid, B);
     ce = pz::launch_full(f, dtype, grid, fsmem, st);
     if (ce != cudaSuccess) return fail_cuda(ce);
+    kernels++;
   }
-  if (ev) cudaEventRecord(ev[2], st);
+  if (ev) {
+    cudaEventRecord(ev[2], st);
+    ctx->prof_kernels += kernels;
+  }
   return PZ_OK;
 }
 
@@ -516,6 +525,7 @@ pz_status pz_ctx_profile(pz_sampler_ctx *ctx, int n_calls) {
   for (cudaEvent_t e : ctx->prof) cudaEventDestroy(e);
   ctx->prof.clear();
   ctx->prof_used = 0;
+  ctx->prof_kernels = 0;
   for (int i = 0; i < 3 * n_calls; i++) {
     cudaEvent_t e;
     const cudaError_t ce = cudaEventCreate(&e);
@@ -526,7 +536,7 @@ pz_status pz_ctx_profile(pz_sampler_ctx *ctx, int n_calls) {
 }
 
 pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms, double *rest_ms,
-                              int *calls) {
+                              int *calls, int *kernels) {
   if (!ctx) return fail(PZ_ERR_INVALID_ARGS);
   DeviceGuard g(ctx->device);
   if (!g.ok) return fail(PZ_ERR_CUDA);
@@ -546,7 +556,9 @@ pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms, double *res
   if (slice_ms) *slice_ms = s1;
   if (rest_ms) *rest_ms = s2;
   if (calls) *calls = ctx->prof_used;
+  if (kernels) *kernels = ctx->prof_kernels;
   ctx->prof_used = 0;
+  ctx->prof_kernels = 0;
   return PZ_OK;
 }
 

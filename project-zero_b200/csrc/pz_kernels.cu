@@ -1244,6 +1244,42 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   }
   if (warp != 0) return;
 
+  if (A.S == 1) {
+    // The row's only slice: decide the row here.  The list is already in
+    // order (rank merge) except on the block-buffer paths; the list
+    // arithmetic's scratch sits in the ring after the first 16 KB.
+    float *fe = reinterpret_cast<float *>(ring + 16384);
+    float *fp = fe + A.kcap;
+    int *ford = reinterpret_cast<int *>(fp + A.kcap);
+    int *s_tokp = ford + A.kcap;
+    unsigned long long *fl = lst;
+    int n_sel = 0;
+    unsigned long long gbest = 0ull;
+    if (use_block || exact_rescan) {
+      fl = rb;
+      n_sel = s_n;
+      for (int i = n_sel + lane; i < A.kcap; i += 32) fl[i] = 0ull;
+      __syncwarp();
+      warp_sort_desc(fl, A.kcap);
+    } else if (use_tq) {
+      n_sel = n_tq;
+      for (int i = n_sel + lane; i < A.kcap; i += 32) fl[i] = 0ull;
+      __syncwarp();
+    } else {
+      const unsigned long long bl = lane < NW ? s_red[lane] : 0ull;
+      gbest = warp_max_u64(bl);
+      if (P.mode == kModeTopK) {  // k_eff == 1 (or a rejected list length)
+        n_sel = gbest > tau0 ? 1 : 0;
+        if (lane == 0) fl[0] = gbest;
+        for (int i = 1 + lane; i < A.kcap; i += 32) fl[i] = 0ull;
+        __syncwarp();
+      }
+    }
+    finalize_row(A, row, P, bad_k, too_long, timed_out, s_x0nan != 0, fl, n_sel, gbest, fe, fp, ford,
+                 s_tokp);
+    return;
+  }
+
   int m = 0;
   unsigned long long *dst =
       A.slice_keys + (static_cast<size_t>(row) * A.S + sl) * static_cast<size_t>(A.kcap);

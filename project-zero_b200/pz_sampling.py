@@ -115,7 +115,8 @@ _sig("pz_sample_batch", ctypes.c_int,
 _sig("pz_rng_seed_batch", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_ulonglong, _vp, _vp])
 _sig("pz_ctx_profile", ctypes.c_int, [_vp, ctypes.c_int])
 _sig("pz_ctx_profile_read", ctypes.c_int,
-     [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int)])
+     [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int),
+      ctypes.POINTER(ctypes.c_int)])
 _sig("pz_sample_batch_static", ctypes.c_int,
      [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp,
       ctypes.POINTER(BatchOutputs), _vp])
@@ -316,12 +317,12 @@ class Sampler:
         _check(_lib.pz_ctx_profile(self._h, int(n_calls)), "pz_ctx_profile")
 
     def profile_read(self):
-        """(slice_kernel ms, rest ms, calls) summed over the timed calls since
-        the last read."""
-        a, b, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
-        _check(_lib.pz_ctx_profile_read(self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(n)),
-               "pz_ctx_profile_read")
-        return a.value, b.value, n.value
+        """(slice_kernel ms, rest ms, calls, kernels launched) summed over the
+        timed calls since the last read."""
+        a, b, n, k = ctypes.c_double(), ctypes.c_double(), ctypes.c_int(), ctypes.c_int()
+        _check(_lib.pz_ctx_profile_read(self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(n),
+                                        ctypes.byref(k)), "pz_ctx_profile_read")
+        return a.value, b.value, n.value, k.value
 
     # ---- vocab sharding --------------------------------------------------
     @staticmethod
