@@ -1201,9 +1201,93 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     __syncthreads();
     // fewer than k real keys: any real discard counts
     const unsigned long long kth = n >= k_sel ? s_dk2 : tau0;
-    // exact unless some thread pushed out a key that beats the k-th
-    exact_rescan = s_dk > kth;
     n_tq = n < k_sel ? n : k_sel;
+    // A thread whose largest discarded key beats the k-th may have pushed
+    // keys of the list out of its queue.  Its warp re-reads that thread's
+    // elements (the thread its history items) and adds back every key at or
+    // above the k-th that the queue does not hold; the list is then ranked
+    // again.  Every other thread's keys at or above the k-th are in the list.
+    const bool bad = dk > kth;
+    if (__syncthreads_or(bad)) {
+      constexpr int kXMax = 2048;
+      unsigned long long *xl = lst + n_tq;  // added keys, after the list
+      if (tid == 0) s_cnt = 0;
+      __syncthreads();
+      auto add_back = [&](unsigned long long key, const unsigned long long (&held)[kTQ]) {
+        bool in_q = false;
+#pragma unroll
+        for (int j = 0; j < kTQ; j++) in_q |= held[j] == key;
+        if (key >= kth && key > tau0 && !in_q) {
+          const int pos = atomicAdd(&s_cnt, 1);
+          if (pos < kXMax) xl[pos] = key;
+        }
+      };
+      uint32_t offenders = __ballot_sync(0xFFFFFFFFu, bad);
+      while (offenders) {
+        const int L = __ffs(offenders) - 1;
+        offenders &= offenders - 1;
+        unsigned long long held[kTQ];
+#pragma unroll
+        for (int j = 0; j < kTQ; j++) held[j] = __shfl_sync(0xFFFFFFFFu, qk[j], L);
+        // lane L's vectors: u*32 + L of each of this warp's chunks
+        for (int t = lane; t < nw * kLaneVecs; t += 32) {
+          const int c = warp + NW * (t / kLaneVecs);
+          const int j = (t % kLaneVecs) * 32 + L;
+          const int cv = c == nchunks - 1 ? (body_bytes - c * kChunkBytes) >> 4 : kChunkBytes / 16;
+          if (j >= cv) continue;
+          const uint4 qq = __ldg(reinterpret_cast<const uint4 *>(body + static_cast<size_t>(c) * kChunkBytes) + j);
+          const int el = a_al + c * (kChunkBytes / static_cast<int>(sizeof(T))) + j * VEC;
+#pragma unroll
+          for (int w = 0; w < VEC; w++) {
+            const int li = el + w;
+            if (in_hist(li)) continue;
+            const float v = temper(LaneVec<T>::elem(qq, w), P);
+            if (v == v) add_back(mkkey(v, static_cast<uint32_t>(li) + goff), held);
+          }
+        }
+      }
+      if (bad) {
+        // this thread's items of the history round (item it: tid, tid + NT, ...)
+        for (int it = tid; it < head + tail + (hist_on ? A.hts : 0); it += NT) {
+          int li, cnt = 0;
+          if (it < head) {
+            li = a + it;
+          } else if (it < head + tail) {
+            li = b_al + (it - head);
+          } else {
+            const int i = it - head - tail;
+            if (hk[i] == kHashEmpty) continue;
+            li = static_cast<int>(hk[i]);
+            cnt = static_cast<int>(hn[i]);
+          }
+          if (cnt == 0 && in_hist(li)) continue;
+          float x = load_scalar<T>(rowp, li);
+          if (cnt > 0) x = penalize(x, cnt, P);
+          const float v = temper(x, P);
+          if (v == v) add_back(mkkey(v, static_cast<uint32_t>(li) + goff), qk);
+        }
+      }
+      __syncthreads();
+      const int ne = s_cnt;
+      if (ne > kXMax) {
+        exact_rescan = true;  // too many to add back: redo the slice below
+      } else {
+        // rank the list and the added keys together; the best k_sel, in
+        // order, go to tmp and then back to the list
+        const int m = n_tq + ne;
+        unsigned long long *tmp = lst + m;
+        for (int i = tid; i < m; i += NT) {
+          const unsigned long long key = lst[i];
+          int r = 0;
+          for (int j2 = 0; j2 < m; j2++) r += lst[j2] > key ? 1 : 0;
+          if (r < k_sel) tmp[r] = key;
+        }
+        __syncthreads();
+        n_tq = m < k_sel ? m : k_sel;
+        for (int i = tid; i < n_tq; i += NT) lst[i] = tmp[i];
+        __syncthreads();
+      }
+    }
   }
   if (exact_rescan) {
     // rare: redo the slice exactly with a block-wide buffer (all threads)
