@@ -563,15 +563,20 @@ constexpr int kTQK = 64;        // lists up to this long use the register queues
 //   ring   NW x nslots x kChunkBytes  (per-warp copy rings; after the
 //          stream: the queues' survivors and the rare exact rescan)
 //   cbuf   block buffer keys           (lists longer than kTQK only)
-//   hash   2 x hts words
+//   hash   2 x hts words                (history ids and counts)
+//   hbm    V/128 words                  (one bit per 4 columns: a history id there)
 __host__ __device__ inline int slice_cbuf_keys(int kcap) {
   return kcap > kTQK ? kcap + kCapB : 0;
 }
 
-size_t slice_smem_bytes(int kcap, int hts, int nslots) {
+__host__ __device__ inline int slice_hbm_words(int V, int hts) {
+  return hts > 0 ? (V + 127) >> 7 : 0;
+}
+
+size_t slice_smem_bytes(int kcap, int hts, int nslots, int V) {
   return static_cast<size_t>(nslots) * kSliceWarps * kChunkBytes +
          sizeof(unsigned long long) * static_cast<size_t>(slice_cbuf_keys(kcap)) +
-         sizeof(uint32_t) * 2 * static_cast<size_t>(hts);
+         sizeof(uint32_t) * (2 * static_cast<size_t>(hts) + slice_hbm_words(V, hts));
 }
 
 // Ring slots per warp: kSlots chunks of 2 KB in flight per warp (48 KB per
@@ -605,6 +610,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   __shared__ uint32_t s_maxv[NT];       // ordered value of each thread's best key
   __shared__ uint32_t s_tauv;           // ordered value: the block's admission bound
   __shared__ uint32_t s_b0;             // first bound, combined over the warps
+  __shared__ RowPlan s_plan;
   __shared__ unsigned long long s_dk;   // largest discarded key of the block
   __shared__ unsigned long long s_dk2;  // the slice's k-th best key
   __shared__ int s_x0nan, s_timeout, s_cnt, s_n;
@@ -621,6 +627,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       reinterpret_cast<unsigned long long *>(smem + static_cast<size_t>(NW) * NS * kChunkBytes);
   uint32_t *hk = reinterpret_cast<uint32_t *>(cbuf + slice_cbuf_keys(A.kcap));
   uint32_t *hn = hk + A.hts;
+  uint32_t *hbm = hn + A.hts;  // one bit per 4 columns of the row
   const uint32_t hmask = static_cast<uint32_t>(A.hts - 1);
   const uint32_t hshift = static_cast<uint32_t>(A.hshift);
   const T *rowp = static_cast<const T *>(A.logits) + static_cast<size_t>(row) * static_cast<size_t>(A.ld);
@@ -679,29 +686,30 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     h1 = A.hist_off[row + 1];
   }
   const float x0raw = (a == 0 && A.v_offset == 0 && tid == 0) ? load_scalar<T>(rowp, 0) : 0.0f;
-  const RowPlan P = plan_row(cfg, A.V_global);
-  const bool greedy = P.mode == kModeGreedy;
+  const RowPlan P0 = plan_row(cfg, A.V_global);
+  const bool greedy = P0.mode == kModeGreedy;
   // a list longer than this launch was sized for (hint broken): flag the row
-  const bool bad_k = P.mode == kModeTopK && (P.keff > A.kmax || P.keff > A.kcap);
-  const int k_sel = (P.mode == kModeTopK && !bad_k) ? P.keff : 1;
+  const bool bad_k = P0.mode == kModeTopK && (P0.keff > A.kmax || P0.keff > A.kcap);
+  const int k_sel = (P0.mode == kModeTopK && !bad_k) ? P0.keff : 1;
   // lists up to kTQK long: per-thread register queues of the kTQ best keys,
   // merged per CTA (exact unless a thread discarded a key that would have
   // made the list, which is detected and redone); longer lists: one
   // block-wide buffer.
   const bool use_tq = k_sel > 1 && k_sel <= kTQK;
   const bool use_block = k_sel > kTQK;
-  const unsigned long long tau0 = (P.mode == kModeTopK) ? key_topk_floor() : 0ull;
+  const unsigned long long tau0 = (P0.mode == kModeTopK) ? key_topk_floor() : 0ull;
   const float tau0_f = tau0 == 0ull ? -INFINITY : key_val(tau0);
   const uint32_t goff = static_cast<uint32_t>(A.v_offset);
   const int cap = A.kcap + kCapB;         // block list buffer
   const int hwm = A.kcap + kCapB / 2;
 
-  const int H = P.pen_on ? h1 - h0 : 0;
+  const int H = P0.pen_on ? h1 - h0 : 0;
   const int32_t *hrow = A.hist + h0;
   const bool too_long = H > A.hcap;
   const bool hist_on = H > 0 && !too_long && A.hts > 0;
 
   if (tid == 0) {
+    s_plan = P0;
     s_x0nan = 0;
     s_timeout = 0;
     s_cnt = 0;
@@ -713,6 +721,9 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   }
   s_maxv[tid] = kOrdNegInf;
   __syncthreads();
+  // The row plan from here on is read from shared memory: its fields are
+  // used now and then, and would otherwise hold registers through the stream.
+  const RowPlan &P = s_plan;
 
   // ---- the slice's history ids and counts (while the first copies fly) ---
   if (hist_on) {
@@ -720,6 +731,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       hk[i] = kHashEmpty;
       hn[i] = 0u;
     }
+    for (int i = tid; i < slice_hbm_words(A.V, A.hts); i += NT) hbm[i] = 0u;
     // ids in batches (all loads of a batch in flight together); argmax rows
     // take the history round right after this, so the logits the ids name
     // are fetched into L2 now
@@ -740,12 +752,17 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       if (base == 0) __syncthreads();  // the table is initialised
 #pragma unroll
       for (int u = 0; u < IPT; u++)
-        if (t[u] >= a && t[u] < b) hash_insert(hk, hn, hmask, hshift, static_cast<uint32_t>(t[u]));
+        if (t[u] >= a && t[u] < b) {
+          hash_insert(hk, hn, hmask, hshift, static_cast<uint32_t>(t[u]));
+          atomicOr(&hbm[t[u] >> 7], 1u << ((t[u] >> 2) & 31));
+        }
     }
     __syncthreads();
   }
+  // the bitmap answers most lookups; a set bit sends the id to the table
   auto in_hist = [&](int li) -> bool {
-    return hist_on && hash_count(hk, hn, hmask, hshift, static_cast<uint32_t>(li)) > 0;
+    return hist_on && ((hbm[li >> 7] >> ((li >> 2) & 31)) & 1u) != 0u &&
+           hash_count(hk, hn, hmask, hshift, static_cast<uint32_t>(li)) > 0;
   };
 
   // register queue of this thread's best keys (descending), the largest key
@@ -989,6 +1006,11 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
         }
         if (qk[0] != top0) s_maxv[tid] = f2ord(key_val(qk[0]));
         retune();
+      }
+      if (hist_on && i == (nw > 3 ? nw - 3 : 0)) {
+        // the history round follows the stream: fetch its logits into L2
+        for (int it = tid; it < A.hts; it += NT)
+          if (hk[it] != kHashEmpty) prefetch_l2(rowp + hk[it]);
       }
       if (i == refresh_at) {
         // the k-th largest of the threads' best values: k distinct elements

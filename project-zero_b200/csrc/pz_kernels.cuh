@@ -102,7 +102,7 @@ struct MergeArgs {               // vocab-sharded merge after the allgather
 // Launchers (pz_kernels.cu).  Return cudaGetLastError() after the launch.
 cudaError_t launch_slice(const SliceArgs &a, int dtype, size_t smem,
                          cudaStream_t st);
-size_t slice_smem_bytes(int kcap, int hts, int nstages);
+size_t slice_smem_bytes(int kcap, int hts, int nstages, int V);
 int slice_stages(int kcap, int hts);
 cudaError_t launch_finalize(const SliceArgs &a, cudaStream_t st);
 __host__ __device__ size_t finalize_smem_per_warp(int S, int kcap);
