@@ -1181,10 +1181,15 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   if (use_tq) {
     // keys whose value is at or above the k-th largest thread maximum (at
     // least k_sel of them), then the best k_sel of those
-    uint32_t v8[NW];
+    if (warp == 0) {
+      uint32_t v8[NW];
 #pragma unroll
-    for (int r = 0; r < NW; r++) v8[r] = s_maxv[r * 32 + lane];
-    const uint32_t bnd = warp_kth_u32<NW>(v8, k_sel, 32);
+      for (int r = 0; r < NW; r++) v8[r] = s_maxv[r * 32 + lane];
+      const uint32_t bw = warp_kth_u32<NW>(v8, k_sel, 32);
+      if (lane == 0) s_b0 = bw;
+    }
+    __syncthreads();
+    const uint32_t bnd = s_b0;
 #pragma unroll
     for (int j = 0; j < kTQ; j++) {
       const bool keep = qk[j] > tau0 && f2ord(key_val(qk[j])) >= bnd;
@@ -1198,27 +1203,35 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     // Each survivor's rank is the number of survivors above it (keys are
     // distinct); the best k_sel go straight to their place in sorted order.
     const int n = s_cnt;
-    int rk[kTQ];
-    bool kept[kTQ];
-    bool any = false;
-#pragma unroll
-    for (int j = 0; j < kTQ; j++) {
-      rk[j] = 0;
-      kept[j] = qk[j] > tau0 && f2ord(key_val(qk[j])) >= bnd;
-      any |= kept[j];
-    }
-    if (any) {
-      for (int i = 0; i < n; i++) {
-        const unsigned long long o = lst[i];
-#pragma unroll
-        for (int j = 0; j < kTQ; j++) rk[j] += o > qk[j] ? 1 : 0;
+    if (n <= 64) {
+      // the usual case: one warp sorts the survivors in place
+      if (warp == 0) {
+        warp_rank_sort_desc(lst, n);
+        if (lane == 0 && n >= k_sel) s_dk2 = lst[k_sel - 1];
       }
-    }
-    __syncthreads();  // every survivor was ranked before the list is rewritten
+    } else {
+      int rk[kTQ];
+      bool kept[kTQ];
+      bool any = false;
 #pragma unroll
-    for (int j = 0; j < kTQ; j++) {
-      if (kept[j] && rk[j] < k_sel) lst[rk[j]] = qk[j];
-      if (kept[j] && rk[j] == k_sel - 1) s_dk2 = qk[j];
+      for (int j = 0; j < kTQ; j++) {
+        rk[j] = 0;
+        kept[j] = qk[j] > tau0 && f2ord(key_val(qk[j])) >= bnd;
+        any |= kept[j];
+      }
+      if (any) {
+        for (int i = 0; i < n; i++) {
+          const unsigned long long o = lst[i];
+#pragma unroll
+          for (int j = 0; j < kTQ; j++) rk[j] += o > qk[j] ? 1 : 0;
+        }
+      }
+      __syncthreads();  // every survivor was ranked before the list is rewritten
+#pragma unroll
+      for (int j = 0; j < kTQ; j++) {
+        if (kept[j] && rk[j] < k_sel) lst[rk[j]] = qk[j];
+        if (kept[j] && rk[j] == k_sel - 1) s_dk2 = qk[j];
+      }
     }
     __syncthreads();
     // fewer than k real keys: any real discard counts
