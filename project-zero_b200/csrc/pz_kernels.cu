@@ -707,6 +707,12 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   const int32_t *hrow = A.hist + h0;
   const bool too_long = H > A.hcap;
   const bool hist_on = H > 0 && !too_long && A.hts > 0;
+  // Penalties that can only lower a value (rep >= 1, freq >= 0, pres >= 0):
+  // a history id whose raw value is below the bound stays below it, so list
+  // rows score history ids inside the stream with their penalised value
+  // (no separate round, no gathers).  Other penalties: the history round.
+  const bool pen_dec = P0.rep >= 1.0f && P0.freq >= 0.0f && P0.pres >= 0.0f;
+  const bool hist_stream = hist_on && use_tq && pen_dec;
 
   if (tid == 0) {
     s_plan = P0;
@@ -760,10 +766,12 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     __syncthreads();
   }
   // the bitmap answers most lookups; a set bit sends the id to the table
-  auto in_hist = [&](int li) -> bool {
-    return hist_on && ((hbm[li >> 7] >> ((li >> 2) & 31)) & 1u) != 0u &&
-           hash_count(hk, hn, hmask, hshift, static_cast<uint32_t>(li)) > 0;
+  auto hist_count = [&](int li) -> int {
+    return hist_on && ((hbm[li >> 7] >> ((li >> 2) & 31)) & 1u) != 0u
+               ? hash_count(hk, hn, hmask, hshift, static_cast<uint32_t>(li))
+               : 0;
   };
+  auto in_hist = [&](int li) -> bool { return hist_count(li) > 0; };
 
   // register queue of this thread's best keys (descending), the largest key
   // it discarded, and their values for the cheap float tests
@@ -825,7 +833,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   // Argmax rows take them before the stream (the best of them is a strong
   // first bound); list rows after it (the tight bound rejects most of them).
   auto history_round = [&]() {
-    const int n_extra = head + tail + (hist_on ? A.hts : 0);
+    const int n_extra = head + tail + ((hist_on && !hist_stream) ? A.hts : 0);
     for (int base = 0; base < n_extra; base += NT * XPE) {
       float xv[XPE];
       int lis[XPE], cnts[XPE];
@@ -994,8 +1002,15 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
           pend &= pend - 1;
           const int pos = ((e / VEC) * 32 + lane) * VEC + (e % VEC);  // element within the chunk
           const int li = e0 + pos;
-          if (in_hist(li)) continue;
-          const float v = temper(LaneVec<T>::smem(sb, pos), P);
+          float x = LaneVec<T>::smem(sb, pos);
+          if (hist_on) {
+            const int hc = hist_count(li);
+            if (hc > 0) {
+              if (!hist_stream) continue;  // offered by the history round
+              x = penalize(x, hc, P);
+            }
+          }
+          const float v = temper(x, P);
           const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
           if (key > qk[kTQ - 1]) {
             q_insert(key);
@@ -1007,7 +1022,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
         if (qk[0] != top0) s_maxv[tid] = f2ord(key_val(qk[0]));
         retune();
       }
-      if (hist_on && i == (nw > 3 ? nw - 3 : 0)) {
+      if (hist_on && !hist_stream && i == (nw > 3 ? nw - 3 : 0)) {
         // the history round follows the stream: fetch its logits into L2
         for (int it = tid; it < A.hts; it += NT)
           if (hk[it] != kHashEmpty) prefetch_l2(rowp + hk[it]);
@@ -1275,15 +1290,20 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
 #pragma unroll
           for (int w = 0; w < VEC; w++) {
             const int li = el + w;
-            if (in_hist(li)) continue;
-            const float v = temper(LaneVec<T>::elem(qq, w), P);
+            float x = LaneVec<T>::elem(qq, w);
+            const int hc = hist_count(li);
+            if (hc > 0) {
+              if (!hist_stream) continue;  // among the history items below
+              x = penalize(x, hc, P);
+            }
+            const float v = temper(x, P);
             if (v == v) add_back(mkkey(v, static_cast<uint32_t>(li) + goff), held);
           }
         }
       }
       if (bad) {
         // this thread's items of the history round (item it: tid, tid + NT, ...)
-        for (int it = tid; it < head + tail + (hist_on ? A.hts : 0); it += NT) {
+        for (int it = tid; it < head + tail + ((hist_on && !hist_stream) ? A.hts : 0); it += NT) {
           int li, cnt = 0;
           if (it < head) {
             li = a + it;

@@ -229,3 +229,19 @@ def test_penalised_maximum_gives_way(cuda, pz, oracle_lib):
             assert (g["tokens"] == tok).all(), (dtype, temp, k)
             mism, _, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
             assert mism == 0, (dtype, temp, k)
+
+
+def test_penalties_that_raise_values(cuda, pz, oracle_lib):
+    """rep < 1 and a negative presence penalty raise history logits (the
+    history ids are then scored in their own round, not in the stream);
+    rep >= 1 with non-negative freq/pres lower them (scored in the stream)."""
+    for seed, cfg in [(91, dict(temperature=0.8, top_k=40, top_p=0.9, rep=0.7, freq=0.0, pres=-1.5)),
+                      (92, dict(temperature=0.8, top_k=50, top_p=1.0, rep=1.0, freq=-0.4, pres=0.0)),
+                      (93, dict(temperature=0.8, top_k=50, top_p=0.9, rep=1.3, freq=0.5, pres=0.2))]:
+        for dtype in ("f32", "bf16"):
+            spec = dict(seed=seed, B=64, V=50000, sd=2.0, boosts=[8, 3.0, 6.0], hist_len=400,
+                        dtype=dtype, cfg=cfg)
+            d = cases.build(spec)
+            g = run_gpu(cuda, pz, d, max_top_k=64, max_history=512)
+            mism, _, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+            assert mism == 0, (seed, dtype)
