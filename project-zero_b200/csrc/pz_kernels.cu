@@ -1010,7 +1010,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
               x = penalize(x, hc, P);
             }
           }
-          const float v = temper(x, P);
+          const float v = mulT ? __fmul_rn(x, scale) : __fdiv_rn(x, P.T);
           const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
           if (key > qk[kTQ - 1]) {
             q_insert(key);
@@ -1030,7 +1030,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       if (i == refresh_at) {
         // the k-th largest of the threads' best values: k distinct elements
         // are at or above it; maxima only grow, so stale entries keep it valid
-        const uint32_t bnd = kth_of_maxima(s_maxv, k_sel, 32);
+        const uint32_t bnd = kth_of_maxima(s_maxv, k_sel, 16);
         if (lane == 0) atomicMax(&s_tauv, bnd);
       }
       // this lane has read its vectors of the slot (every value fed the
