@@ -367,7 +367,15 @@ constexpr int kSliceWarps = kSliceThreads / 32;
 constexpr int kLaneVecs = kChunkBytes / 16 / 32;  // 16-byte vectors per lane per chunk
 constexpr uint32_t kHashEmpty = 0xFFFFFFFFu;
 constexpr uint32_t kOrdNegInf = 0x007FFFFFu;      // f2ord(-inf)
-static_assert(kLaneVecs == 4, "the chunk loop is written for four vectors per lane");
+static_assert(kLaneVecs == 2 || kLaneVecs == 4, "two or four vectors per lane per chunk");
+
+template <int R>
+__device__ __forceinline__ float max_of(const float (&v)[R]) {
+  float m = v[0];
+#pragma unroll
+  for (int r = 1; r < R; r++) m = fmaxf(m, v[r]);
+  return m;
+}
 
 // Open-addressing table of the slice's history ids with their counts.  The
 // table has at least twice as many slots as ids, so probes end.
@@ -550,10 +558,8 @@ __device__ __noinline__ uint32_t kth_of_maxima(const uint32_t *s_maxv, int k, in
   for (int r = 0; r < kSliceWarps; r++) v[r] = *reinterpret_cast<const volatile uint32_t *>(&s_maxv[r * 32 + lane]);
   return warp_kth_u32<kSliceWarps>(v, k, bits);
 }
-__device__ __noinline__ uint32_t kth_of_4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, int k,
-                                          int bits) {
-  const uint32_t v[4] = {a, b, c, d};
-  return warp_kth_u32<4>(v, k, bits);
+__device__ __noinline__ uint32_t kth_of_lane_vecs(const uint32_t (&v)[kLaneVecs], int k, int bits) {
+  return warp_kth_u32<kLaneVecs>(v, k, bits);
 }
 
 constexpr int kTQ = 4;          // keys kept per thread in registers
@@ -941,7 +947,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
         q[u] = *reinterpret_cast<const uint4 *>(lsb + u * 512);
         mv[u] = LaneVec<T>::vmax(q[u]);
       }
-      const float m = fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3]));
+      const float m = max_of(mv);
       const int e0 = a_al + (warp + NW * i) * (kChunkBytes / static_cast<int>(sizeof(T)));
       if (i == 0) {
         // A first bound from the first chunk of every warp: each of the np
@@ -966,7 +972,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
           }
         }
         const int np = min(NW, nchunks);
-        const uint32_t bj = kth_of_4(vm[0], vm[1], vm[2], vm[3], (k_sel + np - 1) / np, 32);
+        const uint32_t bj = kth_of_lane_vecs(vm, (k_sel + np - 1) / np, 32);
         if (lane == 0) atomicMin(&s_b0, bj);
         named_bar_sync(1, np * 32);  // the warps with chunks (warps 0 .. np-1)
         const uint32_t b0 = *reinterpret_cast<volatile uint32_t *>(&s_b0);
@@ -1063,7 +1069,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
         q[u] = *reinterpret_cast<const uint4 *>(lsb + u * 512);
         mv[u] = LaneVec<T>::vmax(q[u]);
       }
-      const float m = fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3]));
+      const float m = max_of(mv);
       const bool hot = mulT ? !(__fmul_rn(m, scale) < tau_wf) : !(m < rthr);
       if (__any_sync(0xFFFFFFFFu, hot)) {
         const int e0 = a_al + (warp + NW * i) * (kChunkBytes / static_cast<int>(sizeof(T)));
@@ -1125,7 +1131,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       const int cv = mine ? kChunkBytes / 16 : 0;  // a short last chunk is NaN-filled
       const int e0 = a_al + c * (kChunkBytes / static_cast<int>(sizeof(T)));
 #pragma unroll
-      for (int h = 0; h < 2; h++) {
+      for (int h = 0; h < kLaneVecs / 2; h++) {
         float xv[HPT];
 #pragma unroll
         for (int uu = 0; uu < 2; uu++) {
