@@ -262,10 +262,10 @@ pz_status pz_sample_batch_static(const void *logits, pz_dtype dtype, int B,
  * slots of CUDA events (n = 0 turns timing off); while on, each of the next
  * n sampling calls on the context records events around its kernels on the
  * call's stream.  pz_ctx_profile_read waits for the recorded calls and
- * returns the summed milliseconds of the streaming kernel (slice_kernel) and
- * of the rest of each call (the row finaliser and any full-vocabulary
- * pass), the number of calls timed and the number of kernels they
- * launched; it then starts a new count. */
+ * returns the summed milliseconds of the streaming kernel (slice_kernel,
+ * which also decides the rows) and of the rest of each call (the
+ * full-vocabulary pass, when a row needs one), the number of calls timed
+ * and the number of kernels they launched; it then starts a new count. */
 pz_status pz_ctx_profile(pz_sampler_ctx *ctx, int n_calls);
 pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms,
                               double *rest_ms, int *calls, int *kernels);

@@ -244,31 +244,49 @@ void pz_row_shard(int B, int world, int rank, int *begin, int *count) {
   if (count) *count = base + (rank < rem ? 1 : 0);
 }
 
-// Slices per row: just enough CTAs to fill the GPU once at the kernel's
-// occupancy (every slice pays a setup and an end-of-slice merge, and with
-// one slice per row the row is decided inside slice_kernel), slices of at
-// least 2048 columns, B*S within the context's scratch, and S lists of the
-// launch's list length fitting the finalizer's merge area (4096 keys).
+// How rows are cut into CTAs.  With at least as many rows as the GPU has
+// CTA slots (SMs x CTAs per SM at the kernel's occupancy), one CTA per row,
+// and the CTA decides its row.  With fewer rows, every row is split into S
+// slices, just enough to fill the slots once: every slice pays a setup and
+// an end-of-slice merge, and the last of a row's slices to finish merges
+// the S lists and decides the row.  Launches of argmax rows only (list
+// length 1) also split the rows of their last, partial wave (rows B1 on),
+// so that this wave fills the GPU too; for list rows that was measured
+// slower (a slice's short stream reaches a tight bound too late).  Slices
+// of at least 2048 columns, the split rows' lists within the context's
+// scratch, and S lists of the launch's list length within the merge area
+// (4096 keys).
 static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
-                          size_t smem, int *S_out, int *L_out) {
+                          size_t smem, int *B1_out, int *S_out, int *L_out) {
   const size_t per_sm = 228 * 1024;
   int occ = static_cast<int>(per_sm / (smem + 2048));
   occ = std::max(1, std::min(occ, 3));
   const int slots = c->num_sms * occ;
-  int S = (slots + B - 1) / B;
-  // PZ_SLICES_PER_ROW: tuning override of the slice count
+  int B1 = 0, S = 1;
+  if (B < slots) {
+    S = (slots + B - 1) / B;
+  } else if (kcap == 1 && B % slots != 0) {
+    B1 = B / slots * slots;
+    S = slots / (B - B1);
+  }
+  // PZ_SLICES_PER_ROW: tuning override (every row in this many slices)
   static const int forced = [] {
     const char *e = std::getenv("PZ_SLICES_PER_ROW");
     return e ? std::atoi(e) : 0;
   }();
-  if (forced > 0) S = forced;
+  if (forced > 0) {
+    B1 = 0;
+    S = forced;
+  }
   S = std::min(S, std::max(1, (V + 2047) / 2048));
-  S = std::min(S, std::max(1, c->slices_cap / std::max(B, 1)));
+  S = std::min(S, std::max(1, c->slices_cap / std::max(B - B1, 1)));
   S = std::min(S, std::max(1, 4096 / std::max(kcap, 1)));
   S = std::max(S, 1);
   int L = (V + S - 1) / S;
   L = (L + 7) / 8 * 8;
   S = (V + L - 1) / L;
+  if (S == 1) B1 = B;
+  *B1_out = B1;
   *S_out = S;
   *L_out = L;
 }
@@ -340,7 +358,7 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   }
   a.nstages = pz::slice_stages(a.kcap, a.hts);
   const size_t smem = pz::slice_smem_bytes(a.kcap, a.hts, a.nstages, a.V);
-  choose_slices(ctx, B, V, a.kcap, smem, &a.S, &a.L);
+  choose_slices(ctx, B, V, a.kcap, smem, &a.B1, &a.S, &a.L);
   if (smem > static_cast<size_t>(pz::max_dynamic_smem())) return fail(PZ_ERR_UNSUPPORTED);
   const bool full_pass = !emit && !no_full;
   if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t), st) != cudaSuccess)
@@ -354,12 +372,7 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   cudaError_t ce = pz::launch_slice(a, dtype, smem, st);
   if (ce != cudaSuccess) return fail_cuda(ce);
   if (ev) cudaEventRecord(ev[1], st);
-  int kernels = 1;
-  if (a.S > 1) {  // with one slice per row, slice_kernel decides the rows itself
-    ce = pz::launch_finalize(a, st);
-    if (ce != cudaSuccess) return fail_cuda(ce);
-    kernels++;
-  }
+  int kernels = 1;  // slice_kernel decides every row itself
   if (full_pass) {
     FullArgs f{};
     f.logits = logits;
@@ -410,14 +423,16 @@ pz_status pz_sample_batch(pz_sampler_ctx *ctx, const void *logits,
 // pz_sample_batch_static: the batched sampler with its scratch carved out of
 // one fixed device array (per device, zero at module load) instead of a
 // context's allocations.  Layout (bytes):
-//   slice lists  kStaticSlices x PZ_STATIC_MAX_TOP_K u64   (B*S <= kStaticSlices)
+//   slice lists  kStaticSlices x PZ_STATIC_MAX_TOP_K u64   (split rows x S <= kStaticSlices)
 //   slice counts kStaticSlices int32
 //   row words    row_tau, row_best (u64), row_arrive, row_flags, full_rows
 //                (32-bit), PZ_STATIC_MAX_BATCH each, then the n_full counter.
 // Every word this path reads is written earlier in the same call (slice
-// counts and lists by every slice CTA, row flags by slice 0), so nothing has
-// to be cleared between calls; the full-vocabulary counter, the one word that
-// must start at zero, is never touched because such rows are refused.
+// counts and lists by every slice CTA, row flags by slice 0), except the
+// split rows' arrival counters, which start at zero with the array and are
+// put back to zero by each row's last slice; the full-vocabulary counter,
+// which must also start at zero, is never touched because such rows are
+// refused.
 // ---------------------------------------------------------------------------
 namespace {
 

@@ -1,13 +1,14 @@
 // pz_kernels.cu — sm_100a kernels of the token sampler.
 //
-//   slice_kernel  one streaming pass over every row, split into S slices of
-//                 L columns (one CTA each): 128-bit loads, penalties
-//                 (shared-memory history bitmap + sorted id counts),
-//                 temperature, and the slice's top-k (or argmax) as 64-bit
-//                 ordered keys.  The last CTA of a row to finish (counted
-//                 with an atomic, no waiting) merges the S lists into the
-//                 exact top-k and runs the reference's list arithmetic
-//                 (top_p.c:37-105 or top_k.c:50-72) to draw the token.
+//   slice_kernel  one streaming pass over every row, one CTA per row (the
+//                 rows of the GPU's last, partial wave split into S slices
+//                 of L columns, one CTA each): 16-byte copies, penalties
+//                 (shared-memory history table and bitmap), temperature,
+//                 and the top-k (or argmax) as 64-bit ordered keys.  The
+//                 row's CTA, or the last of its slices to finish (counted
+//                 with an atomic, no waiting, merging the S lists), runs the
+//                 reference's list arithmetic (top_p.c:37-105 or
+//                 top_k.c:50-72) to draw the token.
 //   full_kernel   rows with no top-k list (k = 0): the exact sequential
 //                 replay (pz_seqsum.cuh) of sample_top_p's normaliser,
 //                 stable sort and CDF (top_p.c:53-105), or of the softmax
@@ -565,6 +566,84 @@ __device__ __noinline__ uint32_t kth_of_lane_vecs(const uint32_t (&v)[kLaneVecs]
 constexpr int kTQ = 4;          // keys kept per thread in registers
 constexpr int kTQK = 64;        // lists up to this long use the register queues
 
+// After the stream the ring holds the row's list (the survivors, or a split
+// row's merged slice lists: up to kMergeKeys keys) and, from kFinalizeOff on,
+// the decision's scratch (values, probabilities, order: 12 bytes a key).
+constexpr int kMergeKeys = 4096;
+constexpr int kFinalizeOff = kMergeKeys * 8;
+static_assert(kSliceWarps * kSlots * kChunkBytes >= kFinalizeOff + 12 * PZ_TOP_K_MAX + 16,
+              "the ring holds the merged lists and the decision's scratch");
+
+// A split row's S slice lists (written to scratch by its S CTAs), merged
+// by one warp into `lst`: for list rows the k_sel best keys in descending
+// order, zero-padded to kcap; for argmax rows and k == 1 the best key, in
+// gbest (and in lst[0] for top-k rows).  A slice that timed out marks the row.
+struct MergedList {
+  unsigned long long gbest;
+  int n_sel;
+  int timed_out;
+};
+__device__ __forceinline__ MergedList merge_slice_lists(const SliceArgs &A, int row, bool topk, int k_sel,
+                                                     unsigned long long tau0,
+                                                     unsigned long long *lst) {
+  const int lane = threadIdx.x & 31;
+  const int S = A.S;
+  const size_t s0 = static_cast<size_t>(row - A.B1) * S;
+  const unsigned long long *sk = A.slice_keys + s0 * static_cast<size_t>(A.kcap);
+  const int32_t *sc = A.slice_cnt + s0;
+  bool to = false;
+  int n_sel = 0;
+  unsigned long long gbest = 0ull;
+  if (topk && k_sel > 1) {
+    int n = 0;
+    for (int s2 = 0; s2 < S; s2++) {
+      const int raw = __ldcg(sc + s2);
+      to |= ((raw >> 30) & 1) != 0;
+      const int c = raw & 0xFFFF;
+      for (int i = lane; i < c; i += 32) lst[n + i] = __ldcg(sk + static_cast<size_t>(s2) * A.kcap + i);
+      n += c;
+    }
+    __syncwarp();
+    if (n > k_sel) {
+      const unsigned long long kth = warp_kth(lst, n, k_sel);
+      n = warp_compact_ge(lst, n, kth);
+    }
+    n_sel = n;
+    if (A.kcap <= 64) {
+      warp_rank_sort_desc(lst, n_sel);
+      for (int i = n_sel + lane; i < A.kcap; i += 32) lst[i] = 0ull;
+      __syncwarp();
+    } else {
+      for (int i = n_sel + lane; i < A.kcap; i += 32) lst[i] = 0ull;
+      warp_sort_desc(lst, A.kcap);
+    }
+  } else {
+    unsigned long long bl = 0ull;
+    bool lto = false;
+    for (int s2 = lane; s2 < S; s2 += 32) {
+      const int raw = __ldcg(sc + s2);
+      lto |= ((raw >> 30) & 1) != 0;
+      if ((raw & 0xFFFF) > 0) {
+        const unsigned long long k = __ldcg(sk + static_cast<size_t>(s2) * A.kcap);
+        bl = k > bl ? k : bl;
+      }
+    }
+    to |= __any_sync(0xFFFFFFFFu, lto);
+    gbest = warp_max_u64(bl);
+    if (topk) {  // k_eff == 1 (or a rejected list length): the single best admitted key
+      n_sel = gbest > tau0 ? 1 : 0;
+      if (lane == 0) lst[0] = gbest;
+      for (int i = 1 + lane; i < A.kcap; i += 32) lst[i] = 0ull;
+      __syncwarp();
+    }
+  }
+  MergedList r;
+  r.gbest = gbest;
+  r.n_sel = n_sel;
+  r.timed_out = to ? 1 : 0;
+  return r;
+}
+
 // Shared memory of slice_kernel:
 //   ring   NW x nslots x kChunkBytes  (per-warp copy rings; after the
 //          stream: the queues' survivors and the rare exact rescan)
@@ -623,9 +702,13 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
-  const int row = blockIdx.y, sl = blockIdx.x;
-  const int a = sl * A.L;
-  const int b = min(A.V, a + A.L);
+  // CTA u < B1 takes all of row u; the rows after B1 come in S slices of L
+  // columns each (the last CTAs launched, filling the GPU's final wave)
+  const int u = blockIdx.x;
+  const bool split = u >= A.B1;
+  const int row = split ? A.B1 + (u - A.B1) / A.S : u;
+  const int a = split ? (u - A.B1) % A.S * A.L : 0;
+  const int b = split ? min(A.V, a + A.L) : A.V;
 
   constexpr int NS = kSlots;
   unsigned char *ring = smem;
@@ -1389,17 +1472,19 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   }
   if (warp != 0) return;
 
-  if (A.S == 1) {
-    // The row's only slice: decide the row here.  The list is already in
-    // order (rank merge) except on the block-buffer paths; the list
-    // arithmetic's scratch sits in the ring after the first 16 KB.
-    float *fe = reinterpret_cast<float *>(ring + 16384);
-    float *fp = fe + A.kcap;
-    int *ford = reinterpret_cast<int *>(fp + A.kcap);
-    int *s_tokp = ford + A.kcap;
-    unsigned long long *fl = lst;
-    int n_sel = 0;
-    unsigned long long gbest = 0ull;
+  // The row's list for the decision: this CTA's own (the whole row), or,
+  // for a split row, the merge of its S slice lists by whichever of its
+  // CTAs finishes last.  The decision's scratch sits in the ring after the
+  // first 32 KB (the survivors or the merged lists).
+  float *fe = reinterpret_cast<float *>(ring + kFinalizeOff);
+  float *fp = fe + A.kcap;
+  int *ford = reinterpret_cast<int *>(fp + A.kcap);
+  int *s_tokp = ford + A.kcap;
+  unsigned long long *fl = lst;
+  int n_sel = 0;
+  unsigned long long gbest = 0ull;
+  bool row_timed_out = timed_out, x0nan = s_x0nan != 0;
+  if (blockIdx.x < static_cast<unsigned>(A.B1)) {
     if (use_block || exact_rescan) {
       fl = rb;
       n_sel = s_n;
@@ -1420,122 +1505,48 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
         __syncwarp();
       }
     }
-    finalize_row(A, row, P, bad_k, too_long, timed_out, s_x0nan != 0, fl, n_sel, gbest, fe, fp, ford,
-                 s_tokp);
-    return;
-  }
-
-  int m = 0;
-  unsigned long long *dst =
-      A.slice_keys + (static_cast<size_t>(row) * A.S + sl) * static_cast<size_t>(A.kcap);
-  if (use_block || exact_rescan) {
-    m = s_n;
-    for (int i = lane; i < m; i += 32) dst[i] = rb[i];
-  } else if (use_tq) {
-    m = n_tq;
-    for (int i = lane; i < m; i += 32) dst[i] = lst[i];
   } else {
-    unsigned long long bl = lane < NW ? s_red[lane] : 0ull;
-    bl = warp_max_u64(bl);
-    m = bl > tau0 ? 1 : 0;
-    if (lane == 0 && m) dst[0] = bl;
-  }
-  if (lane == 0) {
-    A.slice_cnt[static_cast<size_t>(row) * A.S + sl] = m | (timed_out ? (1 << 30) : 0);
-    if (a == 0) A.row_flags[row] = s_x0nan ? 1u : 0u;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// finalize_kernel: one warp per row merges the row's slice lists into the
-// exact top-k (or argmax) and draws (reference list arithmetic), hands
-// full-vocabulary rows to full_kernel, or publishes the list (vocab
-// sharding).  Runs after slice_kernel on the same stream.
-// ---------------------------------------------------------------------------
-__host__ __device__ size_t finalize_smem_per_warp(int S, int kcap) {
-  const int merge = S * kcap > kcap ? S * kcap : kcap;
-  const size_t bytes = sizeof(unsigned long long) * static_cast<size_t>(merge) +
-                       (sizeof(float) * 2 + sizeof(int)) * static_cast<size_t>(kcap) + 16;
-  return (bytes + 15) / 16 * 16;  // each warp's region starts 16-byte aligned
-}
-
-__global__ void __launch_bounds__(128) finalize_kernel(const SliceArgs A, int warps_per_cta) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int row = blockIdx.x * warps_per_cta + warp;
-  if (row >= A.B) return;
-  const size_t per_warp = finalize_smem_per_warp(A.S, A.kcap);
-  unsigned char *base = smem + per_warp * warp;
-  const int merge_keys = A.S * A.kcap > A.kcap ? A.S * A.kcap : A.kcap;
-  unsigned long long *ring_keys = reinterpret_cast<unsigned long long *>(base);
-  float *fe = reinterpret_cast<float *>(ring_keys + merge_keys);
-  float *fp = fe + A.kcap;
-  int *ford = reinterpret_cast<int *>(fp + A.kcap);
-  int *s_tokp = ford + A.kcap;
-
-  const pz_sampler_config cfg = A.cfg[row];
-  const RowPlan P = plan_row(cfg, A.V_global);
-  const bool bad_k = P.mode == kModeTopK && (P.keff > A.kmax || P.keff > A.kcap);
-  const int k_sel = (P.mode == kModeTopK && !bad_k) ? P.keff : 1;
-  const unsigned long long tau0 = (P.mode == kModeTopK) ? key_topk_floor() : 0ull;
-  int H = 0;
-  if (A.hist != nullptr && A.hist_off != nullptr && P.pen_on) H = A.hist_off[row + 1] - A.hist_off[row];
-  const bool too_long = H > A.hcap;
-  const bool timed_out = false;
-  const int S = A.S;
-  const unsigned long long *sk = A.slice_keys + static_cast<size_t>(row) * S * static_cast<size_t>(A.kcap);
-  const int32_t *sc = A.slice_cnt + static_cast<size_t>(row) * S;
-  bool row_timed_out = timed_out;
-  int n_sel = 0;
-  unsigned long long gbest = 0ull;
-  unsigned long long *lst = ring_keys;  // merged list, sorted below
-  if (P.mode == kModeTopK && !bad_k && k_sel > 1) {
-    int n = 0;
-    for (int s2 = 0; s2 < S; s2++) {
-      const int raw = __ldcg(sc + s2);
-      row_timed_out |= ((raw >> 30) & 1) != 0;
-      const int c = raw & 0xFFFF;
-      for (int i = lane; i < c; i += 32) lst[n + i] = __ldcg(sk + static_cast<size_t>(s2) * A.kcap + i);
-      n += c;
-    }
-    __syncwarp();
-    if (n > k_sel) {
-      const unsigned long long kth = warp_kth(lst, n, k_sel);
-      n = warp_compact_ge(lst, n, kth);
-    }
-    n_sel = n;
-    if (A.kcap <= 64) {
-      warp_rank_sort_desc(lst, n_sel);
-      for (int i = n_sel + lane; i < A.kcap; i += 32) lst[i] = 0ull;
-      __syncwarp();
+    int m = 0;
+    const size_t si = static_cast<size_t>(blockIdx.x) - A.B1;  // (row - B1) * S + slice
+    unsigned long long *dst = A.slice_keys + si * static_cast<size_t>(A.kcap);
+    if (use_block || exact_rescan) {
+      m = s_n;
+      for (int i = lane; i < m; i += 32) dst[i] = rb[i];
+    } else if (use_tq) {
+      m = n_tq;
+      for (int i = lane; i < m; i += 32) dst[i] = lst[i];
     } else {
-      for (int i = n_sel + lane; i < A.kcap; i += 32) lst[i] = 0ull;
-      warp_sort_desc(lst, A.kcap);
+      unsigned long long bl = lane < NW ? s_red[lane] : 0ull;
+      bl = warp_max_u64(bl);
+      m = bl > tau0 ? 1 : 0;
+      if (lane == 0 && m) dst[0] = bl;
     }
-  } else {
-    unsigned long long bl = 0ull;
-    for (int s2 = lane; s2 < S; s2 += 32) {
-      const int raw = __ldcg(sc + s2);
-      if ((raw >> 30) & 1) bl = ~0ull;  // marker below
-      if ((raw & 0xFFFF) > 0) {
-        const unsigned long long k = __ldcg(sk + static_cast<size_t>(s2) * A.kcap);
-        if (bl != ~0ull) bl = k > bl ? k : bl;
-      }
+    if (lane == 0) {
+      A.slice_cnt[si] = m | (timed_out ? (1 << 30) : 0);
+      if (a == 0) A.row_flags[row] = s_x0nan ? 1u : 0u;
     }
-    const bool any_to = __any_sync(0xFFFFFFFFu, bl == ~0ull);
-    row_timed_out |= any_to;
-    if (bl == ~0ull) bl = 0ull;
-    gbest = warp_max_u64(bl);
-    if (P.mode == kModeTopK) {  // k_eff == 1: the single best admitted key
-      n_sel = gbest > tau0 ? 1 : 0;
-      if (lane == 0) lst[0] = gbest;
-      for (int i = 1 + lane; i < A.kcap; i += 32) lst[i] = 0ull;
-      __syncwarp();
+    // publish the list, then take a ticket: the row's S-th arrival decides
+    __threadfence();
+    __syncwarp();
+    unsigned last = 0u;
+    if (lane == 0) {
+      last = atomicAdd(A.row_arrive + row, 1u) == static_cast<unsigned>(A.S - 1) ? 1u : 0u;
+      if (last) A.row_arrive[row] = 0u;  // ready for the next launch
     }
+    last = __shfl_sync(0xFFFFFFFFu, last, 0);
+    if (!last) return;
+    __threadfence();
+    fl = reinterpret_cast<unsigned long long *>(ring);
+    const MergedList ml = merge_slice_lists(A, row, P.mode == kModeTopK, k_sel, tau0, fl);
+    n_sel = ml.n_sel;
+    gbest = ml.gbest;
+    row_timed_out |= ml.timed_out != 0;
+    x0nan = (__ldcg(A.row_flags + row) & 1u) != 0u;
   }
-  const bool x0nan = (__ldcg(A.row_flags + row) & 1u) != 0u;
-  finalize_row(A, row, P, bad_k, too_long, row_timed_out, x0nan, lst, n_sel, gbest, fe, fp, ford, s_tokp);
+  finalize_row(A, row, P, bad_k, too_long, row_timed_out, x0nan, fl, n_sel, gbest, fe, fp, ford,
+               s_tokp);
 }
+
 
 // ---------------------------------------------------------------------------
 // full_kernel: rows that need the whole row's distribution.
@@ -1921,14 +1932,13 @@ cudaError_t set_kernel_attributes() {
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(full_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   return e;
 }
 
 cudaError_t launch_slice(const SliceArgs &a, int dtype, size_t smem, cudaStream_t st) {
-  const dim3 grid(a.S, a.B);
+  // rows [0, B1) one CTA each, then S CTAs for each later row
+  const unsigned grid = static_cast<unsigned>(a.B1) + static_cast<unsigned>(a.B - a.B1) * a.S;
   if (dtype == PZ_DTYPE_F32)
     slice_kernel<float><<<grid, kSliceThreads, smem, st>>>(a);
   else
@@ -1941,14 +1951,6 @@ cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem, cud
     full_kernel<float><<<grid, kFullThreads, smem, st>>>(a);
   else
     full_kernel<uint16_t><<<grid, kFullThreads, smem, st>>>(a);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_finalize(const SliceArgs &a, cudaStream_t st) {
-  const size_t per_warp = finalize_smem_per_warp(a.S, a.kcap);
-  int w = 4;
-  while (w > 1 && per_warp * w > 96 * 1024) w >>= 1;
-  finalize_kernel<<<(a.B + w - 1) / w, 32 * w, per_warp * w, st>>>(a, w);
   return cudaGetLastError();
 }
 

@@ -32,8 +32,9 @@ struct SliceArgs {
   const pz_sampler_config *cfg;
   const int32_t *hist;
   const int32_t *hist_off;
-  int S;                // CTAs per row
-  int L;                // columns per CTA (multiple of 8)
+  int B1;               // rows [0, B1) are read by one CTA each
+  int S;                // CTAs per row for the rows after B1 (split rows)
+  int L;                // columns per CTA of a split row (multiple of 8)
   int kcap;             // power of two >= largest k_eff in the launch
   int kmax;             // declared largest k_eff (rows above it are rejected)
   int hcap;             // longest history a row may have (0: no history)
@@ -43,9 +44,9 @@ struct SliceArgs {
   int mode_emit;        // 1: write the merged local list (vocab sharding), no draw
   int no_full_vocab;
   // scratch
-  unsigned long long *slice_keys;  // [B*S][kcap]
-  int32_t *slice_cnt;              // [B*S]
-  uint32_t *row_arrive;            // [B]
+  unsigned long long *slice_keys;  // [(B-B1)*S][kcap] split rows' slice lists
+  int32_t *slice_cnt;              // [(B-B1)*S]
+  uint32_t *row_arrive;            // [B] slices of a split row done (0 between calls)
   uint32_t *row_flags;             // [B]
   unsigned long long *row_tau;     // [B] shared list threshold (0 between calls)
   unsigned long long *row_best;    // [B]
@@ -104,8 +105,6 @@ cudaError_t launch_slice(const SliceArgs &a, int dtype, size_t smem,
                          cudaStream_t st);
 size_t slice_smem_bytes(int kcap, int hts, int nstages, int V);
 int slice_stages(int kcap, int hts);
-cudaError_t launch_finalize(const SliceArgs &a, cudaStream_t st);
-__host__ __device__ size_t finalize_smem_per_warp(int S, int kcap);
 cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem,
                         cudaStream_t st);
 size_t full_smem_bytes(int V, int hcap);

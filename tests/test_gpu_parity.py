@@ -245,3 +245,30 @@ def test_penalties_that_raise_values(cuda, pz, oracle_lib):
             g = run_gpu(cuda, pz, d, max_top_k=64, max_history=512)
             mism, _, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
             assert mism == 0, (seed, dtype)
+
+
+@pytest.mark.parametrize("B", [148 + 21, 296 + 30, 444 + 30, 444 + 3])
+def test_last_wave_rows_split(cuda, pz, oracle_lib, B):
+    """Batches on either side of the GPU's CTA slots (148 SMs x 2 or 3 CTAs):
+    below, every row is split over several CTAs and decided by the slice
+    that finishes last; above, one CTA per row, except that argmax-only
+    launches split the rows of their last, partial wave.  Mixed settings
+    (greedy, top-k, top-p, k = 1024, history) cover every kind of row; a
+    second call checks that the arrival counters start again."""
+    spec = dict(seed=91 + B, B=B, V=50000, sd=2.0, zipf=[64, 6.0], cfg="hetero")
+    d = cases.build(spec)
+    s = pz.Sampler(0, max_batch=B, max_vocab=50000, max_top_k=1024, max_history=2048)
+    g = run_gpu(cuda, pz, d, sampler=s)
+    mism, n, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+    assert mism <= 1, (B, mism)
+    again = run_gpu(cuda, pz, d, sampler=s)
+    assert (again["tokens"] == g["tokens"]).all() and (again["rng"] == g["rng"]).all()
+    spec = dict(seed=92 + B, B=B, V=50000, sd=2.0, boosts=[8, 3.0, 6.0], hist_len=200,
+                cfg=dict(temperature=0.0, rep=1.3))
+    d = cases.build(spec)
+    g = run_gpu(cuda, pz, d, sampler=s, max_top_k=1, max_history=256)
+    mism, n, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+    assert mism == 0, (B, mism)
+    again = run_gpu(cuda, pz, d, sampler=s, max_top_k=1, max_history=256)
+    assert (again["tokens"] == g["tokens"]).all()
+    s.close()
