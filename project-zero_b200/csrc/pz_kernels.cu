@@ -1284,12 +1284,13 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   int n_tq = 0;  // list length (queue path)
   if (use_tq) {
     // keys whose value is at or above the k-th largest thread maximum (at
-    // least k_sel of them), then the best k_sel of those
+    // least k_sel of them; resolved to 16 bits, which can only lower it and
+    // admit a few more), then the best k_sel of those
     if (warp == 0) {
       uint32_t v8[NW];
 #pragma unroll
       for (int r = 0; r < NW; r++) v8[r] = s_maxv[r * 32 + lane];
-      const uint32_t bw = warp_kth_u32<NW>(v8, k_sel, 32);
+      const uint32_t bw = warp_kth_u32<NW>(v8, k_sel, 16);
       if (lane == 0) s_b0 = bw;
     }
     __syncthreads();
