@@ -357,7 +357,8 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     a.cand_stride = outputs->cand_stride;
   }
   a.nstages = pz::slice_stages(a.kcap, a.hts);
-  const size_t smem = pz::slice_smem_bytes(a.kcap, a.hts, a.nstages, a.V);
+  const size_t smem =
+      pz::slice_smem_bytes(a.kcap, a.hts, a.nstages, a.V, dtype == PZ_DTYPE_BF16 ? 2 : 4);
   choose_slices(ctx, B, V, a.kcap, smem, &a.B1, &a.S, &a.L);
   if (smem > static_cast<size_t>(pz::max_dynamic_smem())) return fail(PZ_ERR_UNSUPPORTED);
   const bool full_pass = !emit && !no_full;

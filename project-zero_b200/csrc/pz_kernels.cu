@@ -475,59 +475,8 @@ struct LaneVec<uint16_t> {
   }
 };
 
-// A value v_b with at least k of the warp's 32*R values at or above it
-// (duplicates count): the k-th largest, resolved to `bits` bits below the
-// highest bit in which the values differ (fully resolved: exact).
-template <int R>
-__device__ __forceinline__ uint32_t warp_kth_u32(const uint32_t (&v)[R], int k, int bits) {
-  uint32_t lo = 0xFFFFFFFFu, hi = 0u;
-#pragma unroll
-  for (int r = 0; r < R; r++) {
-    lo = min(lo, v[r]);
-    hi = max(hi, v[r]);
-  }
-  lo = __reduce_min_sync(0xFFFFFFFFu, lo);
-  hi = __reduce_max_sync(0xFFFFFFFFu, hi);
-  if (lo == hi) return lo;
-  int b = 31 - __clz(static_cast<int>(lo ^ hi));
-  uint32_t mask = b == 31 ? 0u : (0xFFFFFFFFu << (b + 1));
-  uint32_t prefix = hi & mask;
-  int need = k;
-  const int stop = b - bits;
-  for (; b >= 0 && b > stop; b--) {
-    const uint32_t bit = 1u << b;
-    int cm = 0, c1 = 0;
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-      const bool m = (v[r] & mask) == prefix;
-      cm += m ? 1 : 0;
-      c1 += (m && (v[r] & bit)) ? 1 : 0;
-    }
-    cm = __reduce_add_sync(0xFFFFFFFFu, cm);
-    if (cm == need) break;  // every value under the prefix is in: the k-th is their minimum
-    c1 = __reduce_add_sync(0xFFFFFFFFu, c1);
-    if (c1 >= need) {
-      prefix |= bit;
-    } else {
-      need -= c1;
-    }
-    mask |= bit;
-  }
-  uint32_t m = 0xFFFFFFFFu;
-#pragma unroll
-  for (int r = 0; r < R; r++)
-    if ((v[r] & mask) == prefix) m = min(m, v[r]);
-  return __reduce_min_sync(0xFFFFFFFFu, m);
-}
-
 __device__ __forceinline__ void prefetch_l2(const void *p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-
-// Barrier `id` (not 0, which __syncthreads uses) over the first `count`
-// threads' warps; count a multiple of 32.
-__device__ __forceinline__ void named_bar_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // The float just below x (x > -inf).
@@ -551,20 +500,64 @@ __device__ __noinline__ float raw_floor(float t, const RowPlan P) {
   return -INFINITY;
 }
 
-// Out of line so the streaming loops stay short.
-__device__ __noinline__ uint32_t kth_of_maxima(const uint32_t *s_maxv, int k, int bits) {
-  const int lane = threadIdx.x & 31;
-  uint32_t v[kSliceWarps];
-#pragma unroll
-  for (int r = 0; r < kSliceWarps; r++) v[r] = *reinterpret_cast<const volatile uint32_t *>(&s_maxv[r * 32 + lane]);
-  return warp_kth_u32<kSliceWarps>(v, k, bits);
-}
-__device__ __noinline__ uint32_t kth_of_lane_vecs(const uint32_t (&v)[kLaneVecs], int k, int bits) {
-  return warp_kth_u32<kLaneVecs>(v, k, bits);
-}
+constexpr int kTQK = 64;        // lists up to this long use the sketch path
 
-constexpr int kTQ = 4;          // keys kept per thread in registers
-constexpr int kTQK = 64;        // lists up to this long use the register queues
+// The sketch of a list row's stream: for every chunk, the largest raw value
+// of each group of kSkGroupLanes lanes' vectors (64 f32 or 128 bf16
+// elements), kept as the top 16 bits of its ordered value (0: no value);
+// and one bit per group that holds a history id.  After the stream the
+// k-th largest sketch value bounds the list from below, and only the groups
+// whose maximum can reach the bound are read again.
+constexpr int kSkGroupLanes = 4;
+constexpr int kSkPerChunk = 32 / kSkGroupLanes;
+constexpr int kGCap = 1024;     // candidate groups
+constexpr int kCCap = 2048;     // candidate keys
+__host__ __device__ inline int slice_sketch_entries(int V, int elem_bytes, int kcap) {
+  if (kcap <= 1) return 0;
+  const long long nchunks = (static_cast<long long>(V) * elem_bytes + kChunkBytes - 1) / kChunkBytes + 1;
+  return static_cast<int>((nchunks * kSkPerChunk + 31) / 32 * 32);
+}
+__device__ __forceinline__ uint32_t sk16(float m) { return m == m ? f2ord(m) >> 16 : 0u; }
+
+// Warp 0: the bin of `bins` (256 counts, the highest bin first in rank)
+// holding the need-th largest value, and how many of that bin's values are
+// still needed; bin -1 if the bins hold fewer than `need` values.
+__device__ __noinline__ void radix_pick(const uint32_t *bins, int need, int *bin_out, int *rem_out) {
+  const int lane = threadIdx.x & 31;
+  uint32_t c[8], sum = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    c[j] = bins[lane * 8 + j];
+    sum += c[j];
+  }
+  uint32_t suf = sum;  // values in this lane's bins and above
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_down_sync(0xFFFFFFFFu, suf, o);
+    if (lane + o < 32) suf += t;
+  }
+  const uint32_t above = suf - sum;
+  const uint32_t n = static_cast<uint32_t>(need);
+  const uint32_t m = __ballot_sync(0xFFFFFFFFu, above < n && suf >= n);
+  if (m == 0u) {
+    if (lane == 0) {
+      *bin_out = -1;
+      *rem_out = 0;
+    }
+    return;
+  }
+  if (lane == __ffs(m) - 1) {
+    uint32_t acc = above;
+    for (int j = 7; j >= 0; j--) {
+      if (acc + c[j] >= n) {
+        *bin_out = lane * 8 + j;
+        *rem_out = static_cast<int>(n - acc);
+        break;
+      }
+      acc += c[j];
+    }
+  }
+}
 
 // After the stream the ring holds the row's list (the survivors, or a split
 // row's merged slice lists: up to kMergeKeys keys) and, from kFinalizeOff on,
@@ -650,6 +643,7 @@ __device__ __forceinline__ MergedList merge_slice_lists(const SliceArgs &A, int 
 //   cbuf   block buffer keys           (lists longer than kTQK only)
 //   hash   2 x hts words                (history ids and counts)
 //   hbm    V/128 words                  (one bit per 4 columns: a history id there)
+//   sketch 16-bit group maxima of the stream, then one bit per group (list rows)
 __host__ __device__ inline int slice_cbuf_keys(int kcap) {
   return kcap > kTQK ? kcap + kCapB : 0;
 }
@@ -658,10 +652,12 @@ __host__ __device__ inline int slice_hbm_words(int V, int hts) {
   return hts > 0 ? (V + 127) >> 7 : 0;
 }
 
-size_t slice_smem_bytes(int kcap, int hts, int nslots, int V) {
+size_t slice_smem_bytes(int kcap, int hts, int nslots, int V, int elem_bytes) {
+  const size_t sk = static_cast<size_t>(slice_sketch_entries(V, elem_bytes, kcap));
   return static_cast<size_t>(nslots) * kSliceWarps * kChunkBytes +
          sizeof(unsigned long long) * static_cast<size_t>(slice_cbuf_keys(kcap)) +
-         sizeof(uint32_t) * (2 * static_cast<size_t>(hts) + slice_hbm_words(V, hts));
+         sizeof(uint32_t) * (2 * static_cast<size_t>(hts) + slice_hbm_words(V, hts)) +
+         sizeof(uint16_t) * sk + sizeof(uint32_t) * (sk / 32);
 }
 
 // Ring slots per warp: kSlots chunks of 2 KB in flight per warp (48 KB per
@@ -692,12 +688,9 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ SelShared sh;
   __shared__ unsigned long long s_red[NW];
-  __shared__ uint32_t s_maxv[NT];       // ordered value of each thread's best key
   __shared__ uint32_t s_tauv;           // ordered value: the block's admission bound
-  __shared__ uint32_t s_b0;             // first bound, combined over the warps
   __shared__ RowPlan s_plan;
-  __shared__ unsigned long long s_dk;   // largest discarded key of the block
-  __shared__ unsigned long long s_dk2;  // the slice's k-th best key
+  __shared__ int s_sel[4];              // radix picks of the sketch bound
   __shared__ int s_x0nan, s_timeout, s_cnt, s_n;
 
   const int tid = threadIdx.x;
@@ -717,6 +710,9 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   uint32_t *hk = reinterpret_cast<uint32_t *>(cbuf + slice_cbuf_keys(A.kcap));
   uint32_t *hn = hk + A.hts;
   uint32_t *hbm = hn + A.hts;  // one bit per 4 columns of the row
+  uint16_t *sketch = reinterpret_cast<uint16_t *>(hbm + slice_hbm_words(A.V, A.hts));
+  const int sk_cap = slice_sketch_entries(A.V, static_cast<int>(sizeof(T)), A.kcap);
+  uint32_t *gbm = reinterpret_cast<uint32_t *>(sketch + sk_cap);  // one bit per sketch group
   const uint32_t hmask = static_cast<uint32_t>(A.hts - 1);
   const uint32_t hshift = static_cast<uint32_t>(A.hshift);
   const T *rowp = static_cast<const T *>(A.logits) + static_cast<size_t>(row) * static_cast<size_t>(A.ld);
@@ -780,11 +776,10 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   // a list longer than this launch was sized for (hint broken): flag the row
   const bool bad_k = P0.mode == kModeTopK && (P0.keff > A.kmax || P0.keff > A.kcap);
   const int k_sel = (P0.mode == kModeTopK && !bad_k) ? P0.keff : 1;
-  // lists up to kTQK long: per-thread register queues of the kTQ best keys,
-  // merged per CTA (exact unless a thread discarded a key that would have
-  // made the list, which is detected and redone); longer lists: one
+  // lists up to kTQK long: the stream keeps only the sketch, and the list
+  // comes from the groups that can reach its bound; longer lists: one
   // block-wide buffer.
-  const bool use_tq = k_sel > 1 && k_sel <= kTQK;
+  const bool use_tq = k_sel > 1 && k_sel <= kTQK && nchunks * kSkPerChunk <= sk_cap;
   const bool use_block = k_sel > kTQK;
   const unsigned long long tau0 = (P0.mode == kModeTopK) ? key_topk_floor() : 0ull;
   const float tau0_f = tau0 == 0ull ? -INFINITY : key_val(tau0);
@@ -798,8 +793,8 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   const bool hist_on = H > 0 && !too_long && A.hts > 0;
   // Penalties that can only lower a value (rep >= 1, freq >= 0, pres >= 0):
   // a history id whose raw value is below the bound stays below it, so list
-  // rows score history ids inside the stream with their penalised value
-  // (no separate round, no gathers).  Other penalties: the history round.
+  // rows score history ids among the read-again groups with their penalised
+  // value.  Other penalties: every history id in the history round.
   const bool pen_dec = P0.rep >= 1.0f && P0.freq >= 0.0f && P0.pres >= 0.0f;
   const bool hist_stream = hist_on && use_tq && pen_dec;
 
@@ -809,51 +804,72 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     s_timeout = 0;
     s_cnt = 0;
     s_tauv = f2ord(tau0_f);
-    s_b0 = 0xFFFFFFFFu;
-    s_dk = tau0;
     sh.n = 0;
     sh.tau = tau0;
   }
-  s_maxv[tid] = kOrdNegInf;
   __syncthreads();
   // The row plan from here on is read from shared memory: its fields are
   // used now and then, and would otherwise hold registers through the stream.
   const RowPlan &P = s_plan;
 
-  // ---- the slice's history ids and counts (while the first copies fly) ---
-  if (hist_on) {
+  // ---- the slice's history ids and counts ---------------------------------
+  // The first NT*IPT ids are loaded now, while the first copies fly.  Argmax
+  // and long-list rows build the table before the stream, which consults
+  // it; list rows after it, when the loads have long landed (their stream
+  // keeps only the sketch).
+  constexpr int IPT = 4;
+  int hid[IPT];
+#pragma unroll
+  for (int u = 0; u < IPT; u++) {
+    const int j = u * NT + tid;
+    hid[u] = hist_on && j < H ? static_cast<int>(static_cast<long long>(hrow[j]) - A.v_offset) : -1;
+  }
+  auto build_hist = [&]() {
     for (int i = tid; i < A.hts; i += NT) {
       hk[i] = kHashEmpty;
       hn[i] = 0u;
     }
     for (int i = tid; i < slice_hbm_words(A.V, A.hts); i += NT) hbm[i] = 0u;
-    // ids in batches (all loads of a batch in flight together); argmax rows
-    // take the history round right after this, so the logits the ids name
-    // are fetched into L2 now
-    constexpr int IPT = 4;
+    if (use_tq)
+      for (int i = tid; i < sk_cap / 32; i += NT) gbm[i] = 0u;
+    // argmax rows take the history round right after this, so the logits
+    // the ids name are fetched into L2 now
     const bool pre = !use_tq && !use_block;
+    if (pre) {
+#pragma unroll
+      for (int u = 0; u < IPT; u++)
+        if (hid[u] >= a && hid[u] < b) prefetch_l2(rowp + hid[u]);
+    }
+    __syncthreads();  // the table is initialised
     for (int base = 0; base < H; base += NT * IPT) {
-      long long t[IPT];
+      int t[IPT];
 #pragma unroll
       for (int u = 0; u < IPT; u++) {
         const int j = base + u * NT + tid;
-        t[u] = j < H ? static_cast<long long>(hrow[j]) - A.v_offset : -1;
+        t[u] = base == 0 ? hid[u] : (j < H ? static_cast<int>(static_cast<long long>(hrow[j]) - A.v_offset) : -1);
       }
-      if (pre) {
+      if (pre && base > 0) {
 #pragma unroll
         for (int u = 0; u < IPT; u++)
           if (t[u] >= a && t[u] < b) prefetch_l2(rowp + t[u]);
       }
-      if (base == 0) __syncthreads();  // the table is initialised
 #pragma unroll
       for (int u = 0; u < IPT; u++)
         if (t[u] >= a && t[u] < b) {
           hash_insert(hk, hn, hmask, hshift, static_cast<uint32_t>(t[u]));
           atomicOr(&hbm[t[u] >> 7], 1u << ((t[u] >> 2) & 31));
+          if (use_tq && t[u] >= a_al && t[u] < b_al) {
+            // the sketch group of column t: chunk, then the lane of its vector
+            constexpr int kPerChunk = kChunkBytes / static_cast<int>(sizeof(T));
+            const int off = t[u] - a_al;
+            const int g = (off / kPerChunk) * kSkPerChunk + (((off % kPerChunk) / VEC) & 31) / kSkGroupLanes;
+            atomicOr(&gbm[g >> 5], 1u << (g & 31));
+          }
         }
     }
     __syncthreads();
-  }
+  };
+  if (hist_on && !use_tq) build_hist();
   // the bitmap answers most lookups; a set bit sends the id to the table
   auto hist_count = [&](int li) -> int {
     return hist_on && ((hbm[li >> 7] >> ((li >> 2) & 31)) & 1u) != 0u
@@ -862,14 +878,6 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   };
   auto in_hist = [&](int li) -> bool { return hist_count(li) > 0; };
 
-  // register queue of this thread's best keys (descending), the largest key
-  // it discarded, and their values for the cheap float tests
-  unsigned long long qk[kTQ];
-#pragma unroll
-  for (int j = 0; j < kTQ; j++) qk[j] = tau0;
-  float q_lo = tau0_f;                  // value of qk[kTQ-1]
-  unsigned long long dk = tau0;         // largest discarded key
-  float dv = tau0_f;
   unsigned long long best = 0ull;       // argmax path
   float best_f = -INFINITY;
   // Admission bound: a value below it cannot make the slice's list (at
@@ -878,49 +886,37 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   float tau_wf = tau0_f;
   const float nanf_ = __int_as_float(0x7FC00000);
 
-  auto q_insert = [&](unsigned long long key) {  // key > qk[kTQ-1]
-    unsigned long long ev = qk[kTQ - 1];
-#pragma unroll
-    for (int j = kTQ - 1; j > 0; j--) {
-      if (key > qk[j - 1]) {
-        qk[j] = qk[j - 1];
-      } else if (key > qk[j]) {
-        qk[j] = key;
-      }
-    }
-    if (key > qk[0]) qk[0] = key;
-    if (ev > dk) {
-      dk = ev;
-      dv = key_val(ev);
-    }
-    q_lo = key_val(qk[kTQ - 1]);
-  };
-  auto offer_key = [&](unsigned long long key) {
-    if (use_tq) {
-      if (key > qk[kTQ - 1]) {
-        q_insert(key);
-      } else if (key > dk) {
-        dk = key;
-        dv = key_val(key);
-      }
-    } else if (key > best) {
+  auto offer_key = [&](unsigned long long key) {  // argmax rows
+    if (key > best) {
       best = key;
       best_f = key_val(key);
     }
   };
+  // list rows: the candidates read again after the stream, and their bound
+  unsigned long long *ck = reinterpret_cast<unsigned long long *>(ring + 8192);
+  float tb = -INFINITY;
+  auto cand_push = [&](unsigned long long key) {
+    const int p = atomicAdd(&s_cnt, 1);
+    if (p < kCCap) ck[p] = key;
+  };
 
   // ---- row 0's first logit (the NaN rule of argmax.c:3-13) ---------------
-  if (a == 0 && goff == 0 && tid == 0) {
-    float x = x0raw;
-    const int c = hist_on ? hash_count(hk, hn, hmask, hshift, 0u) : 0;
-    if (c > 0) x = penalize(x, c, P);
-    const float v = greedy ? x : temper(x, P);
-    s_x0nan = (v != v) ? 1 : 0;
-  }
+  // (with the table built: before the stream, or after it for list rows)
+  auto x0_check = [&]() {
+    if (a == 0 && goff == 0 && tid == 0) {
+      float x = x0raw;
+      const int c = hist_on ? hash_count(hk, hn, hmask, hshift, 0u) : 0;
+      if (c > 0) x = penalize(x, c, P);
+      const float v = greedy ? x : temper(x, P);
+      s_x0nan = (v != v) ? 1 : 0;
+    }
+  };
+  if (!use_tq) x0_check();
 
   // ---- head, tail and the penalised history ids: exact keys ---------------
   // Argmax rows take them before the stream (the best of them is a strong
   // first bound); list rows after it (the tight bound rejects most of them).
+  // A history id in the head or tail is scored there, with its count.
   auto history_round = [&]() {
     const int n_extra = head + tail + ((hist_on && !hist_stream) ? A.hts : 0);
     for (int base = 0; base < n_extra; base += NT * XPE) {
@@ -936,14 +932,16 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
         bool h = false;
         if (it < head) {
           li = a + it;
+          cnt = hist_count(li);
           h = true;
         } else if (it < head + tail) {
           li = b_al + (it - head);
+          cnt = hist_count(li);
           h = true;
         } else if (it < n_extra) {
           const int i = it - head - tail;
           const uint32_t t = hk[i];
-          if (t != kHashEmpty) {
+          if (t != kHashEmpty && static_cast<int>(t) >= a_al && static_cast<int>(t) < b_al) {
             li = static_cast<int>(t);
             cnt = static_cast<int>(hn[i]);
             h = true;
@@ -958,10 +956,6 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   #pragma unroll
       for (int e = 0; e < XPE; e++) {
         if (!((have >> e) & 1u)) continue;
-        if (cnts[e] == 0 && in_hist(lis[e])) {
-          have &= ~(1u << e);
-          continue;
-        }
         float x = xv[e];
         if (cnts[e] > 0) x = penalize(x, cnts[e], P);
         xv[e] = greedy ? x : temper(x, P);
@@ -978,8 +972,15 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
           }
         }
         offer_round<NT, MAXPER, XPE>(cbuf, cap, hwm, k_sel, sh, keys, valid);
-      } else {
+      } else if (use_tq) {
         // after the stream the bound is tight: most values stop here
+  #pragma unroll
+        for (int e = 0; e < XPE; e++)
+          if (((have >> e) & 1u) && xv[e] >= tb) {
+            const unsigned long long key = mkkey(xv[e], static_cast<uint32_t>(lis[e]) + goff);
+            if (key > tau0) cand_push(key);
+          }
+      } else {
   #pragma unroll
         for (int e = 0; e < XPE; e++)
           if (((have >> e) & 1u) && xv[e] >= tau_wf)
@@ -1001,137 +1002,23 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   const bool mulT = greedy || !P.divide;
   const float scale = greedy ? 1.0f : P.inv_T;
   if (use_tq) {
-    // Per lane: thr, the tempered value below which nothing can change this
-    // thread's state (below the block bound, or below a key it already
-    // discarded); rthr (division only), a raw value below which every value
-    // tempers below thr.
-    uint32_t seen_tau = *reinterpret_cast<volatile uint32_t *>(&s_tauv);
-    tau_wf = fmaxf(tau_wf, ord2f(seen_tau));
-    float thr = fmaxf(fminf(q_lo, dv), tau_wf);
-    float rthr = mulT ? 0.0f : raw_floor(thr, P);
-    auto retune = [&]() {
-      const float t = fmaxf(fminf(q_lo, dv), tau_wf);
-      if (t != thr) {
-        thr = t;
-        if (!mulT) rthr = raw_floor(t, P);
-      }
-    };
-    // warp w refreshes the block bound once, after its chunk refresh_at
-    const int refresh_at = warp < 4 ? 2 + warp : 2 * warp;
+    // List rows: the stream only records the sketch (each group's raw
+    // maximum; temperature is monotone, so it orders the tempered values too).
     int slot = 0;
     for (int i = 0; i < nw; i++) {
       cp_async_wait<NS - 1>();
-      const unsigned char *sb = wring + slot * kChunkBytes;
       const unsigned char *lsb = ldst + slot * kChunkBytes;
-      uint4 q[kLaneVecs];
       float mv[kLaneVecs];
 #pragma unroll
-      for (int u = 0; u < kLaneVecs; u++) {
-        q[u] = *reinterpret_cast<const uint4 *>(lsb + u * 512);
-        mv[u] = LaneVec<T>::vmax(q[u]);
-      }
-      const float m = max_of(mv);
-      const int e0 = a_al + (warp + NW * i) * (kChunkBytes / static_cast<int>(sizeof(T)));
-      if (i == 0) {
-        // A first bound from the first chunk of every warp: each of the np
-        // warps that have chunks offers the jq-th largest of its 128 vector
-        // maxima (distinct elements; a maximum that is a history id does
-        // not count, its penalised value is not known here), and the
-        // smallest offer has np * jq >= k elements at or above it.
-        uint32_t vm[kLaneVecs];
+      for (int u = 0; u < kLaneVecs; u++) mv[u] = LaneVec<T>::vmax(*reinterpret_cast<const uint4 *>(lsb + u * 512));
+      float m = max_of(mv);
 #pragma unroll
-        for (int u = 0; u < kLaneVecs; u++) {
-          vm[u] = kOrdNegInf;
-          if (mv[u] == mv[u]) {
-            bool ok = true;
-            if (hist_on) {
-              int w0 = VEC - 1;
-#pragma unroll
-              for (int w = VEC - 2; w >= 0; w--)
-                if (LaneVec<T>::elem(q[u], w) == mv[u]) w0 = w;
-              ok = !in_hist(e0 + (u * 32 + lane) * VEC + w0);
-            }
-            if (ok) vm[u] = f2ord(temper(mv[u], P));
-          }
-        }
-        const int np = min(NW, nchunks);
-        const uint32_t bj = kth_of_lane_vecs(vm, (k_sel + np - 1) / np, 32);
-        if (lane == 0) atomicMin(&s_b0, bj);
-        named_bar_sync(1, np * 32);  // the warps with chunks (warps 0 .. np-1)
-        const uint32_t b0 = *reinterpret_cast<volatile uint32_t *>(&s_b0);
-        tau_wf = fmaxf(tau_wf, ord2f(b0));
-        if (warp == 0 && lane == 0) atomicMax(&s_tauv, b0);
-        retune();
-      }
-      const bool hot = mulT ? !(__fmul_rn(m, scale) < thr) : !(m < rthr);
-      if (__any_sync(0xFFFFFFFFu, hot)) {
-        uint32_t pend = 0;
-        if (hot) {
-          if (mulT) {
-#pragma unroll
-            for (int u = 0; u < kLaneVecs; u++) {
-              if (__fmul_rn(mv[u], scale) < thr) continue;
-#pragma unroll
-              for (int w = 0; w < VEC; w++)
-                if (__fmul_rn(LaneVec<T>::elem(q[u], w), scale) >= thr) pend |= 1u << (u * VEC + w);
-            }
-          } else {
-#pragma unroll
-            for (int u = 0; u < kLaneVecs; u++) {
-              if (mv[u] < rthr) continue;
-#pragma unroll
-              for (int w = 0; w < VEC; w++)
-                if (LaneVec<T>::elem(q[u], w) >= rthr) pend |= 1u << (u * VEC + w);
-            }
-          }
-        }
-        const unsigned long long top0 = qk[0];
-        while (pend) {
-          const int e = __ffs(pend) - 1;
-          pend &= pend - 1;
-          const int pos = ((e / VEC) * 32 + lane) * VEC + (e % VEC);  // element within the chunk
-          const int li = e0 + pos;
-          float x = LaneVec<T>::smem(sb, pos);
-          if (hist_on) {
-            const int hc = hist_count(li);
-            if (hc > 0) {
-              if (!hist_stream) continue;  // offered by the history round
-              x = penalize(x, hc, P);
-            }
-          }
-          const float v = mulT ? __fmul_rn(x, scale) : __fdiv_rn(x, P.T);
-          const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
-          if (key > qk[kTQ - 1]) {
-            q_insert(key);
-          } else if (key > dk) {
-            dk = key;
-            dv = v;
-          }
-        }
-        if (qk[0] != top0) s_maxv[tid] = f2ord(key_val(qk[0]));
-        retune();
-      }
-      if (hist_on && !hist_stream && i == (nw > 3 ? nw - 3 : 0)) {
-        // the history round follows the stream: fetch its logits into L2
-        for (int it = tid; it < A.hts; it += NT)
-          if (hk[it] != kHashEmpty) prefetch_l2(rowp + hk[it]);
-      }
-      if (i == refresh_at) {
-        // the k-th largest of the threads' best values: k distinct elements
-        // are at or above it; maxima only grow, so stale entries keep it valid
-        const uint32_t bnd = kth_of_maxima(s_maxv, k_sel, 16);
-        if (lane == 0) atomicMax(&s_tauv, bnd);
-      }
-      // this lane has read its vectors of the slot (every value fed the
-      // maximum): refill them
+      for (int o = 1; o < kSkGroupLanes; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+      if ((lane & (kSkGroupLanes - 1)) == 0)
+        sketch[(warp + NW * i) * kSkPerChunk + lane / kSkGroupLanes] = static_cast<uint16_t>(sk16(m));
+      // this lane has read its vectors of the slot: refill them
       if (i + NS < nw) issue(i + NS, slot);
       cp_async_commit();
-      const uint32_t tb = *reinterpret_cast<volatile uint32_t *>(&s_tauv);
-      if (tb != seen_tau) {
-        seen_tau = tb;
-        tau_wf = fmaxf(tau_wf, ord2f(tb));
-        retune();
-      }
       slot = slot + 1 == NS ? 0 : slot + 1;
     }
   } else if (!use_block) {
@@ -1255,8 +1142,12 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   }
   cp_async_wait<0>();
 
-  // list rows: the history round after the stream, where the bounds are tight
-  if (use_tq || use_block) history_round();
+  // long-list rows: the history round after the stream, where the bound is tight
+  if (use_block) history_round();
+  if (use_tq) {
+    if (hist_on) build_hist();
+    x0_check();
+  }
   __syncthreads();
   const bool timed_out = s_timeout != 0;
 
@@ -1271,11 +1162,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       n = k_sel;
     }
     if (tid == 0) s_n = n;
-  } else if (use_tq) {
-    s_maxv[tid] = qk[0] > tau0 ? f2ord(key_val(qk[0])) : kOrdNegInf;
-    const unsigned long long d = warp_max_u64(dk);
-    if (lane == 0) atomicMax(&s_dk, d);
-  } else {
+  } else if (!use_tq) {
     best = warp_max_u64(best);
     if (lane == 0) s_red[warp] = best;
   }
@@ -1283,155 +1170,150 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   bool exact_rescan = false;
   int n_tq = 0;  // list length (queue path)
   if (use_tq) {
-    // keys whose value is at or above the k-th largest thread maximum (at
-    // least k_sel of them; resolved to 16 bits, which can only lower it and
-    // admit a few more), then the best k_sel of those
-    if (warp == 0) {
-      uint32_t v8[NW];
-#pragma unroll
-      for (int r = 0; r < NW; r++) v8[r] = s_maxv[r * 32 + lane];
-      const uint32_t bw = warp_kth_u32<NW>(v8, k_sel, 16);
-      if (lane == 0) s_b0 = bw;
-    }
-    __syncthreads();
-    const uint32_t bnd = s_b0;
-#pragma unroll
-    for (int j = 0; j < kTQ; j++) {
-      const bool keep = qk[j] > tau0 && f2ord(key_val(qk[j])) >= bnd;
-      const uint32_t bal = __ballot_sync(0xFFFFFFFFu, keep);
-      int base = 0;
-      if (lane == 0 && bal) base = atomicAdd(&s_cnt, __popc(bal));
-      base = __shfl_sync(0xFFFFFFFFu, base, 0);
-      if (keep) lst[base + __popc(bal & lanemask_lt())] = qk[j];
-    }
-    __syncthreads();
-    // Each survivor's rank is the number of survivors above it (keys are
-    // distinct); the best k_sel go straight to their place in sorted order.
-    const int n = s_cnt;
-    if (n <= 64) {
-      // the usual case: one warp sorts the survivors in place
-      if (warp == 0) {
-        warp_rank_sort_desc(lst, n);
-        if (lane == 0 && n >= k_sel) s_dk2 = lst[k_sel - 1];
-      }
-    } else {
-      int rk[kTQ];
-      bool kept[kTQ];
-      bool any = false;
-#pragma unroll
-      for (int j = 0; j < kTQ; j++) {
-        rk[j] = 0;
-        kept[j] = qk[j] > tau0 && f2ord(key_val(qk[j])) >= bnd;
-        any |= kept[j];
-      }
-      if (any) {
-        for (int i = 0; i < n; i++) {
-          const unsigned long long o = lst[i];
-#pragma unroll
-          for (int j = 0; j < kTQ; j++) rk[j] += o > qk[j] ? 1 : 0;
-        }
-      }
-      __syncthreads();  // every survivor was ranked before the list is rewritten
-#pragma unroll
-      for (int j = 0; j < kTQ; j++) {
-        if (kept[j] && rk[j] < k_sel) lst[rk[j]] = qk[j];
-        if (kept[j] && rk[j] == k_sel - 1) s_dk2 = qk[j];
-      }
-    }
-    __syncthreads();
-    // fewer than k real keys: any real discard counts
-    const unsigned long long kth = n >= k_sel ? s_dk2 : tau0;
-    n_tq = n < k_sel ? n : k_sel;
-    // A thread whose largest discarded key beats the k-th may have pushed
-    // keys of the list out of its queue.  Its warp re-reads that thread's
-    // elements (the thread its history items) and adds back every key at or
-    // above the k-th that the queue does not hold; the list is then ranked
-    // again.  Every other thread's keys at or above the k-th are in the list.
-    const bool bad = dk > kth;
-    if (__syncthreads_or(bad)) {
-      constexpr int kXMax = 2048;
-      unsigned long long *xl = lst + n_tq;  // added keys, after the list
+    // ---- a list row's list, from the sketch ---------------------------------
+    // The bound: the k-th largest sketch value, by a two-pass radix select
+    // over the 16-bit values; tb, the tempered floor of that value.
+    // Candidates, each with its exact key: every element at or above tb of
+    // the groups whose maximum can temper to tb or above, the head and tail,
+    // and (penalties that can raise a value) every history id.  Every
+    // element at or above tb is a candidate, so if k of them are, the list
+    // (their best k_sel, ranked) is exact.  The first pass counts every
+    // group; a group maximum that is a history id can fall below tb once
+    // penalised, and if fewer than k candidates remain, a second pass bounds
+    // with the groups that hold no history id, whose k maxima stand.
+    const int ng = nchunks * kSkPerChunk;
+    uint32_t *bins = reinterpret_cast<uint32_t *>(ring);  // 2 x 256 counts
+    int *glist = reinterpret_cast<int *>(ring + 2048);    // kGCap groups
+    unsigned long long *sorted = reinterpret_cast<unsigned long long *>(ring + 6144);
+    const uint32_t ord_inf = f2ord(INFINITY);
+    int nc = 0, ngs = 0;
+    for (int pass = 0; pass < 2; pass++) {
+      const bool all = pass == 0;
+      for (int i = tid; i < 512; i += NT) bins[i] = 0u;
       if (tid == 0) s_cnt = 0;
       __syncthreads();
-      auto add_back = [&](unsigned long long key, const unsigned long long (&held)[kTQ]) {
-        bool in_q = false;
-#pragma unroll
-        for (int j = 0; j < kTQ; j++) in_q |= held[j] == key;
-        if (key >= kth && key > tau0 && !in_q) {
-          const int pos = atomicAdd(&s_cnt, 1);
-          if (pos < kXMax) xl[pos] = key;
-        }
+      auto eligible = [&](int g) -> bool {
+        return all || !(hist_on && ((gbm[g >> 5] >> (g & 31)) & 1u) != 0u);
       };
-      uint32_t offenders = __ballot_sync(0xFFFFFFFFu, bad);
-      while (offenders) {
-        const int L = __ffs(offenders) - 1;
-        offenders &= offenders - 1;
-        unsigned long long held[kTQ];
-#pragma unroll
-        for (int j = 0; j < kTQ; j++) held[j] = __shfl_sync(0xFFFFFFFFu, qk[j], L);
-        // lane L's vectors: u*32 + L of each of this warp's chunks
-        for (int t = lane; t < nw * kLaneVecs; t += 32) {
-          const int c = warp + NW * (t / kLaneVecs);
-          const int j = (t % kLaneVecs) * 32 + L;
-          const int cv = c == nchunks - 1 ? (body_bytes - c * kChunkBytes) >> 4 : kChunkBytes / 16;
-          if (j >= cv) continue;
-          const uint4 qq = __ldg(reinterpret_cast<const uint4 *>(body + static_cast<size_t>(c) * kChunkBytes) + j);
-          const int el = a_al + c * (kChunkBytes / static_cast<int>(sizeof(T))) + j * VEC;
-#pragma unroll
-          for (int w = 0; w < VEC; w++) {
-            const int li = el + w;
-            float x = LaneVec<T>::elem(qq, w);
-            const int hc = hist_count(li);
-            if (hc > 0) {
-              if (!hist_stream) continue;  // among the history items below
-              x = penalize(x, hc, P);
-            }
-            const float v = temper(x, P);
-            if (v == v) add_back(mkkey(v, static_cast<uint32_t>(li) + goff), held);
+      for (int g = tid; g < ng; g += NT) {
+        const uint32_t v = sketch[g];
+        if (v != 0u && eligible(g)) atomicAdd(&bins[v >> 8], 1u);
+      }
+      __syncthreads();
+      // pass 0 bounds a few places lower, so that a handful of group maxima
+      // that are penalised history ids do not force the second pass
+      if (warp == 0) radix_pick(bins, all && hist_on ? k_sel + 8 : k_sel, &s_sel[0], &s_sel[1]);
+      __syncthreads();
+      const int hb = s_sel[0];
+      uint32_t b16 = 0u;  // 0: fewer than k groups, no bound
+      if (hb >= 0) {
+        const int need = s_sel[1];
+        for (int g = tid; g < ng; g += NT) {
+          const uint32_t v = sketch[g];
+          if (static_cast<int>(v >> 8) == hb && eligible(g)) atomicAdd(&bins[256 + (v & 255u)], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) radix_pick(bins + 256, need, &s_sel[2], &s_sel[3]);
+        __syncthreads();
+        b16 = (static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(s_sel[2]);
+      }
+      const uint32_t bord = b16 << 16;
+      tb = bord > kOrdNegInf ? temper(ord2f(bord), P) : -INFINITY;
+      // the groups to read again: a maximum below ord2f((v + 1) << 16)
+      // tempers to at most that value's temper
+      for (int g0 = 0; g0 < ng; g0 += NT) {
+        const int g = g0 + tid;
+        bool sel = false;
+        if (g < ng) {
+          const uint32_t v = sketch[g];
+          if (v != 0u) {
+            const uint32_t up = min((v << 16) | 0xFFFFu, ord_inf);
+            sel = !(temper(ord2f(up), P) < tb);
           }
         }
-      }
-      if (bad) {
-        // this thread's items of the history round (item it: tid, tid + NT, ...)
-        for (int it = tid; it < head + tail + ((hist_on && !hist_stream) ? A.hts : 0); it += NT) {
-          int li, cnt = 0;
-          if (it < head) {
-            li = a + it;
-          } else if (it < head + tail) {
-            li = b_al + (it - head);
-          } else {
-            const int i = it - head - tail;
-            if (hk[i] == kHashEmpty) continue;
-            li = static_cast<int>(hk[i]);
-            cnt = static_cast<int>(hn[i]);
-          }
-          if (cnt == 0 && in_hist(li)) continue;
-          float x = load_scalar<T>(rowp, li);
-          if (cnt > 0) x = penalize(x, cnt, P);
-          const float v = temper(x, P);
-          if (v == v) add_back(mkkey(v, static_cast<uint32_t>(li) + goff), qk);
+        const uint32_t bal = __ballot_sync(0xFFFFFFFFu, sel);
+        int base = 0;
+        if (lane == 0 && bal) base = atomicAdd(&s_cnt, __popc(bal));
+        base = __shfl_sync(0xFFFFFFFFu, base, 0);
+        if (sel) {
+          const int p = base + __popc(bal & lanemask_lt());
+          if (p < kGCap) glist[p] = g;
         }
       }
       __syncthreads();
-      const int ne = s_cnt;
-      if (ne > kXMax) {
-        exact_rescan = true;  // too many to add back: redo the slice below
-      } else {
-        // rank the list and the added keys together; the best k_sel, in
-        // order, go to tmp and then back to the list
-        const int m = n_tq + ne;
-        unsigned long long *tmp = lst + m;
-        for (int i = tid; i < m; i += NT) {
-          const unsigned long long key = lst[i];
-          int r = 0;
-          for (int j2 = 0; j2 < m; j2++) r += lst[j2] > key ? 1 : 0;
-          if (r < k_sel) tmp[r] = key;
+      ngs = s_cnt;
+      __syncthreads();
+      if (tid == 0) s_cnt = 0;
+      __syncthreads();
+      if (ngs <= kGCap) {
+        // each group: kSkGroupLanes lanes x kLaneVecs vectors, read from L2
+        // or HBM, XG at a time per thread with all loads in flight together
+        constexpr int GV = kSkGroupLanes * kLaneVecs;
+        constexpr int XG = 4;
+        constexpr int kPerChunk = kChunkBytes / static_cast<int>(sizeof(T));
+        for (int base = 0; base < ngs * GV; base += NT * XG) {
+          uint4 qv[XG];
+          int el[XG];
+          uint32_t ok = 0u;
+#pragma unroll
+          for (int e = 0; e < XG; e++) {
+            const int it = base + e * NT + tid;
+            el[e] = 0;
+            if (it < ngs * GV) {
+              const int g = glist[it / GV];
+              const int v = it % GV;
+              const int c = g / kSkPerChunk, pq = g % kSkPerChunk;
+              const int vi = (v / kSkGroupLanes) * 32 + pq * kSkGroupLanes + (v % kSkGroupLanes);
+              const int cv = c == nchunks - 1 ? (body_bytes - c * kChunkBytes) >> 4 : kChunkBytes / 16;
+              if (vi < cv) {
+                qv[e] = __ldg(reinterpret_cast<const uint4 *>(body + static_cast<size_t>(c) * kChunkBytes) + vi);
+                el[e] = a_al + c * kPerChunk + vi * VEC;
+                ok |= 1u << e;
+              }
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < XG; e++) {
+            if (!((ok >> e) & 1u)) continue;
+#pragma unroll
+            for (int w = 0; w < VEC; w++) {
+              const int li = el[e] + w;
+              float x = LaneVec<T>::elem(qv[e], w);
+              if (hist_on) {
+                const int hc = hist_count(li);
+                if (hc > 0) {
+                  if (!pen_dec) continue;  // scored in the history round
+                  x = penalize(x, hc, P);
+                }
+              }
+              const float v = temper(x, P);
+              if (v >= tb) {
+                const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
+                if (key > tau0) cand_push(key);
+              }
+            }
+          }
         }
-        __syncthreads();
-        n_tq = m < k_sel ? m : k_sel;
-        for (int i = tid; i < n_tq; i += NT) lst[i] = tmp[i];
-        __syncthreads();
+        history_round();
       }
+      __syncthreads();
+      nc = s_cnt;
+      if (ngs > kGCap || nc > kCCap) break;
+      if (nc >= k_sel || !hist_on || b16 == 0u) break;
+      __syncthreads();  // every thread has read s_cnt before the next pass resets it
+    }
+    if (ngs > kGCap || nc > kCCap) {
+      exact_rescan = true;  // too many to keep: redo the slice below
+    } else {
+      for (int i = tid; i < nc; i += NT) {
+        const unsigned long long key = ck[i];
+        int r = 0;
+        for (int j = 0; j < nc; j++) r += ck[j] > key ? 1 : 0;
+        if (r < k_sel) sorted[r] = key;
+      }
+      __syncthreads();
+      n_tq = nc < k_sel ? nc : k_sel;
+      lst = sorted;
     }
   }
   if (exact_rescan) {

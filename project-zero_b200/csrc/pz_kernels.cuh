@@ -103,7 +103,7 @@ struct MergeArgs {               // vocab-sharded merge after the allgather
 // Launchers (pz_kernels.cu).  Return cudaGetLastError() after the launch.
 cudaError_t launch_slice(const SliceArgs &a, int dtype, size_t smem,
                          cudaStream_t st);
-size_t slice_smem_bytes(int kcap, int hts, int nstages, int V);
+size_t slice_smem_bytes(int kcap, int hts, int nstages, int V, int elem_bytes);
 int slice_stages(int kcap, int hts);
 cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem,
                         cudaStream_t st);
