@@ -519,6 +519,14 @@ __host__ __device__ inline int slice_sketch_entries(int V, int elem_bytes, int k
 }
 __device__ __forceinline__ uint32_t sk16(float m) { return m == m ? f2ord(m) >> 16 : 0u; }
 
+// A 32-bit global load issued where it stands (volatile asm keeps it ahead
+// of the stream's copies), for a value first used after the stream.
+__device__ __forceinline__ int ld_early(const int32_t *p) {
+  int v;
+  asm volatile("ld.global.nc.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
 // Warp 0: the bin of `bins` (256 counts, the highest bin first in rank)
 // holding the need-th largest value, and how many of that bin's values are
 // still needed; bin -1 if the bins hold fewer than `need` values.
@@ -691,6 +699,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   __shared__ uint32_t s_tauv;           // ordered value: the block's admission bound
   __shared__ RowPlan s_plan;
   __shared__ int s_sel[4];              // radix picks of the sketch bound
+  __shared__ uint32_t s_skmax;          // largest sketch value of the slice
   __shared__ int s_x0nan, s_timeout, s_cnt, s_n;
 
   const int tid = threadIdx.x;
@@ -804,6 +813,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     s_timeout = 0;
     s_cnt = 0;
     s_tauv = f2ord(tau0_f);
+    s_skmax = 0u;
     sh.n = 0;
     sh.tau = tau0;
   }
@@ -822,7 +832,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
 #pragma unroll
   for (int u = 0; u < IPT; u++) {
     const int j = u * NT + tid;
-    hid[u] = hist_on && j < H ? static_cast<int>(static_cast<long long>(hrow[j]) - A.v_offset) : -1;
+    hid[u] = hist_on && j < H ? static_cast<int>(static_cast<long long>(ld_early(hrow + j)) - A.v_offset) : -1;
   }
   auto build_hist = [&]() {
     for (int i = tid; i < A.hts; i += NT) {
@@ -1014,8 +1024,11 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       float m = max_of(mv);
 #pragma unroll
       for (int o = 1; o < kSkGroupLanes; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+      const uint32_t v16 = sk16(m);
       if ((lane & (kSkGroupLanes - 1)) == 0)
-        sketch[(warp + NW * i) * kSkPerChunk + lane / kSkGroupLanes] = static_cast<uint16_t>(sk16(m));
+        sketch[(warp + NW * i) * kSkPerChunk + lane / kSkGroupLanes] = static_cast<uint16_t>(v16);
+      const uint32_t wmax = __reduce_max_sync(0xFFFFFFFFu, v16);
+      if (lane == 0 && wmax > *reinterpret_cast<volatile uint32_t *>(&s_skmax)) atomicMax(&s_skmax, wmax);
       // this lane has read its vectors of the slot: refill them
       if (i + NS < nw) issue(i + NS, slot);
       cp_async_commit();
@@ -1195,27 +1208,44 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       auto eligible = [&](int g) -> bool {
         return all || !(hist_on && ((gbm[g >> 5] >> (g & 31)) & 1u) != 0u);
       };
-      for (int g = tid; g < ng; g += NT) {
-        const uint32_t v = sketch[g];
-        if (v != 0u && eligible(g)) atomicAdd(&bins[v >> 8], 1u);
-      }
-      __syncthreads();
       // pass 0 bounds a few places lower, so that a handful of group maxima
       // that are penalised history ids do not force the second pass
-      if (warp == 0) radix_pick(bins, all && hist_on ? k_sel + 8 : k_sel, &s_sel[0], &s_sel[1]);
+      const int kb = all && hist_on ? k_sel + 8 : k_sel;
+      // usually one pass: the values within 255 of the largest, M, each in
+      // its own bin; else the high byte, then the low byte
+      const uint32_t M = s_skmax;
+      for (int g = tid; g < ng; g += NT) {
+        const uint32_t v = sketch[g];
+        if (v != 0u && M - v < 256u && eligible(g)) atomicAdd(&bins[255u - (M - v)], 1u);
+      }
       __syncthreads();
-      const int hb = s_sel[0];
+      if (warp == 0) radix_pick(bins, kb, &s_sel[0], &s_sel[1]);
+      __syncthreads();
       uint32_t b16 = 0u;  // 0: fewer than k groups, no bound
-      if (hb >= 0) {
-        const int need = s_sel[1];
+      if (s_sel[0] >= 0) {
+        b16 = M - 255u + static_cast<uint32_t>(s_sel[0]);
+      } else {
+        for (int i = tid; i < 256; i += NT) bins[i] = 0u;
+        __syncthreads();
         for (int g = tid; g < ng; g += NT) {
           const uint32_t v = sketch[g];
-          if (static_cast<int>(v >> 8) == hb && eligible(g)) atomicAdd(&bins[256 + (v & 255u)], 1u);
+          if (v != 0u && eligible(g)) atomicAdd(&bins[v >> 8], 1u);
         }
         __syncthreads();
-        if (warp == 0) radix_pick(bins + 256, need, &s_sel[2], &s_sel[3]);
+        if (warp == 0) radix_pick(bins, kb, &s_sel[0], &s_sel[1]);
         __syncthreads();
-        b16 = (static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(s_sel[2]);
+        const int hb = s_sel[0];
+        if (hb >= 0) {
+          const int need = s_sel[1];
+          for (int g = tid; g < ng; g += NT) {
+            const uint32_t v = sketch[g];
+            if (static_cast<int>(v >> 8) == hb && eligible(g)) atomicAdd(&bins[256 + (v & 255u)], 1u);
+          }
+          __syncthreads();
+          if (warp == 0) radix_pick(bins + 256, need, &s_sel[2], &s_sel[3]);
+          __syncthreads();
+          b16 = (static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(s_sel[2]);
+        }
       }
       const uint32_t bord = b16 << 16;
       tb = bord > kOrdNegInf ? temper(ord2f(bord), P) : -INFINITY;
@@ -1254,7 +1284,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
         for (int base = 0; base < ngs * GV; base += NT * XG) {
           uint4 qv[XG];
           int el[XG];
-          uint32_t ok = 0u;
+          uint32_t ok = 0u, gh = 0u;  // loaded; in a group with a history id
 #pragma unroll
           for (int e = 0; e < XG; e++) {
             const int it = base + e * NT + tid;
@@ -1269,6 +1299,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
                 qv[e] = __ldg(reinterpret_cast<const uint4 *>(body + static_cast<size_t>(c) * kChunkBytes) + vi);
                 el[e] = a_al + c * kPerChunk + vi * VEC;
                 ok |= 1u << e;
+                if (hist_on && ((gbm[g >> 5] >> (g & 31)) & 1u) != 0u) gh |= 1u << e;
               }
             }
           }
@@ -1279,7 +1310,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
             for (int w = 0; w < VEC; w++) {
               const int li = el[e] + w;
               float x = LaneVec<T>::elem(qv[e], w);
-              if (hist_on) {
+              if ((gh >> e) & 1u) {
                 const int hc = hist_count(li);
                 if (hc > 0) {
                   if (!pen_dec) continue;  // scored in the history round

@@ -263,16 +263,35 @@ __device__ __noinline__ int warp_sample_small(const unsigned long long *lk, int 
   };
   // lane 0's running sums of x[0..n) into out[]; returns the first j with
   // out[j] >= stop (or n)
+  // (four at a time, the loads ahead of the sums: the addends are not
+  // negative, so the sums only grow and a block whose last sum is below
+  // `stop` has no hit; sums past the hit are scratch)
   auto seq_cum = [&](const float *x, int n, float *out, float stop) -> int {
     int hit = n;
     if (lane == 0) {
       float s = 0.0f;
-      for (int j = 0; j < n; j++) {
-        s = __fadd_rn(s, x[j]);
-        out[j] = s;
-        if (s >= stop) {
-          hit = j;
+      int j = 0;
+      for (; j + 4 <= n; j += 4) {
+        const float a = x[j], b = x[j + 1], d = x[j + 2], f = x[j + 3];
+        const float s1 = __fadd_rn(s, a), s2 = __fadd_rn(s1, b), s3 = __fadd_rn(s2, d), s4 = __fadd_rn(s3, f);
+        out[j] = s1;
+        out[j + 1] = s2;
+        out[j + 2] = s3;
+        out[j + 3] = s4;
+        if (s4 >= stop) {
+          hit = s1 >= stop ? j : s2 >= stop ? j + 1 : s3 >= stop ? j + 2 : j + 3;
           break;
+        }
+        s = s4;
+      }
+      if (hit == n) {
+        for (; j < n; j++) {
+          s = __fadd_rn(s, x[j]);
+          out[j] = s;
+          if (s >= stop) {
+            hit = j;
+            break;
+          }
         }
       }
     }
