@@ -256,11 +256,20 @@ void pz_row_shard(int B, int world, int rank, int *begin, int *count) {
 // of at least 2048 columns, the split rows' lists within the context's
 // scratch, and S lists of the launch's list length within the merge area
 // (4096 keys).
+// B200 HBM3e, bytes per ns (measured copy bandwidth), and the fraction of
+// a CTA's life by which the slots of an SM are staggered.
+constexpr double kHbmBytesPerNs = 6400.0;
+constexpr double kStaggerFrac = 0.4;
+
+static int slice_occupancy(size_t smem) {
+  const size_t per_sm = 228 * 1024;
+  const int occ = static_cast<int>(per_sm / (smem + 2048));
+  return std::max(1, std::min(occ, 3));
+}
+
 static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
                           size_t smem, int *B1_out, int *S_out, int *L_out) {
-  const size_t per_sm = 228 * 1024;
-  int occ = static_cast<int>(per_sm / (smem + 2048));
-  occ = std::max(1, std::min(occ, 3));
+  const int occ = slice_occupancy(smem);
   const int slots = c->num_sms * occ;
   int B1 = 0, S = 1;
   if (B < slots) {
@@ -361,6 +370,24 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
       pz::slice_smem_bytes(a.kcap, a.hts, a.nstages, a.V, dtype == PZ_DTYPE_BF16 ? 2 : 4);
   choose_slices(ctx, B, V, a.kcap, smem, &a.B1, &a.S, &a.L);
   if (smem > static_cast<size_t>(pz::max_dynamic_smem())) return fail(PZ_ERR_UNSUPPORTED);
+  // Stagger of the first wave's list-row CTAs.  A wave's CTAs start
+  // together, stream together and then all run their end-of-row work with
+  // HBM idle; starting the CTA slots of an SM a fraction of a CTA's life
+  // apart keeps some of them streaming at any time.  A CTA's life is about
+  // its bytes at its share of HBM (CTAs in flight x bytes / bandwidth).
+  {
+    const int occ = slice_occupancy(smem);
+    const int slots = ctx->num_sms * occ;
+    const double cta_bytes = static_cast<double>(a.S == 1 ? V : a.L) * (dtype == PZ_DTYPE_BF16 ? 2 : 4);
+    const double life_ns = cta_bytes * std::min(slots, B * a.S) / kHbmBytesPerNs;
+    static const int forced = [] {
+      const char *e = std::getenv("PZ_STAGGER_NS");  // tuning override
+      return e ? std::atoi(e) : -1;
+    }();
+    a.stagger_ns = forced >= 0 ? forced : static_cast<int>(kStaggerFrac * life_ns);
+    a.stagger_ctas = slots;
+    a.stagger_occ = occ;
+  }
   const bool full_pass = !emit && !no_full;
   if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t), st) != cudaSuccess)
     return fail(PZ_ERR_CUDA);

@@ -527,9 +527,10 @@ __device__ __forceinline__ int ld_early(const int32_t *p) {
   return v;
 }
 
-// Warp 0: the bin of `bins` (256 counts, the highest bin first in rank)
-// holding the need-th largest value, and how many of that bin's values are
-// still needed; bin -1 if the bins hold fewer than `need` values.
+// One warp: the bin of `bins` (256 counts; bin j holds the j-th smallest
+// value range) that holds the need-th largest counted value, and how many
+// of that bin's values are still needed; bin -1 if the bins hold fewer
+// than `need` values.
 __device__ __noinline__ void radix_pick(const uint32_t *bins, int need, int *bin_out, int *rem_out) {
   const int lane = threadIdx.x & 31;
   uint32_t c[8], sum = 0u;
@@ -682,6 +683,10 @@ int slice_stages(int, int) { return kSlots; }
 // takes their maximum; temperature is monotone, so the tempered maximum
 // decides with one compare whether any of the lane's values can still
 // matter.  Only those values are tempered, keyed and offered.
+// Arrivals of first-wave CTAs per SM (counted across launches; consecutive
+// arrivals on an SM take consecutive slots modulo its CTAs in flight).
+__device__ unsigned g_slot_arrivals[256];
+
 template <typename T>
 __global__ void __launch_bounds__(kSliceThreads, 3)
     slice_kernel(const SliceArgs A) {
@@ -788,7 +793,9 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   // lists up to kTQK long: the stream keeps only the sketch, and the list
   // comes from the groups that can reach its bound; longer lists: one
   // block-wide buffer.
-  const bool use_tq = k_sel > 1 && k_sel <= kTQK && nchunks * kSkPerChunk <= sk_cap;
+  const bool use_tq = k_sel > 1 && k_sel <= kTQK;
+  // the sketch covers a whole row (the largest slice), so this always holds
+  const bool sketch_ok = nchunks * kSkPerChunk <= sk_cap;
   const bool use_block = k_sel > kTQK;
   const unsigned long long tau0 = (P0.mode == kModeTopK) ? key_topk_floor() : 0ull;
   const float tau0_f = tau0 == 0ull ? -INFINITY : key_val(tau0);
@@ -808,6 +815,24 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   const bool hist_stream = hist_on && use_tq && pen_dec;
 
   if (tid == 0) {
+    if ((use_tq || use_block) && A.stagger_ns > 0 && blockIdx.x < static_cast<unsigned>(A.stagger_ctas)) {
+      // the first wave: this CTA's slot on its SM (arrival order), and a
+      // start that many stagger steps late (the first copies already fly;
+      // the wait is bounded by the clock and by a step count)
+      unsigned smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      const unsigned slot = atomicAdd(&g_slot_arrivals[smid & 255u], 1u) % static_cast<unsigned>(A.stagger_occ);
+      const unsigned long long wait = static_cast<unsigned long long>(slot) * static_cast<unsigned>(A.stagger_ns);
+      if (wait > 0ull) {
+        unsigned long long t0, t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        for (int it = 0; it < 20000; it++) {
+          __nanosleep(500);
+          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+          if (t - t0 >= wait) break;
+        }
+      }
+    }
     s_plan = P0;
     s_x0nan = 0;
     s_timeout = 0;
@@ -1025,7 +1050,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
 #pragma unroll
       for (int o = 1; o < kSkGroupLanes; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
       const uint32_t v16 = sk16(m);
-      if ((lane & (kSkGroupLanes - 1)) == 0)
+      if ((lane & (kSkGroupLanes - 1)) == 0 && sketch_ok)
         sketch[(warp + NW * i) * kSkPerChunk + lane / kSkGroupLanes] = static_cast<uint16_t>(v16);
       const uint32_t wmax = __reduce_max_sync(0xFFFFFFFFu, v16);
       if (lane == 0 && wmax > *reinterpret_cast<volatile uint32_t *>(&s_skmax)) atomicMax(&s_skmax, wmax);
@@ -1194,7 +1219,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     // group; a group maximum that is a history id can fall below tb once
     // penalised, and if fewer than k candidates remain, a second pass bounds
     // with the groups that hold no history id, whose k maxima stand.
-    const int ng = nchunks * kSkPerChunk;
+    const int ng = sketch_ok ? nchunks * kSkPerChunk : 0;
     uint32_t *bins = reinterpret_cast<uint32_t *>(ring);  // 2 x 256 counts
     int *glist = reinterpret_cast<int *>(ring + 2048);    // kGCap groups
     unsigned long long *sorted = reinterpret_cast<unsigned long long *>(ring + 6144);
@@ -1333,7 +1358,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       if (nc >= k_sel || !hist_on || b16 == 0u) break;
       __syncthreads();  // every thread has read s_cnt before the next pass resets it
     }
-    if (ngs > kGCap || nc > kCCap) {
+    if (ngs > kGCap || nc > kCCap || !sketch_ok) {
       exact_rescan = true;  // too many to keep: redo the slice below
     } else {
       for (int i = tid; i < nc; i += NT) {

@@ -43,6 +43,11 @@ struct SliceArgs {
   int nstages;          // bulk-copy ring slots per warp
   int mode_emit;        // 1: write the merged local list (vocab sharding), no draw
   int no_full_vocab;
+  // The first wave's list-row CTAs start stagger_ns apart per CTA slot of
+  // an SM (0: off); the first stagger_ctas CTAs are that wave.
+  int stagger_ns;
+  int stagger_ctas;
+  int stagger_occ;      // CTAs in flight per SM
   // scratch
   unsigned long long *slice_keys;  // [(B-B1)*S][kcap] split rows' slice lists
   int32_t *slice_cnt;              // [(B-B1)*S]

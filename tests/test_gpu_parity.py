@@ -182,11 +182,11 @@ def test_vocab_sharded_single_rank(cuda, pz, golden):
     s.close()
 
 
-def test_register_queue_overflow_falls_back_exactly(cuda, pz, oracle_lib):
-    """The per-thread queues keep 4 keys; when one thread's share of a slice
-    holds more of the list than that (large values at positions that all map
-    to the same thread), the kernel must detect it and redo the slice
-    exactly."""
+def test_list_values_crowded_in_few_lanes(cuda, pz, oracle_lib):
+    """The list's values at positions that all fall to the same lanes of
+    every chunk (one sketch group per chunk holds several of them): the
+    group maxima alone undercount the list, and the re-read of the groups
+    at or above the bound must still find every value of the exact list."""
     rs = np.random.default_rng(5)
     for dtype, period in [("f32", 1024), ("bf16", 2048)]:
         B, V = 4, 65536
