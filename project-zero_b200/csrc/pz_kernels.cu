@@ -270,13 +270,14 @@ __device__ __noinline__ int sample_list(const unsigned long long *lk, int n_sel,
 // The decision for one row from its merged list (one warp): the draw (or
 // argmax), its outputs, a full-vocabulary hand-off to full_kernel, or the
 // published list (vocab sharding).  lst: sorted descending, n_sel real keys
-// then zeros up to kcap (top-k rows); gbest: the best key (other rows).
-// fe, fp, ford, s_tok: the warp's shared scratch of kcap entries each.
+// then zeros up to kcap (top-k rows); gbest: the best key (other rows);
+// rs: the row's RNG state.  fe, fp, ford, s_tok: the warp's shared scratch
+// of kcap entries each.
 __device__ __forceinline__ void finalize_row(const SliceArgs &A, int row, const RowPlan &P, bool bad_k,
                                           bool too_long, bool row_timed_out, bool x0nan,
                                           const unsigned long long *lst, int n_sel,
-                                          unsigned long long gbest, float *fe, float *fp, int *ford,
-                                          int *s_tokp) {
+                                          unsigned long long gbest, unsigned long long rs, float *fe,
+                                          float *fp, int *ford, int *s_tokp) {
   const int lane = threadIdx.x & 31;
   int &s_tok = *s_tokp;
   const unsigned long long tau0 = (P.mode == kModeTopK) ? key_topk_floor() : 0ull;
@@ -300,7 +301,6 @@ __device__ __forceinline__ void finalize_row(const SliceArgs &A, int row, const 
     return;
   }
 
-  unsigned long long rs = A.rng[row];
   int tok = -1;
   int status = too_long ? PZ_ROW_HISTORY_TOO_LONG : PZ_ROW_OK;
   bool pending = false;
@@ -511,6 +511,7 @@ constexpr int kTQK = 64;        // lists up to this long use the sketch path
 constexpr int kSkGroupLanes = 4;
 constexpr int kSkPerChunk = 32 / kSkGroupLanes;
 constexpr int kGCap = 1024;     // candidate groups
+constexpr int kInsertAt = 2;    // list rows: chunk at which a warp files the first history ids
 constexpr int kCCap = 2048;     // candidate keys
 __host__ __device__ inline int slice_sketch_entries(int V, int elem_bytes, int kcap) {
   if (kcap <= 1) return 0;
@@ -703,6 +704,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   __shared__ unsigned long long s_red[NW];
   __shared__ uint32_t s_tauv;           // ordered value: the block's admission bound
   __shared__ RowPlan s_plan;
+  __shared__ unsigned long long s_rng;  // the row's RNG state at entry
   __shared__ int s_sel[4];              // radix picks of the sketch bound
   __shared__ uint32_t s_skmax;          // largest sketch value of the slice
   __shared__ int s_x0nan, s_timeout, s_cnt, s_n;
@@ -785,6 +787,8 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     h1 = A.hist_off[row + 1];
   }
   const float x0raw = (a == 0 && A.v_offset == 0 && tid == 0) ? load_scalar<T>(rowp, 0) : 0.0f;
+  // the row's RNG state, needed only by the decision: fetched now, with the settings
+  const unsigned long long rng0 = (tid == 0 && !A.mode_emit) ? A.rng[row] : 0ull;
   const RowPlan P0 = plan_row(cfg, A.V_global);
   const bool greedy = P0.mode == kModeGreedy;
   // a list longer than this launch was sized for (hint broken): flag the row
@@ -834,6 +838,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       }
     }
     s_plan = P0;
+    s_rng = rng0;
     s_x0nan = 0;
     s_timeout = 0;
     s_cnt = 0;
@@ -850,8 +855,8 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   // ---- the slice's history ids and counts ---------------------------------
   // The first NT*IPT ids are loaded now, while the first copies fly.  Argmax
   // and long-list rows build the table before the stream, which consults
-  // it; list rows after it, when the loads have long landed (their stream
-  // keeps only the sketch).
+  // it; list rows during it (their stream keeps only the sketch, and the
+  // table is first needed after it).
   constexpr int IPT = 4;
   int hid[IPT];
 #pragma unroll
@@ -859,7 +864,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     const int j = u * NT + tid;
     hid[u] = hist_on && j < H ? static_cast<int>(static_cast<long long>(ld_early(hrow + j)) - A.v_offset) : -1;
   }
-  auto build_hist = [&]() {
+  auto init_hist = [&]() {
     for (int i = tid; i < A.hts; i += NT) {
       hk[i] = kHashEmpty;
       hn[i] = 0u;
@@ -867,44 +872,59 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     for (int i = tid; i < slice_hbm_words(A.V, A.hts); i += NT) hbm[i] = 0u;
     if (use_tq)
       for (int i = tid; i < sk_cap / 32; i += NT) gbm[i] = 0u;
-    // argmax rows take the history round right after this, so the logits
-    // the ids name are fetched into L2 now
-    const bool pre = !use_tq && !use_block;
+  };
+  auto insert_ids = [&](const int (&t)[IPT]) {
+#pragma unroll
+    for (int u = 0; u < IPT; u++)
+      if (t[u] >= a && t[u] < b) {
+        hash_insert(hk, hn, hmask, hshift, static_cast<uint32_t>(t[u]));
+        atomicOr(&hbm[t[u] >> 7], 1u << ((t[u] >> 2) & 31));
+        if (use_tq && t[u] >= a_al && t[u] < b_al) {
+          // the sketch group of column t: chunk, then the lane of its vector
+          constexpr int kPerChunk = kChunkBytes / static_cast<int>(sizeof(T));
+          const int off = t[u] - a_al;
+          const int g = (off / kPerChunk) * kSkPerChunk + (((off % kPerChunk) / VEC) & 31) / kSkGroupLanes;
+          atomicOr(&gbm[g >> 5], 1u << (g & 31));
+        }
+      }
+  };
+  // argmax rows take the history round right after the table is built, so
+  // the logits the ids name are fetched into L2 first
+  const bool pre = !use_tq && !use_block;
+  auto insert_rest = [&]() {  // the ids past the first NT*IPT
+    for (int base = NT * IPT; base < H; base += NT * IPT) {
+      int t[IPT];
+#pragma unroll
+      for (int u = 0; u < IPT; u++) {
+        const int j = base + u * NT + tid;
+        t[u] = j < H ? static_cast<int>(static_cast<long long>(hrow[j]) - A.v_offset) : -1;
+      }
+      if (pre) {
+#pragma unroll
+        for (int u = 0; u < IPT; u++)
+          if (t[u] >= a && t[u] < b) prefetch_l2(rowp + t[u]);
+      }
+      insert_ids(t);
+    }
+  };
+  if (hist_on && !use_tq) {
+    init_hist();
     if (pre) {
 #pragma unroll
       for (int u = 0; u < IPT; u++)
         if (hid[u] >= a && hid[u] < b) prefetch_l2(rowp + hid[u]);
     }
     __syncthreads();  // the table is initialised
-    for (int base = 0; base < H; base += NT * IPT) {
-      int t[IPT];
-#pragma unroll
-      for (int u = 0; u < IPT; u++) {
-        const int j = base + u * NT + tid;
-        t[u] = base == 0 ? hid[u] : (j < H ? static_cast<int>(static_cast<long long>(hrow[j]) - A.v_offset) : -1);
-      }
-      if (pre && base > 0) {
-#pragma unroll
-        for (int u = 0; u < IPT; u++)
-          if (t[u] >= a && t[u] < b) prefetch_l2(rowp + t[u]);
-      }
-#pragma unroll
-      for (int u = 0; u < IPT; u++)
-        if (t[u] >= a && t[u] < b) {
-          hash_insert(hk, hn, hmask, hshift, static_cast<uint32_t>(t[u]));
-          atomicOr(&hbm[t[u] >> 7], 1u << ((t[u] >> 2) & 31));
-          if (use_tq && t[u] >= a_al && t[u] < b_al) {
-            // the sketch group of column t: chunk, then the lane of its vector
-            constexpr int kPerChunk = kChunkBytes / static_cast<int>(sizeof(T));
-            const int off = t[u] - a_al;
-            const int g = (off / kPerChunk) * kSkPerChunk + (((off % kPerChunk) / VEC) & 31) / kSkGroupLanes;
-            atomicOr(&gbm[g >> 5], 1u << (g & 31));
-          }
-        }
-    }
+    insert_ids(hid);
+    insert_rest();
     __syncthreads();
-  };
-  if (hist_on && !use_tq) build_hist();
+  }
+  if (hist_on && use_tq) {
+    // list rows: the table is filled during the stream (the first ids at the
+    // warp's chunk kInsertAt, when their loads have landed), the rest after it
+    init_hist();
+    __syncthreads();
+  }
   // the bitmap answers most lookups; a set bit sends the id to the table
   auto hist_count = [&](int li) -> int {
     return hist_on && ((hbm[li >> 7] >> ((li >> 2) & 31)) & 1u) != 0u
@@ -1054,11 +1074,13 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
         sketch[(warp + NW * i) * kSkPerChunk + lane / kSkGroupLanes] = static_cast<uint16_t>(v16);
       const uint32_t wmax = __reduce_max_sync(0xFFFFFFFFu, v16);
       if (lane == 0 && wmax > *reinterpret_cast<volatile uint32_t *>(&s_skmax)) atomicMax(&s_skmax, wmax);
+      if (i == kInsertAt && hist_on) insert_ids(hid);
       // this lane has read its vectors of the slot: refill them
       if (i + NS < nw) issue(i + NS, slot);
       cp_async_commit();
       slot = slot + 1 == NS ? 0 : slot + 1;
     }
+    if (hist_on && nw <= kInsertAt) insert_ids(hid);  // a warp with too few chunks
   } else if (!use_block) {
     // argmax: the threshold is the block's best value so far (warp-uniform);
     // only a lane's maximum and its ties can beat it
@@ -1182,10 +1204,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
 
   // long-list rows: the history round after the stream, where the bound is tight
   if (use_block) history_round();
-  if (use_tq) {
-    if (hist_on) build_hist();
-    x0_check();
-  }
+  if (use_tq && hist_on) insert_rest();
   __syncthreads();
   const bool timed_out = s_timeout != 0;
 
@@ -1230,6 +1249,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       for (int i = tid; i < 512; i += NT) bins[i] = 0u;
       if (tid == 0) s_cnt = 0;
       __syncthreads();
+      if (pass == 0) x0_check();  // the history table is complete
       auto eligible = [&](int g) -> bool {
         return all || !(hist_on && ((gbm[g >> 5] >> (g & 31)) & 1u) != 0u);
       };
@@ -1482,7 +1502,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     row_timed_out |= ml.timed_out != 0;
     x0nan = (__ldcg(A.row_flags + row) & 1u) != 0u;
   }
-  finalize_row(A, row, P, bad_k, too_long, row_timed_out, x0nan, fl, n_sel, gbest, fe, fp, ford,
+  finalize_row(A, row, P, bad_k, too_long, row_timed_out, x0nan, fl, n_sel, gbest, s_rng, fe, fp, ford,
                s_tokp);
 }
 
