@@ -1355,15 +1355,20 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
             for (int w = 0; w < VEC; w++) {
               const int li = el[e] + w;
               float x = LaneVec<T>::elem(qv[e], w);
-              if ((gh >> e) & 1u) {
-                const int hc = hist_count(li);
-                if (hc > 0) {
-                  if (!pen_dec) continue;  // scored in the history round
-                  x = penalize(x, hc, P);
-                }
-              }
-              const float v = temper(x, P);
+              float v = temper(x, P);
               if (v >= tb) {
+                // only a value that reaches the bound unpenalised is looked
+                // up: a penalty that can only lower it cannot lift a value
+                // below the bound, and the other penalties' ids are scored
+                // in the history round
+                if ((gh >> e) & 1u) {
+                  const int hc = hist_count(li);
+                  if (hc > 0) {
+                    if (!pen_dec) continue;
+                    v = temper(penalize(x, hc, P), P);
+                    if (!(v >= tb)) continue;
+                  }
+                }
                 const unsigned long long key = mkkey(v, static_cast<uint32_t>(li) + goff);
                 if (key > tau0) cand_push(key);
               }
