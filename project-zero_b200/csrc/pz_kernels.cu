@@ -671,22 +671,26 @@ size_t slice_smem_bytes(int kcap, int hts, int nslots, int V, int elem_bytes) {
 }
 
 // Ring slots per warp: kSlots chunks of 2 KB in flight per warp (48 KB per
-// CTA; with the history table, three CTAs fit in an SM's 228 KB).  The
-// end-of-slice merge needs 16 KB of the ring and the rescan buffer
-// kTQK + kCapB keys, both well inside it.
+// CTA; with the history table and the sketch, three CTAs fit in an SM's
+// 228 KB).  After the stream the ring holds the list work: the candidates
+// (up to kCCap keys from 8 KB on), the merged slice lists and the
+// decision's scratch (from kFinalizeOff on), or the rescan buffer.
 int slice_stages(int, int) { return kSlots; }
 
-// One CTA per (row, slice of L columns).  The slice's 16-byte-aligned body
-// is cut into chunks of kChunkBytes; warp w streams chunks w, w + NW, ...
-// through its own ring of bulk copies (its lane 0 issues them and refills a
-// slot as soon as the warp has read it), so warps never wait for one
-// another while streaming.  Per chunk a lane reads four 16-byte vectors and
-// takes their maximum; temperature is monotone, so the tempered maximum
-// decides with one compare whether any of the lane's values can still
-// matter.  Only those values are tempered, keyed and offered.
 // Arrivals of first-wave CTAs per SM (counted across launches; consecutive
 // arrivals on an SM take consecutive slots modulo its CTAs in flight).
 __device__ unsigned g_slot_arrivals[256];
+
+// One CTA per row (or per slice of L columns of a split row).  The slice's
+// 16-byte-aligned body is cut into chunks of kChunkBytes; warp w streams
+// chunks w, w + NW, ... through its own ring, each lane copying (cp.async)
+// the four 16-byte vectors it reads and refilling its part of a slot as soon
+// as it has read it, so warps never wait for one another while streaming.
+// Per chunk a lane takes the maximum of its vectors.  List rows (k <= 64)
+// keep only that, as the group maxima of the sketch, and find their list
+// after the stream; argmax and long-list rows compare the tempered maximum
+// with their bound (temperature is monotone) and look at the values of the
+// lanes that reach it.
 
 template <typename T>
 __global__ void __launch_bounds__(kSliceThreads, 3)
