@@ -1205,6 +1205,16 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     }
   }
   cp_async_wait<0>();
+  // The CTA that will most likely take this slot next (one wave of CTAs
+  // later) finds its row's settings in L2: its setup waits on them.
+  if (tid == 0 && !split && A.stagger_ctas > 0) {
+    const int nu = u + A.stagger_ctas;
+    if (nu < A.B1) {
+      prefetch_l2(A.cfg + nu);
+      if (A.hist_off != nullptr) prefetch_l2(A.hist_off + nu);
+      if (A.rng != nullptr) prefetch_l2(A.rng + nu);
+    }
+  }
 
   // long-list rows: the history round after the stream, where the bound is tight
   if (use_block) history_round();
