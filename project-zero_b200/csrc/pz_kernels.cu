@@ -23,7 +23,7 @@
 #include "pz_kernels.cuh"
 #include "pz_select.cuh"
 #include "pz_seqsum.cuh"
-#include "pz_tma.cuh"
+#include "pz_async_copy.cuh"
 #include "pz_warpsel.cuh"
 #include "pz_listmath.cuh"
 

@@ -1,10 +1,7 @@
-// pz_warpsel.cuh — warp-level exact top-k over 64-bit ordered keys.
-//
-// Each warp filters its share of a slice against its own threshold and keeps
-// the survivors in a warp-private shared-memory buffer (ballot appends, no
-// atomics, no block barrier).  When the buffer fills, a bitwise radix select
-// (counts by __reduce_add_sync) finds the exact k-th largest key, the buffer
-// is compacted to the k best and the threshold rises.  Keys are unique per
+// pz_warpsel.cuh — one warp's exact selection over 64-bit ordered keys in
+// shared memory: the k-th largest key (a bitwise radix select, counts by
+// __reduce_add_sync), compaction to the keys at or above it, and a bitonic
+// sort.  Used where a row's slice lists are merged.  Keys are unique per
 // element, so the result is exactly the reference's top-k set.
 #pragma once
 
@@ -65,49 +62,6 @@ __device__ __noinline__ unsigned long long warp_kth(const unsigned long long *ke
   return warp_min_u64(kth);
 }
 
-// The j-th largest (1-based) of R keys per lane held in registers (32*R
-// keys, duplicates allowed: ties count once per copy).  Warp-wide.
-template <int R>
-__device__ __forceinline__ unsigned long long warp_jth_reg(const unsigned long long (&v)[R], int j) {
-  unsigned long long mn = ~0ull, mx = 0ull;
-#pragma unroll
-  for (int r = 0; r < R; r++) {
-    mn = v[r] < mn ? v[r] : mn;
-    mx = v[r] > mx ? v[r] : mx;
-  }
-  mn = warp_min_u64(mn);
-  mx = warp_max_u64(mx);
-  if (mn == mx) return mn;
-  int b = 63 - __clzll(static_cast<long long>(mn ^ mx));
-  unsigned long long mask = b == 63 ? 0ull : (~0ull << (b + 1));
-  unsigned long long prefix = mn & mask;
-  int need = j;
-  for (; b >= 0; b--) {
-    const unsigned long long bit = 1ull << b;
-    int c1 = 0, cm = 0;
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-      const bool m = (v[r] & mask) == prefix;
-      cm += m ? 1 : 0;
-      c1 += (m && (v[r] & bit)) ? 1 : 0;
-    }
-    cm = __reduce_add_sync(0xFFFFFFFFu, cm);
-    if (cm == need) break;  // all keys under this prefix are in: the j-th is their minimum
-    c1 = __reduce_add_sync(0xFFFFFFFFu, c1);
-    if (c1 >= need) {
-      prefix |= bit;
-    } else {
-      need -= c1;
-    }
-    mask |= bit;
-  }
-  unsigned long long kth = ~0ull;
-#pragma unroll
-  for (int r = 0; r < R; r++)
-    if ((v[r] & mask) == prefix && v[r] < kth) kth = v[r];
-  return warp_min_u64(kth);
-}
-
 // Moves the keys >= kth to the front of keys[0..n) in place, keeping their
 // order; returns their number.  Warp-wide.
 __device__ __noinline__ int warp_compact_ge(unsigned long long *keys, int n, unsigned long long kth) {
@@ -124,70 +78,6 @@ __device__ __noinline__ int warp_compact_ge(unsigned long long *keys, int n, uns
     __syncwarp();
   }
   return out;
-}
-
-// Warp-private candidate buffer state (registers, warp-uniform).
-struct WarpCand {
-  unsigned long long *keys;  // shared memory, `cap` slots
-  int cap;
-  int n;
-  unsigned long long tau;    // keys must be > tau to enter
-  float tau_f;               // value part of tau: values below it never enter
-  // Thresholds shared with the other warps of the block (shared memory) and
-  // with the other slices of the row (global): each warp's k-th best key is
-  // a lower bound on the row's k-th best, so the largest one is too.
-  unsigned long long *block_tau;
-  unsigned long long *row_tau;
-};
-
-// Adopts a higher threshold published by another warp or slice.
-__device__ __forceinline__ void warp_adopt(WarpCand &w, unsigned long long t) {
-  if (t > w.tau) {
-    w.tau = t;
-    w.tau_f = key_val(t);
-  }
-}
-
-// Keeps the best k keys of a full buffer and raises its threshold.
-__device__ __noinline__ void warp_make_room(WarpCand &w, int k) {
-  const unsigned long long kth = warp_kth(w.keys, w.n, k);
-  w.n = warp_compact_ge(w.keys, w.n, kth);
-  if (kth > w.tau) {
-    w.tau = kth;
-    w.tau_f = key_val(kth);
-  }
-  if (lane_id() == 0) {
-    if (w.block_tau) atomicMax(w.block_tau, w.tau);
-    if (w.row_tau) atomicMax(w.row_tau, w.tau);
-  }
-  __syncwarp();
-}
-
-// Offers one key per lane (`q` = the lane has a key above tau).  Keeps the
-// buffer exact: when the batch does not fit, selects the best k first.
-__device__ __forceinline__ void warp_offer(WarpCand &w, int k, bool q, unsigned long long key) {
-  uint32_t bal = __ballot_sync(0xFFFFFFFFu, q);
-  if (bal == 0u) return;
-  if (w.n + __popc(bal) > w.cap) {
-    warp_make_room(w, k);
-    q = q && key > w.tau;
-    bal = __ballot_sync(0xFFFFFFFFu, q);
-  }
-  if (q) w.keys[w.n + __popc(bal & lanemask_lt())] = key;
-  w.n += __popc(bal);
-  __syncwarp();
-}
-
-// Reduces the buffer to its best k keys (unordered).
-__device__ __forceinline__ void warp_finish(WarpCand &w, int k) {
-  if (w.n > k) {
-    const unsigned long long kth = warp_kth(w.keys, w.n, k);
-    w.n = warp_compact_ge(w.keys, w.n, kth);
-    if (kth > w.tau) {
-      w.tau = kth;
-      w.tau_f = key_val(kth);
-    }
-  }
 }
 
 // Bitonic sort of a[0..n2) descending (n2 a power of two), one warp.
