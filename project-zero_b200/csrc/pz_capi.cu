@@ -255,7 +255,7 @@ void pz_row_shard(int B, int world, int rank, int *begin, int *count) {
 // slower (a slice's short stream reaches a tight bound too late).  Slices
 // of at least 2048 columns, the split rows' lists within the context's
 // scratch, and S lists of the launch's list length within the merge area
-// (4096 keys).
+// (2048 keys).
 // B200 HBM3e, bytes per ns (measured copy bandwidth), and the fraction of
 // a CTA's life by which the slots of an SM are staggered.
 constexpr double kHbmBytesPerNs = 6400.0;
@@ -264,7 +264,7 @@ constexpr double kStaggerFrac = 0.38;
 static int slice_occupancy(size_t smem) {
   const size_t per_sm = 228 * 1024;
   const int occ = static_cast<int>(per_sm / (smem + 2048));
-  return std::max(1, std::min(occ, 3));
+  return std::max(1, std::min(occ, 4));
 }
 
 static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
@@ -289,7 +289,7 @@ static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
   }
   S = std::min(S, std::max(1, (V + 2047) / 2048));
   S = std::min(S, std::max(1, c->slices_cap / std::max(B - B1, 1)));
-  S = std::min(S, std::max(1, 4096 / std::max(kcap, 1)));
+  S = std::min(S, std::max(1, 2048 / std::max(kcap, 1)));
   S = std::max(S, 1);
   int L = (V + S - 1) / S;
   L = (L + 7) / 8 * 8;
@@ -379,7 +379,8 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     const int occ = slice_occupancy(smem);
     const int slots = ctx->num_sms * occ;
     const double cta_bytes = static_cast<double>(a.S == 1 ? V : a.L) * (dtype == PZ_DTYPE_BF16 ? 2 : 4);
-    const double life_ns = cta_bytes * std::min(slots, B * a.S) / kHbmBytesPerNs;
+    // (measured best: the life at three CTAs per SM, shared by the slots)
+    const double life_ns = cta_bytes * std::min(ctx->num_sms * 3, B * a.S) / kHbmBytesPerNs * 3.0 / occ;
     static const int forced = [] {
       const char *e = std::getenv("PZ_STAGGER_NS");  // tuning override
       return e ? std::atoi(e) : -1;

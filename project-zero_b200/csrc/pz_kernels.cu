@@ -363,7 +363,7 @@ __device__ __forceinline__ void finalize_row(const SliceArgs &A, int row, const 
 // slice_kernel
 // ---------------------------------------------------------------------------
 constexpr int kChunkBytes = 2048;    // one bulk copy: a warp's chunk of the slice
-constexpr int kSlots = 3;            // ring slots per warp (copies in flight per warp)
+constexpr int kSlots = 2;            // ring slots per warp (copies in flight per warp)
 constexpr int kSliceWarps = kSliceThreads / 32;
 constexpr int kLaneVecs = kChunkBytes / 16 / 32;  // 16-byte vectors per lane per chunk
 constexpr uint32_t kHashEmpty = 0xFFFFFFFFu;
@@ -572,7 +572,7 @@ __device__ __noinline__ void radix_pick(const uint32_t *bins, int need, int *bin
 // After the stream the ring holds the row's list (the survivors, or a split
 // row's merged slice lists: up to kMergeKeys keys) and, from kFinalizeOff on,
 // the decision's scratch (values, probabilities, order: 12 bytes a key).
-constexpr int kMergeKeys = 4096;
+constexpr int kMergeKeys = 2048;
 constexpr int kFinalizeOff = kMergeKeys * 8;
 static_assert(kSliceWarps * kSlots * kChunkBytes >= kFinalizeOff + 12 * PZ_TOP_K_MAX + 16,
               "the ring holds the merged lists and the decision's scratch");
@@ -658,21 +658,23 @@ __host__ __device__ inline int slice_cbuf_keys(int kcap) {
   return kcap > kTQK ? kcap + kCapB : 0;
 }
 
-__host__ __device__ inline int slice_hbm_words(int V, int hts) {
-  return hts > 0 ? (V + 127) >> 7 : 0;
+// The bitmap only where there is room for it: in launches of argmax rows
+// (no sketch).  Without it a lookup goes to the table directly.
+__host__ __device__ inline int slice_hbm_words(int V, int hts, int kcap) {
+  return hts > 0 && kcap <= 1 ? (V + 127) >> 7 : 0;
 }
 
 size_t slice_smem_bytes(int kcap, int hts, int nslots, int V, int elem_bytes) {
   const size_t sk = static_cast<size_t>(slice_sketch_entries(V, elem_bytes, kcap));
   return static_cast<size_t>(nslots) * kSliceWarps * kChunkBytes +
          sizeof(unsigned long long) * static_cast<size_t>(slice_cbuf_keys(kcap)) +
-         sizeof(uint32_t) * (2 * static_cast<size_t>(hts) + slice_hbm_words(V, hts)) +
+         sizeof(uint32_t) * (2 * static_cast<size_t>(hts) + slice_hbm_words(V, hts, kcap)) +
          sizeof(uint16_t) * sk + sizeof(uint32_t) * (sk / 32);
 }
 
-// Ring slots per warp: kSlots chunks of 2 KB in flight per warp (48 KB per
-// CTA; with the history table and the sketch, three CTAs fit in an SM's
-// 228 KB).  After the stream the ring holds the list work: the candidates
+// Ring slots per warp: kSlots chunks of 2 KB in flight per warp (32 KB per
+// CTA; with the history table and the sketch, four CTAs fit in an SM's
+// 228 KB, 128 KB of copies in flight per SM).  After the stream the ring holds the list work: the candidates
 // (up to kCCap keys from 8 KB on), the merged slice lists and the
 // decision's scratch (from kFinalizeOff on), or the rescan buffer.
 int slice_stages(int, int) { return kSlots; }
@@ -693,7 +695,7 @@ __device__ unsigned g_slot_arrivals[256];
 // lanes that reach it.
 
 template <typename T>
-__global__ void __launch_bounds__(kSliceThreads, 3)
+__global__ void __launch_bounds__(kSliceThreads, 4)
     slice_kernel(const SliceArgs A) {
   constexpr int NT = kSliceThreads;
   constexpr int NW = kSliceWarps;
@@ -729,8 +731,9 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       reinterpret_cast<unsigned long long *>(smem + static_cast<size_t>(NW) * NS * kChunkBytes);
   uint32_t *hk = reinterpret_cast<uint32_t *>(cbuf + slice_cbuf_keys(A.kcap));
   uint32_t *hn = hk + A.hts;
-  uint32_t *hbm = hn + A.hts;  // one bit per 4 columns of the row
-  uint16_t *sketch = reinterpret_cast<uint16_t *>(hbm + slice_hbm_words(A.V, A.hts));
+  uint32_t *hbm = hn + A.hts;  // one bit per 4 columns of the row (argmax launches)
+  const bool has_hbm = slice_hbm_words(A.V, A.hts, A.kcap) > 0;
+  uint16_t *sketch = reinterpret_cast<uint16_t *>(hbm + slice_hbm_words(A.V, A.hts, A.kcap));
   const int sk_cap = slice_sketch_entries(A.V, static_cast<int>(sizeof(T)), A.kcap);
   uint32_t *gbm = reinterpret_cast<uint32_t *>(sketch + sk_cap);  // one bit per sketch group
   const uint32_t hmask = static_cast<uint32_t>(A.hts - 1);
@@ -873,7 +876,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
       hk[i] = kHashEmpty;
       hn[i] = 0u;
     }
-    for (int i = tid; i < slice_hbm_words(A.V, A.hts); i += NT) hbm[i] = 0u;
+    for (int i = tid; i < slice_hbm_words(A.V, A.hts, A.kcap); i += NT) hbm[i] = 0u;
     if (use_tq)
       for (int i = tid; i < sk_cap / 32; i += NT) gbm[i] = 0u;
   };
@@ -882,7 +885,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
     for (int u = 0; u < IPT; u++)
       if (t[u] >= a && t[u] < b) {
         hash_insert(hk, hn, hmask, hshift, static_cast<uint32_t>(t[u]));
-        atomicOr(&hbm[t[u] >> 7], 1u << ((t[u] >> 2) & 31));
+        if (has_hbm) atomicOr(&hbm[t[u] >> 7], 1u << ((t[u] >> 2) & 31));
         if (use_tq && t[u] >= a_al && t[u] < b_al) {
           // the sketch group of column t: chunk, then the lane of its vector
           constexpr int kPerChunk = kChunkBytes / static_cast<int>(sizeof(T));
@@ -931,7 +934,7 @@ __global__ void __launch_bounds__(kSliceThreads, 3)
   }
   // the bitmap answers most lookups; a set bit sends the id to the table
   auto hist_count = [&](int li) -> int {
-    return hist_on && ((hbm[li >> 7] >> ((li >> 2) & 31)) & 1u) != 0u
+    return hist_on && (!has_hbm || ((hbm[li >> 7] >> ((li >> 2) & 31)) & 1u) != 0u)
                ? hash_count(hk, hn, hmask, hshift, static_cast<uint32_t>(li))
                : 0;
   };
