@@ -259,7 +259,7 @@ void pz_row_shard(int B, int world, int rank, int *begin, int *count) {
 // B200 HBM3e, bytes per ns (measured copy bandwidth), and the fraction of
 // a CTA's life by which the slots of an SM are staggered.
 constexpr double kHbmBytesPerNs = 6400.0;
-constexpr double kStaggerFrac = 0.38;
+constexpr double kStaggerFrac = 0.41;
 
 static int slice_occupancy(size_t smem) {
   const size_t per_sm = 228 * 1024;
