@@ -362,7 +362,7 @@ __device__ __forceinline__ void finalize_row(const SliceArgs &A, int row, const 
 // ---------------------------------------------------------------------------
 // slice_kernel
 // ---------------------------------------------------------------------------
-constexpr int kChunkBytes = 2048;    // one bulk copy: a warp's chunk of the slice
+constexpr int kChunkBytes = 2048;    // a warp's chunk of the slice (16 bytes per lane x 4)
 constexpr int kSlots = 2;            // ring slots per warp (copies in flight per warp)
 constexpr int kSliceWarps = kSliceThreads / 32;
 constexpr int kLaneVecs = kChunkBytes / 16 / 32;  // 16-byte vectors per lane per chunk
@@ -569,9 +569,10 @@ __device__ __noinline__ void radix_pick(const uint32_t *bins, int need, int *bin
   }
 }
 
-// After the stream the ring holds the row's list (the survivors, or a split
-// row's merged slice lists: up to kMergeKeys keys) and, from kFinalizeOff on,
-// the decision's scratch (values, probabilities, order: 12 bytes a key).
+// After the stream the ring holds the row's list work (the candidates and
+// the ranked list, or a split row's merged slice lists: up to kMergeKeys
+// keys) and, from kFinalizeOff on, the decision's scratch (values,
+// probabilities, order: 12 bytes a key).
 constexpr int kMergeKeys = 2048;
 constexpr int kFinalizeOff = kMergeKeys * 8;
 static_assert(kSliceWarps * kSlots * kChunkBytes >= kFinalizeOff + 12 * PZ_TOP_K_MAX + 16,
@@ -649,10 +650,11 @@ __device__ __forceinline__ MergedList merge_slice_lists(const SliceArgs &A, int 
 
 // Shared memory of slice_kernel:
 //   ring   NW x nslots x kChunkBytes  (per-warp copy rings; after the
-//          stream: the queues' survivors and the rare exact rescan)
+//          stream: the list work and the rare exact rescan)
 //   cbuf   block buffer keys           (lists longer than kTQK only)
 //   hash   2 x hts words                (history ids and counts)
-//   hbm    V/128 words                  (one bit per 4 columns: a history id there)
+//   hbm    V/128 words                  (one bit per 4 columns: a history id there;
+//                                        argmax launches only)
 //   sketch 16-bit group maxima of the stream, then one bit per group (list rows)
 __host__ __device__ inline int slice_cbuf_keys(int kcap) {
   return kcap > kTQK ? kcap + kCapB : 0;
@@ -1226,7 +1228,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   const bool timed_out = s_timeout != 0;
 
   // ---- this slice's list -> scratch ---------------------------------------
-  unsigned long long *lst = reinterpret_cast<unsigned long long *>(ring);  // survivors
+  unsigned long long *lst = reinterpret_cast<unsigned long long *>(ring);  // the list
   unsigned long long *rb = use_block ? cbuf : lst;                         // block buffer
   if (use_block) {
     int n = sh.n < cap ? sh.n : cap;
@@ -1242,7 +1244,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   }
   __syncthreads();
   bool exact_rescan = false;
-  int n_tq = 0;  // list length (queue path)
+  int n_tq = 0;  // list length (sketch path)
   if (use_tq) {
     // ---- a list row's list, from the sketch ---------------------------------
     // The bound: the k-th largest sketch value, by a two-pass radix select
@@ -1455,8 +1457,8 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
 
   // The row's list for the decision: this CTA's own (the whole row), or,
   // for a split row, the merge of its S slice lists by whichever of its
-  // CTAs finishes last.  The decision's scratch sits in the ring after the
-  // first 32 KB (the survivors or the merged lists).
+  // CTAs finishes last.  The decision's scratch sits in the ring from
+  // kFinalizeOff on, after the list work or the merged lists.
   float *fe = reinterpret_cast<float *>(ring + kFinalizeOff);
   float *fp = fe + A.kcap;
   int *ford = reinterpret_cast<int *>(fp + A.kcap);
