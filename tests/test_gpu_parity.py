@@ -272,3 +272,36 @@ def test_last_wave_rows_split(cuda, pz, oracle_lib, B):
     again = run_gpu(cuda, pz, d, sampler=s, max_top_k=1, max_history=256)
     assert (again["tokens"] == g["tokens"]).all()
     s.close()
+
+
+def test_sketch_bound_second_pass_and_overflow(cuda, pz, oracle_lib):
+    """The list path's fallbacks.  Rows whose largest logits are all history
+    ids under a strong penalty: the first bound, taken over every group's
+    maximum, is too high once those maxima are penalised, and the second
+    pass (groups without history ids only) must find the list.  Rows of
+    equal values: every group reaches the bound, the candidates overflow,
+    and the slice is redone exactly with the block-wide buffer."""
+    rs = np.random.default_rng(23)
+    B, V, n_top = 8, 50000, 80
+    for dtype in ("f32", "bf16"):
+        x = (rs.standard_normal((B, V)) * 1.0).astype(np.float32)
+        hist, off = [], [0]
+        for r in range(B):
+            if r < 4:
+                top = rs.choice(V, n_top, replace=False)
+                x[r, top] = 12.0 + rs.random(n_top).astype(np.float32)
+                hist += [int(t) for t in top]
+            else:
+                x[r, :] = np.float32(0.5) if r % 2 else np.float32(-1.25)
+                hist += [7, 11]
+            off.append(len(hist))
+        logits = synth.to_bf16_bits(x) if dtype == "bf16" else x
+        for k, p_ in [(50, 0.9), (8, 1.0)]:
+            cfg = cases.configs(B, temperature=0.9, top_k=k, top_p=p_, rep=4.0, freq=0.5)
+            d = dict(logits=logits, cfg=cfg, rng=np.arange(5, 5 + B, dtype=np.uint64),
+                     hist=np.array(hist, dtype=np.int32), hist_off=np.array(off, dtype=np.int32))
+            g = run_gpu(cuda, pz, d, max_top_k=64, max_history=128)
+            tok, *_ = oracle_lib.sample_batch(d["logits"], d["cfg"], d["rng"], d["hist"], d["hist_off"])
+            assert (g["tokens"] == tok).all(), (dtype, k)
+            mism, _, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+            assert mism == 0, (dtype, k)
