@@ -261,9 +261,12 @@ void pz_row_shard(int B, int world, int rank, int *begin, int *count) {
 constexpr double kHbmBytesPerNs = 6400.0;
 constexpr double kStaggerFrac = 0.41;
 
+// CTAs of slice_kernel per SM: its shared memory (dynamic, plus its static
+// 1.3 KB and the 1 KB the hardware reserves per CTA) against the SM's 228 KB;
+// its registers (64 a thread) allow four.
 static int slice_occupancy(size_t smem) {
   const size_t per_sm = 228 * 1024;
-  const int occ = static_cast<int>(per_sm / (smem + 2048));
+  const int occ = static_cast<int>(per_sm / (smem + 2304));
   return std::max(1, std::min(occ, 4));
 }
 
