@@ -2,7 +2,8 @@
 
 For list rows (k <= 64) slice_kernel keeps only a sketch of the stream: per
 group of 4 lanes' vectors (64 f32 elements: 16 contiguous columns at each of
-4 places 128 columns apart in a 512-column chunk) the top 16 bits of the
+4 places 128 columns apart in a 512-column chunk; 128 bf16 elements in a
+1024-column chunk) the top 16 bits of the
 ordered value of the group's largest raw logit.  The bound is the k-th
 largest sketch value (k + 8 in a first pass when the row has history ids);
 `tb`, its tempered floor.  Candidates are the elements at or above `tb` of
@@ -52,15 +53,17 @@ def penalize(x, c, rep, freq, pres):
     return (v - F32(pen)).astype(F32)
 
 
-def groups_of(V):
-    """Column lists of the sketch groups of an f32 row starting 16-byte aligned."""
+def groups_of(V, vec=4):
+    """Column lists of the sketch groups of a row starting 16-byte aligned
+    (vec = 4 f32 or 8 bf16 values per 16-byte vector; a chunk is 2 KB)."""
     out = []
-    for c in range((V * 4 + 2047) // 2048):
+    per_chunk = 2048 // (16 // vec)
+    for c in range((V + per_chunk - 1) // per_chunk):
         for p in range(8):
             cols = []
             for u in range(4):
-                base = c * 512 + (u * 32 + 4 * p) * 4
-                cols.extend(range(base, base + 16))
+                base = c * per_chunk + (u * 32 + 4 * p) * vec
+                cols.extend(range(base, base + 4 * vec))
             cols = [j for j in cols if j < V]
             out.append(np.array(cols, dtype=np.int64))
     return out
@@ -71,11 +74,11 @@ def kth_largest(vals, k):
     return int(vals[k - 1]) if len(vals) >= k else 0
 
 
-def candidates(x, k, hist, T, divide, rep, freq, pres):
+def candidates(x, k, hist, T, divide, rep, freq, pres, vec=4):
     """The list path's candidate columns for one row (None: overflow, the
     device redoes the slice exactly)."""
     V = len(x)
-    grp = groups_of(V)
+    grp = groups_of(V, vec)
     counts = {}
     for h in hist:
         counts[int(h)] = counts.get(int(h), 0) + 1
@@ -158,12 +161,24 @@ def make_row(rs, V, kind):
 KINDS = ["plain", "boosted", "ties", "negative", "nan", "crowded"]
 
 
+def to_bf16_values(x):
+    """bf16 logits as the kernel widens them (round to nearest even)."""
+    u = x.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) & 0xFFFF
+    r = np.where(np.isnan(x), 0x7FC0, r).astype(np.uint32)
+    return (r << 16).astype(np.uint32).view(F32)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("kind", KINDS)
-def test_exact_list_is_among_candidates(kind):
-    rs = np.random.default_rng(100 + KINDS.index(kind))
+def test_exact_list_is_among_candidates(kind, dtype):
+    rs = np.random.default_rng(100 + KINDS.index(kind) + (50 if dtype == "bf16" else 0))
     V = 5000
+    vec = 4 if dtype == "f32" else 8
     for trial in range(12):
         x = make_row(rs, V, kind)
+        if dtype == "bf16":
+            x = to_bf16_values(x)
         k = int(rs.choice([2, 8, 50, 64]))
         T = float(rs.choice([0.3, 0.7, 1.5]))
         divide = bool(trial % 2)
@@ -174,7 +189,7 @@ def test_exact_list_is_among_candidates(kind):
             top = np.argsort(-np.nan_to_num(x, nan=-np.inf))[:80]
             hist = list(rs.choice(V, 60)) + list(top[: 40 if mode == 1 else 10])
             rep, freq, pres = (3.0, 0.5, 0.2) if mode == 1 else (0.8, 0.0, -0.5)
-        cand = candidates(x, k, hist, T, divide, rep, freq, pres)
+        cand = candidates(x, k, hist, T, divide, rep, freq, pres, vec)
         if cand is None:
             continue  # overflow: the device redoes the slice exactly
         want = exact_topk(x, k, hist, T, divide, rep, freq, pres)
