@@ -131,8 +131,9 @@ float pz_rng_float(unsigned long long *state);
 
 /* Full-softmax draw of the reference's generate loop
  * (src/transformer/generate.c:157-168): softmax over the whole row, then the
- * CDF walk in index order; fallback V-1.  `logits` is overwritten with the
- * probabilities, as tn_softmax does in the reference. */
+ * CDF walk in index order; fallback V-1.  `logits` is read, not modified
+ * (the reference's tn_softmax leaves the probabilities in the buffer; no
+ * caller reads them after the draw). */
 int pz_sample_softmax(float *logits, int vocab_size,
                       unsigned long long *rng_state);
 
@@ -269,6 +270,11 @@ pz_status pz_sample_batch_static(const void *logits, pz_dtype dtype, int B,
 pz_status pz_ctx_profile(pz_sampler_ctx *ctx, int n_calls);
 pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms,
                               double *rest_ms, int *calls, int *kernels);
+/* The same timing split by phase: phase_ms[0] slice_kernel, [1] the
+ * full-vocabulary pass (full_kernel), [2] the vocab-sharded allgather,
+ * [3] merge_kernel; summed over the timed calls.  Starts a new count. */
+pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double phase_ms[4],
+                                int *calls, int *kernels);
 
 /* Seeds B RNG states on the device: state[r] = seed_base + r (0 -> 1, as
  * rng_seed does), or state[r] = seeds[r] when `seeds` (device) is non-NULL. */
@@ -294,8 +300,26 @@ void pz_row_shard(int B, int world, int rank, int *begin, int *count);
  * get token -1 and PZ_ROW_HINT_VIOLATED.  Greedy rows take the global
  * argmax. */
 pz_status pz_nccl_get_unique_id(void *id_out, size_t id_bytes);
+/* Joins the context to a communicator of `world` ranks.  The communicator
+ * is non-blocking: its set-up and every allgather are polled against a
+ * deadline of timeout_ms (60 s for pz_ctx_init_nccl).  A rank that never
+ * joins, or an NCCL error, makes the call abort the communicator and return
+ * PZ_ERR_TIMEOUT / PZ_ERR_NCCL instead of waiting for ever; later sharded
+ * calls on the context then fail with PZ_ERR_NCCL. */
 pz_status pz_ctx_init_nccl(pz_sampler_ctx *ctx, int world, int rank,
                            const void *unique_id, size_t id_bytes);
+pz_status pz_ctx_init_nccl_timeout(pz_sampler_ctx *ctx, int world, int rank,
+                                   const void *unique_id, size_t id_bytes,
+                                   int timeout_ms);
+/* Waits at most timeout_ms for the work queued on `stream` (a sharded
+ * call's allgather included).  Polls the communicator's asynchronous error
+ * meanwhile: an NCCL error gives PZ_ERR_NCCL, and the deadline
+ * PZ_ERR_TIMEOUT; either way the communicator is aborted, which ends its
+ * collectives still in flight.  PZ_OK once the stream is idle. */
+pz_status pz_ctx_wait(pz_sampler_ctx *ctx, void *stream, int timeout_ms);
+/* Aborts the context's communicator (for a caller that learned from
+ * elsewhere, e.g. a heartbeat, that a peer has gone). */
+pz_status pz_ctx_abort_nccl(pz_sampler_ctx *ctx);
 pz_status pz_sample_batch_vocab_sharded(
     pz_sampler_ctx *ctx, const void *logits_slice, pz_dtype dtype, int B,
     int V_local, int64_t ld, int64_t v_offset, int V_global,

@@ -21,6 +21,10 @@ import subprocess
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+# The reference checkout: PZ_REFERENCE, else a directory named `reference`
+# beside this repository.
+REFERENCE_DIR = os.environ.get("PZ_REFERENCE") or os.path.join(
+    os.path.dirname(os.path.dirname(HERE)), "reference")
 ORACLE_SO = os.path.join(HERE, "libpzoracle.so")
 REF_DIR = os.path.join(HERE, "_ref")
 
@@ -77,12 +81,9 @@ def build(ref: bool = True) -> None:
     """Builds the restatement (always) and the reference library (when the
     reference tree is present)."""
     targets = ["oracle"]
-    if ref and os.path.isdir(os.environ.get("PZ_REFERENCE", "/root/reference")):
+    if ref and os.path.isdir(REFERENCE_DIR):
         targets.append("ref")
-    env = dict(os.environ)
-    if "PZ_REFERENCE" in env:
-        env["REF"] = env["PZ_REFERENCE"]
-    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True, env=env)
+    subprocess.run(["make", "-s", "-C", HERE, f"PZ_REFERENCE={REFERENCE_DIR}"] + targets, check=True)
 
 
 def _ptr(a, t):
@@ -166,6 +167,10 @@ class Oracle(_Lib):
                                        ctypes.c_int64, ctypes.c_void_p, _i32p, _i32p, _u64p, _i32p,
                                        _i32p, _f32p, _i32p, ctypes.c_int]
         L.pzo_sample_batch.restype = ctypes.c_int
+        L.pzo_row_trace.argtypes = [_f32p, ctypes.c_int, ctypes.c_void_p, _i32p, ctypes.c_int, ctypes.c_uint64,
+                                    _f32p, _i32p, _f32p, ctypes.POINTER(ctypes.c_int),
+                                    ctypes.POINTER(ctypes.c_int32)]
+        L.pzo_row_trace.restype = ctypes.c_int
 
     def apply_temperature(self, x, T, divide=False):
         x = np.array(x, dtype=np.float32, copy=True)
@@ -178,6 +183,30 @@ class Oracle(_Lib):
         self.lib.pzo_apply_penalties(_ptr(x, _f32p), x.size, _ptr(h, _i32p), h.size,
                                      ctypes.c_float(rep), ctypes.c_float(freq), ctypes.c_float(pres))
         return x
+
+    def row_trace(self, row, cfg_row, rng, hist=None):
+        """The draw of one pipeline row, traced (pzo_row_trace): returns
+        (token, r, order, cdf, fallback) where order/cdf are the walk's ids
+        and running float CDF (empty when the row draws nothing), r the draw
+        as compared with the CDF and fallback the id taken past its end.
+        row: [V] float32 or uint16 (bf16 bits); rng: the state before."""
+        row = np.ascontiguousarray(row)
+        if row.dtype == np.uint16:
+            row = (row.astype(np.uint32) << np.uint32(16)).view(np.float32)
+        row = np.ascontiguousarray(row, dtype=np.float32)
+        V = row.size
+        cfg = np.ascontiguousarray(np.asarray(cfg_row, dtype=CONFIG_DTYPE).reshape(1))
+        h = np.ascontiguousarray(hist, dtype=np.int32) if hist is not None else np.zeros(0, np.int32)
+        order = np.zeros(V, dtype=np.int32)
+        cdf = np.zeros(V, dtype=np.float32)
+        r = ctypes.c_float(0.0)
+        n = ctypes.c_int(0)
+        fb = ctypes.c_int32(-1)
+        tok = self.lib.pzo_row_trace(_ptr(row, _f32p), V, cfg.ctypes.data, _ptr(h, _i32p), h.size,
+                                     ctypes.c_uint64(int(rng)), ctypes.byref(r), _ptr(order, _i32p),
+                                     _ptr(cdf, _f32p), ctypes.byref(n), ctypes.byref(fb))
+        k = n.value
+        return int(tok), float(np.float32(r.value)), order[:k].copy(), cdf[:k].copy(), int(fb.value)
 
     def sample_batch(self, logits, cfg, rng, hist=None, hist_off=None, cand_stride=0):
         """logits: [B, V] float32 or uint16 (bf16 bits).  Returns

@@ -309,3 +309,154 @@ int pzo_sample_batch(const void *logits, int dtype, int B, int V, int64_t ld,
   free(x);
   return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Draw trace of one pipeline row (test support for boundary cases).
+ *
+ * Runs the same steps as pzo_sample_row and records the walk the draw makes:
+ * order[j] is the id at walk position j, cdf[j] the running float sum the
+ * reference compares the draw with at that position (top_p.c:96-105,
+ * top_k.c:62-70, generate.c:159-167), r the draw as compared (u * trunc_sum
+ * for top-p, u otherwise), and *fallback the id taken when r reaches past
+ * the last position.  *n_walk is the number of positions (0: no draw, the
+ * token comes from argmax).  order and cdf hold at least V entries.
+ * Returns the sampled id. */
+static int walk_list(const float *probs, const int32_t *ids, int n, float r,
+                     int32_t *order, float *cdf, int *n_walk) {
+  float c = 0.0f;
+  int res = -1;
+  for (int i = 0; i < n; i++) {
+    c += probs[i];
+    order[i] = ids[i];
+    cdf[i] = c;
+    if (res < 0 && r < c) res = ids[i];
+  }
+  *n_walk = n;
+  return res;
+}
+
+int pzo_row_trace(const float *x_in, int V, const pz_sampler_config *cfg,
+                  const int32_t *hist, int H, uint64_t rng, float *r_out,
+                  int32_t *order, float *cdf, int *n_walk, int32_t *fallback) {
+  float *x = (float *)malloc((size_t)V * sizeof(float));
+  if (!x) abort();
+  memcpy(x, x_in, (size_t)V * sizeof(float));
+  *n_walk = 0;
+  *r_out = 0.0f;
+  *fallback = -1;
+  int tok = -1;
+  const float rep = cfg->repetition_penalty, freq = cfg->frequency_penalty,
+              pres = cfg->presence_penalty;
+  if (H > 0 && (rep != 1.0f || freq != 0.0f || pres != 0.0f))
+    pzc_apply_penalties(x, V, hist, H, rep, freq, pres);
+  const float T = cfg->temperature;
+  if (T <= 0.0f || T < 1e-6f) {
+    tok = pzo_sample_argmax(x, V);
+    free(x);
+    return tok;
+  }
+  pzo_apply_temperature(x, V, T, (cfg->flags & PZ_CFG_TEMP_DIVIDE) != 0);
+  const int keff = pzc_k_eff(cfg->top_k, V);
+  const float p = cfg->top_p;
+  const int p_on = (p < 1.0f && p > 0.0f);
+  float *vals = x; /* the array the top-p steps run over */
+  int n_vals = V;
+  int32_t *ids = (int32_t *)malloc((size_t)V * sizeof(int32_t));
+  float *lv = (float *)malloc((size_t)V * sizeof(float));
+  prob_index *c = (prob_index *)malloc((size_t)V * sizeof *c);
+  prob_index *tmp = (prob_index *)malloc((size_t)V * sizeof *tmp);
+  float *pr = (float *)malloc((size_t)V * sizeof(float));
+  if (!ids || !lv || !c || !tmp || !pr) abort();
+  if (keff > 0) {
+    pzc_select_top_k(x, V, keff, lv, ids);
+    vals = lv;
+    n_vals = keff;
+  } else {
+    for (int i = 0; i < V; i++) ids[i] = i;
+  }
+  if (keff == 0 && !p_on) {
+    /* softmax over the row, CDF walk in index order, fallback V-1 */
+    float mx = x[0];
+    for (int i = 1; i < V; i++)
+      if (x[i] > mx) mx = x[i];
+    float sum = 0.0f;
+    for (int i = 0; i < V; i++) {
+      x[i] = expf(x[i] - mx);
+      sum += x[i];
+    }
+    const float inv = 1.0f / sum;
+    for (int i = 0; i < V; i++) x[i] *= inv;
+    const float r = pzo_rng_float(&rng);
+    *r_out = r;
+    *fallback = V - 1;
+    tok = walk_list(x, ids, V, r, order, cdf, n_walk);
+    if (tok < 0) tok = V - 1;
+  } else if (keff > 0 && !p_on) {
+    /* top_k.c:50-72 over the list, fallback indices[0] */
+    const float mx = vals[0];
+    float sum = 0.0f;
+    for (int i = 0; i < keff; i++) {
+      vals[i] = expf(vals[i] - mx);
+      sum += vals[i];
+    }
+    for (int i = 0; i < keff; i++) vals[i] /= sum;
+    const float r = pzo_rng_float(&rng);
+    *r_out = r;
+    *fallback = ids[0];
+    tok = walk_list(vals, ids, keff, r, order, cdf, n_walk);
+    if (tok < 0) tok = ids[0];
+  } else if (keff == 0 && V > 200000) {
+    tok = pzo_sample_argmax(x, V); /* top_p.c:33-34 */
+  } else {
+    /* top_p.c:37-105 over vals[0..n_vals) */
+    float mx = vals[0];
+    for (int i = 1; i < n_vals; i++)
+      if (vals[i] > mx) mx = vals[i];
+    const float thr = mx - 20.0f;
+    int n = 0;
+    float sum = 0.0f;
+    for (int i = 0; i < n_vals; i++) {
+      if (vals[i] >= thr) {
+        const float e = expf(vals[i] - mx);
+        c[n].prob = e;
+        c[n].index = ids[i];
+        sum += e;
+        n++;
+      }
+    }
+    if (n == 0) {
+      tok = ids[pzo_sample_argmax(vals, n_vals)];
+    } else {
+      const float inv = 1.0f / sum;
+      for (int i = 0; i < n; i++) c[i].prob *= inv;
+      stable_sort_desc(c, n, tmp);
+      float cum = 0.0f;
+      int cutoff = n;
+      for (int i = 0; i < n; i++) {
+        cum += c[i].prob;
+        if (cum >= p) {
+          cutoff = i + 1;
+          break;
+        }
+      }
+      float trunc = 0.0f;
+      for (int i = 0; i < cutoff; i++) trunc += c[i].prob;
+      const float r = pzo_rng_float(&rng) * trunc;
+      *r_out = r;
+      *fallback = c[0].index;
+      for (int i = 0; i < cutoff; i++) {
+        pr[i] = c[i].prob;
+        ids[i] = c[i].index;
+      }
+      tok = walk_list(pr, ids, cutoff, r, order, cdf, n_walk);
+      if (tok < 0) tok = c[0].index;
+    }
+  }
+  free(x);
+  free(ids);
+  free(lv);
+  free(c);
+  free(tmp);
+  free(pr);
+  return tok;
+}

@@ -55,6 +55,13 @@ int pzo_sample_batch(const void *logits, int dtype, int B, int V, int64_t ld,
                      int32_t *cand_ids, float *cand_probs, int32_t *n_cand,
                      int cand_stride);
 
+/* The draw of one pipeline row, traced: walk order, running CDF, the draw
+ * as compared, and the fallback id (see pz_oracle.c).  x_in is not
+ * modified; `rng` is the row's state before the call. */
+int pzo_row_trace(const float *x_in, int V, const pz_sampler_config *cfg,
+                  const int32_t *hist, int H, uint64_t rng, float *r_out,
+                  int32_t *order, float *cdf, int *n_walk, int32_t *fallback);
+
 /* Penalty stage alone (A8), exposed for tests: applies the contract to x. */
 void pzo_apply_penalties(float *x, int V, const int32_t *hist, int H,
                          float rep, float freq, float pres);

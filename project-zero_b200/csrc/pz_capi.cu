@@ -7,10 +7,12 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "../../include/pz_sampling.h"
@@ -50,26 +52,50 @@ int next_pow2(int x) {
 }
 
 // Restores the caller's current device on scope exit.
+// (No device switch at all when the device is already current, so calls
+// made during stream capture stay capture-safe.)
 struct DeviceGuard {
   int prev = -1;
   bool ok = false;
+  bool switched = false;
   explicit DeviceGuard(int dev) {
     if (cudaGetDevice(&prev) != cudaSuccess) return;
-    ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
+    if (prev == dev) {
+      ok = true;
+      return;
+    }
+    ok = switched = (cudaSetDevice(dev) == cudaSuccess);
   }
   ~DeviceGuard() {
-    if (prev >= 0) cudaSetDevice(prev);
+    if (switched) cudaSetDevice(prev);
   }
 };
+
+// ---- kernel attributes, once per device ------------------------------------
+// cudaFuncSetAttribute applies to the device that is current when it is
+// called, so every device that runs the kernels needs its own call.
+constexpr int kMaxDevices = 64;
+std::mutex g_attr_mu;
+bool g_attr_done[kMaxDevices];
+
+cudaError_t ensure_kernel_attributes(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  if (g_attr_done[dev]) return cudaSuccess;
+  const cudaError_t e = pz::set_kernel_attributes();
+  if (e == cudaSuccess) g_attr_done[dev] = true;
+  return e;
+}
 
 // ---- NCCL, loaded at run time (the process may already hold torch's) ----
 struct NcclApi {
   bool loaded = false;
   void *h = nullptr;
   ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
-  ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *) = nullptr;
   ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t,
                             ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
@@ -90,8 +116,9 @@ bool load_nccl() {
   g_nccl.field = reinterpret_cast<decltype(g_nccl.field)>(dlsym(g_nccl.h, name)); \
   if (!g_nccl.field) return false;
   PZ_SYM(GetUniqueId, "ncclGetUniqueId")
-  PZ_SYM(CommInitRank, "ncclCommInitRank")
+  PZ_SYM(CommInitRankConfig, "ncclCommInitRankConfig")
   PZ_SYM(AllGather, "ncclAllGather")
+  PZ_SYM(CommFinalize, "ncclCommFinalize")
   PZ_SYM(CommDestroy, "ncclCommDestroy")
   PZ_SYM(CommAbort, "ncclCommAbort")
   PZ_SYM(CommGetAsyncError, "ncclCommGetAsyncError")
@@ -126,9 +153,12 @@ struct pz_sampler_ctx {
   // vocab sharding
   ncclComm_t comm = nullptr;
   int world = 1, rank = 0;
+  int nccl_timeout_ms = 60000;
+  bool comm_failed = false;  // aborted after a timeout or an asynchronous error
   unsigned long long *emit = nullptr;
   unsigned long long *gathered = nullptr;
-  // kernel timing: three events per call (start, after slice_kernel, end)
+  // kernel timing: kProfEvents events per call, bracketing its phases
+  // (slice_kernel, full_kernel, the allgather, merge_kernel)
   std::vector<cudaEvent_t> prof;
   int prof_used = 0;
   int prof_kernels = 0;
@@ -154,6 +184,48 @@ struct pz_sampler_ctx {
     prof.clear();
   }
 };
+
+namespace {
+
+double now_ms() {
+  return std::chrono::duration<double, std::milli>(
+             std::chrono::steady_clock::now().time_since_epoch())
+      .count();
+}
+
+// Aborts the context's communicator (it is unusable afterwards).
+void abort_comm(pz_sampler_ctx *ctx) {
+  if (ctx->comm && g_nccl.loaded) g_nccl.CommAbort(ctx->comm);
+  ctx->comm = nullptr;
+  ctx->comm_failed = true;
+}
+
+// Waits, by polling the communicator's asynchronous error, until a
+// non-blocking NCCL call that returned `r` has finished.  Past the
+// context's deadline the communicator is aborted and PZ_ERR_TIMEOUT comes
+// back; an NCCL error aborts it too.
+pz_status nccl_settle(pz_sampler_ctx *ctx, ncclResult_t r, double t0) {
+  while (r == ncclInProgress) {
+    if (now_ms() - t0 > ctx->nccl_timeout_ms) {
+      abort_comm(ctx);
+      g_last_error = PZ_ERR_TIMEOUT;
+      std::snprintf(g_detail, sizeof g_detail, "NCCL call unfinished after %d ms; communicator aborted",
+                    ctx->nccl_timeout_ms);
+      return PZ_ERR_TIMEOUT;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    if (g_nccl.CommGetAsyncError(ctx->comm, &r) != ncclSuccess) r = ncclSystemError;
+  }
+  if (r != ncclSuccess) {
+    abort_comm(ctx);
+    g_last_error = PZ_ERR_NCCL;
+    std::snprintf(g_detail, sizeof g_detail, "NCCL error %d; communicator aborted", static_cast<int>(r));
+    return PZ_ERR_NCCL;
+  }
+  return PZ_OK;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -190,9 +262,7 @@ pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
   if (device < 0 || device >= ndev) return fail(PZ_ERR_INVALID_ARGS);
   DeviceGuard g(device);
   if (!g.ok) return fail(PZ_ERR_CUDA);
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] { attr_err = pz::set_kernel_attributes(); });
+  const cudaError_t attr_err = ensure_kernel_attributes(device);
   if (attr_err != cudaSuccess) return fail_cuda(attr_err);
 
   pz_sampler_ctx *c = new pz_sampler_ctx();
@@ -223,8 +293,19 @@ pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
 pz_status pz_ctx_destroy(pz_sampler_ctx *ctx) {
   if (!ctx) return PZ_OK;
   DeviceGuard g(ctx->device);
+  if (ctx->comm && g_nccl.loaded) {
+    // The communicator is non-blocking: finalize it (flushes its pending
+    // collectives) within the deadline, else abort it; then free it.
+    const double t0 = now_ms();
+    ncclResult_t r = g_nccl.CommFinalize(ctx->comm);
+    if (r == ncclSuccess || r == ncclInProgress) {
+      if (nccl_settle(ctx, r, t0) == PZ_OK) g_nccl.CommDestroy(ctx->comm);
+    } else {
+      g_nccl.CommAbort(ctx->comm);
+    }
+    ctx->comm = nullptr;
+  }
   cudaDeviceSynchronize();
-  if (ctx->comm && g_nccl.loaded) g_nccl.CommDestroy(ctx->comm);
   ctx->release();
   delete ctx;
   return PZ_OK;
@@ -303,6 +384,23 @@ static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
   *L_out = L;
 }
 
+// Events per profiled call: start, after slice_kernel, after full_kernel,
+// after the allgather, end (after merge_kernel).  Phases a call does not
+// have are recorded back to back and time as zero.
+constexpr int kProfEvents = 5;
+
+// The next profiling slot of the context (nullptr when timing is off or
+// its slots are used up).
+static cudaEvent_t *next_prof_slot(pz_sampler_ctx *ctx) {
+  if ((ctx->prof_used + 1) * kProfEvents > static_cast<int>(ctx->prof.size())) return nullptr;
+  cudaEvent_t *ev = &ctx->prof[ctx->prof_used * kProfEvents];
+  ctx->prof_used++;
+  return ev;
+}
+
+// ev_out: when not null, the call's profiling slot is handed back with its
+// events 0..2 recorded and 3..4 left to the caller (vocab sharding records
+// them around its allgather and merge).
 static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
                              pz_dtype dtype, int B, int V, int64_t ld,
                              int64_t v_offset, int V_global,
@@ -311,7 +409,8 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
                              unsigned long long *rng_state, int32_t *out,
                              const pz_batch_hints *hints,
                              const pz_batch_outputs *outputs, void *stream,
-                             bool emit) {
+                             bool emit, cudaEvent_t **ev_out = nullptr) {
+  if (ev_out) *ev_out = nullptr;
   if (!ctx || !logits || !cfg || B < 0 || V <= 0 || ld < V) return fail(PZ_ERR_INVALID_ARGS);
   if (dtype != PZ_DTYPE_F32 && dtype != PZ_DTYPE_BF16) return fail(PZ_ERR_INVALID_ARGS);
   if (!emit && (!rng_state || !out)) return fail(PZ_ERR_INVALID_ARGS);
@@ -395,12 +494,8 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   const bool full_pass = !emit && !no_full;
   if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t), st) != cudaSuccess)
     return fail(PZ_ERR_CUDA);
-  cudaEvent_t *ev = nullptr;
-  if (ctx->prof_used * 3 + 3 <= static_cast<int>(ctx->prof.size())) {
-    ev = &ctx->prof[ctx->prof_used * 3];
-    ctx->prof_used++;
-    cudaEventRecord(ev[0], st);
-  }
+  cudaEvent_t *ev = next_prof_slot(ctx);
+  if (ev) cudaEventRecord(ev[0], st);
   cudaError_t ce = pz::launch_slice(a, dtype, smem, st);
   if (ce != cudaSuccess) return fail_cuda(ce);
   if (ev) cudaEventRecord(ev[1], st);
@@ -434,6 +529,12 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   if (ev) {
     cudaEventRecord(ev[2], st);
     ctx->prof_kernels += kernels;
+    if (ev_out) {
+      *ev_out = ev;
+    } else {
+      cudaEventRecord(ev[3], st);
+      cudaEventRecord(ev[4], st);
+    }
   }
   return PZ_OK;
 }
@@ -502,7 +603,7 @@ pz_status static_scratch(int dev, unsigned char **base, int *num_sms) {
       void *q = nullptr;
       cudaError_t e = cudaGetSymbolAddress(&q, g_static_scratch);
       if (e != cudaSuccess) return fail_cuda(e);
-      e = pz::set_kernel_attributes();
+      e = ensure_kernel_attributes(dev);
       if (e != cudaSuccess) return fail_cuda(e);
       int sms = 0;
       e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -573,7 +674,7 @@ pz_status pz_ctx_profile(pz_sampler_ctx *ctx, int n_calls) {
   ctx->prof.clear();
   ctx->prof_used = 0;
   ctx->prof_kernels = 0;
-  for (int i = 0; i < 3 * n_calls; i++) {
+  for (int i = 0; i < kProfEvents * n_calls; i++) {
     cudaEvent_t e;
     const cudaError_t ce = cudaEventCreate(&e);
     if (ce != cudaSuccess) return fail_cuda(ce);
@@ -582,30 +683,39 @@ pz_status pz_ctx_profile(pz_sampler_ctx *ctx, int n_calls) {
   return PZ_OK;
 }
 
-pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms, double *rest_ms,
-                              int *calls, int *kernels) {
+pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double *phase_ms, int *calls,
+                                int *kernels) {
   if (!ctx) return fail(PZ_ERR_INVALID_ARGS);
   DeviceGuard g(ctx->device);
   if (!g.ok) return fail(PZ_ERR_CUDA);
-  double s1 = 0.0, s2 = 0.0;
+  double sum[kProfEvents - 1] = {0.0, 0.0, 0.0, 0.0};
   for (int i = 0; i < ctx->prof_used; i++) {
-    cudaEvent_t *ev = &ctx->prof[i * 3];
-    cudaError_t ce = cudaEventSynchronize(ev[2]);
+    cudaEvent_t *ev = &ctx->prof[i * kProfEvents];
+    cudaError_t ce = cudaEventSynchronize(ev[kProfEvents - 1]);
     if (ce != cudaSuccess) return fail_cuda(ce);
-    float t1 = 0.0f, t2 = 0.0f;
-    ce = cudaEventElapsedTime(&t1, ev[0], ev[1]);
-    if (ce != cudaSuccess) return fail_cuda(ce);
-    ce = cudaEventElapsedTime(&t2, ev[1], ev[2]);
-    if (ce != cudaSuccess) return fail_cuda(ce);
-    s1 += t1;
-    s2 += t2;
+    for (int j = 0; j + 1 < kProfEvents; j++) {
+      float t = 0.0f;
+      ce = cudaEventElapsedTime(&t, ev[j], ev[j + 1]);
+      if (ce != cudaSuccess) return fail_cuda(ce);
+      sum[j] += t;
+    }
   }
-  if (slice_ms) *slice_ms = s1;
-  if (rest_ms) *rest_ms = s2;
+  if (phase_ms)
+    for (int j = 0; j + 1 < kProfEvents; j++) phase_ms[j] = sum[j];
   if (calls) *calls = ctx->prof_used;
   if (kernels) *kernels = ctx->prof_kernels;
   ctx->prof_used = 0;
   ctx->prof_kernels = 0;
+  return PZ_OK;
+}
+
+pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms, double *rest_ms,
+                              int *calls, int *kernels) {
+  double ph[kProfEvents - 1];
+  const pz_status s = pz_ctx_profile_phases(ctx, ph, calls, kernels);
+  if (s != PZ_OK) return s;
+  if (slice_ms) *slice_ms = ph[0];
+  if (rest_ms) *rest_ms = ph[1] + ph[2] + ph[3];
   return PZ_OK;
 }
 
@@ -632,10 +742,11 @@ pz_status pz_nccl_get_unique_id(void *id_out, size_t id_bytes) {
   return PZ_OK;
 }
 
-pz_status pz_ctx_init_nccl(pz_sampler_ctx *ctx, int world, int rank,
-                           const void *unique_id, size_t id_bytes) {
+pz_status pz_ctx_init_nccl_timeout(pz_sampler_ctx *ctx, int world, int rank,
+                                   const void *unique_id, size_t id_bytes,
+                                   int timeout_ms) {
   if (!ctx || !unique_id || id_bytes < sizeof(ncclUniqueId) || world < 1 ||
-      rank < 0 || rank >= world)
+      rank < 0 || rank >= world || timeout_ms <= 0 || ctx->comm)
     return fail(PZ_ERR_INVALID_ARGS);
   if (!load_nccl()) return fail(PZ_ERR_NCCL);
   DeviceGuard g(ctx->device);
@@ -645,11 +756,69 @@ pz_status pz_ctx_init_nccl(pz_sampler_ctx *ctx, int world, int rank,
   if (!ctx->gathered && !ctx->alloc(&ctx->gathered, per_rank * world)) return fail(PZ_ERR_OOM);
   ncclUniqueId id;
   std::memcpy(&id, unique_id, sizeof id);
+  // Non-blocking communicator: init and every collective return at once,
+  // and their progress is polled against the deadline.
+  ncclConfig_t conf = NCCL_CONFIG_INITIALIZER;
+  conf.blocking = 0;
   ncclComm_t comm = nullptr;
-  if (g_nccl.CommInitRank(&comm, world, id, rank) != ncclSuccess) return fail(PZ_ERR_NCCL);
+  ctx->nccl_timeout_ms = timeout_ms;
+  ctx->comm_failed = false;
+  const double t0 = now_ms();
+  const ncclResult_t r = g_nccl.CommInitRankConfig(&comm, world, id, rank, &conf);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    if (comm) g_nccl.CommAbort(comm);
+    return fail(PZ_ERR_NCCL);
+  }
   ctx->comm = comm;
+  const pz_status s = nccl_settle(ctx, r, t0);
+  if (s != PZ_OK) return s;
   ctx->world = world;
   ctx->rank = rank;
+  return PZ_OK;
+}
+
+pz_status pz_ctx_init_nccl(pz_sampler_ctx *ctx, int world, int rank,
+                           const void *unique_id, size_t id_bytes) {
+  return pz_ctx_init_nccl_timeout(ctx, world, rank, unique_id, id_bytes, 60000);
+}
+
+pz_status pz_ctx_wait(pz_sampler_ctx *ctx, void *stream, int timeout_ms) {
+  if (!ctx || timeout_ms <= 0) return fail(PZ_ERR_INVALID_ARGS);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(PZ_ERR_CUDA);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const double t0 = now_ms();
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(st);
+    if (q == cudaSuccess) return PZ_OK;
+    if (q != cudaErrorNotReady) return fail_cuda(q);
+    if (ctx->comm) {
+      ncclResult_t ar = ncclSuccess;
+      if (g_nccl.CommGetAsyncError(ctx->comm, &ar) != ncclSuccess || (ar != ncclSuccess && ar != ncclInProgress)) {
+        abort_comm(ctx);
+        g_last_error = PZ_ERR_NCCL;
+        std::snprintf(g_detail, sizeof g_detail, "NCCL asynchronous error %d; communicator aborted",
+                      static_cast<int>(ar));
+        return PZ_ERR_NCCL;
+      }
+    }
+    if (now_ms() - t0 > timeout_ms) {
+      // aborting the communicator ends its collectives still in flight
+      if (ctx->comm) abort_comm(ctx);
+      g_last_error = PZ_ERR_TIMEOUT;
+      std::snprintf(g_detail, sizeof g_detail, "stream unfinished after %d ms", timeout_ms);
+      return PZ_ERR_TIMEOUT;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+pz_status pz_ctx_abort_nccl(pz_sampler_ctx *ctx) {
+  if (!ctx) return fail(PZ_ERR_INVALID_ARGS);
+  if (ctx->comm) {
+    DeviceGuard g(ctx->device);
+    abort_comm(ctx);
+  }
   return PZ_OK;
 }
 
@@ -659,7 +828,8 @@ pz_status pz_sample_batch_vocab_sharded(
     const pz_sampler_config *cfg, const int32_t *hist, const int32_t *hist_off,
     unsigned long long *rng_state, int32_t *out_tokens,
     const pz_batch_outputs *outputs, void *stream) {
-  if (!ctx || !ctx->comm || !rng_state || !out_tokens) return fail(PZ_ERR_INVALID_ARGS);
+  if (!ctx || !rng_state || !out_tokens) return fail(PZ_ERR_INVALID_ARGS);
+  if (!ctx->comm) return fail(ctx->comm_failed ? PZ_ERR_NCCL : PZ_ERR_INVALID_ARGS);
   if (outputs && (outputs->cand_ids || outputs->cand_probs) &&
       outputs->cand_stride < std::max(ctx->lim.max_top_k, 1))
     return fail(PZ_ERR_INVALID_ARGS);
@@ -667,17 +837,25 @@ pz_status pz_sample_batch_vocab_sharded(
     return fail(PZ_ERR_INVALID_ARGS);
   pz_batch_hints h{};
   h.no_full_vocab = 1;
+  cudaEvent_t *ev = nullptr;
   pz_status s = sample_impl(ctx, logits_slice, dtype, B, V_local, ld, v_offset,
                             V_global, cfg, hist, hist_off, nullptr, nullptr, &h,
-                            nullptr, stream, true);
+                            nullptr, stream, true, &ev);
   if (s != PZ_OK) return s;
   DeviceGuard g(ctx->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int kcap = next_pow2(std::max(ctx->lim.max_top_k, 1));
   const size_t per_rank = static_cast<size_t>(B) * (kcap + 1);
   // ONE allgather: every rank's [B][kcap+1] list block, counts included.
-  if (g_nccl.AllGather(ctx->emit, ctx->gathered, per_rank, ncclUint64, ctx->comm, st) != ncclSuccess)
+  const double t0 = now_ms();
+  const ncclResult_t r = g_nccl.AllGather(ctx->emit, ctx->gathered, per_rank, ncclUint64, ctx->comm, st);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    abort_comm(ctx);
     return fail(PZ_ERR_NCCL);
+  }
+  s = nccl_settle(ctx, r, t0);  // the call is enqueued (not finished) when this returns
+  if (s != PZ_OK) return s;
+  if (ev) cudaEventRecord(ev[3], st);
   MergeArgs m{};
   m.gathered = ctx->gathered;
   m.G = ctx->world;
@@ -695,7 +873,12 @@ pz_status pz_sample_batch_vocab_sharded(
     m.row_status = outputs->row_status;
     m.cand_stride = outputs->cand_stride;
   }
-  if (pz::launch_merge(m, pz::merge_smem_bytes(kcap), st) != cudaSuccess) return fail(PZ_ERR_CUDA);
+  const cudaError_t ce = pz::launch_merge(m, pz::merge_smem_bytes(kcap), st);
+  if (ce != cudaSuccess) return fail_cuda(ce);
+  if (ev) {
+    cudaEventRecord(ev[4], st);
+    ctx->prof_kernels += 1;
+  }
   return PZ_OK;
 }
 
@@ -703,6 +886,9 @@ pz_status pz_sample_batch_vocab_sharded(
 // Layer 1: the reference's six calls on host pointers.
 // ---------------------------------------------------------------------------
 namespace {
+// One staging area per device: a single-row context, its stream and device
+// buffers.  Calls on one device are serialised by its mutex (the
+// reference's sample_top_p is not reentrant either).
 struct LegacyState {
   std::mutex mu;
   pz_sampler_ctx *ctx = nullptr;
@@ -712,48 +898,51 @@ struct LegacyState {
   pz_sampler_config *d_cfg = nullptr;
   unsigned long long *d_rng = nullptr;
   int32_t *d_out = nullptr;
-  int device = -1;
 };
-LegacyState g_legacy;
+LegacyState g_legacy[kMaxDevices];
 
-void legacy_free() {
-  if (g_legacy.d_logits) cudaFree(g_legacy.d_logits);
-  if (g_legacy.d_cfg) cudaFree(g_legacy.d_cfg);
-  if (g_legacy.d_rng) cudaFree(g_legacy.d_rng);
-  if (g_legacy.d_out) cudaFree(g_legacy.d_out);
-  g_legacy.d_logits = nullptr;
-  g_legacy.d_cfg = nullptr;
-  g_legacy.d_rng = nullptr;
-  g_legacy.d_out = nullptr;
-  if (g_legacy.ctx) pz_ctx_destroy(g_legacy.ctx);
-  g_legacy.ctx = nullptr;
-  g_legacy.vocab = 0;
+void legacy_free(LegacyState &L) {
+  if (L.d_logits) cudaFree(L.d_logits);
+  if (L.d_cfg) cudaFree(L.d_cfg);
+  if (L.d_rng) cudaFree(L.d_rng);
+  if (L.d_out) cudaFree(L.d_out);
+  L.d_logits = nullptr;
+  L.d_cfg = nullptr;
+  L.d_rng = nullptr;
+  L.d_out = nullptr;
+  if (L.ctx) pz_ctx_destroy(L.ctx);
+  L.ctx = nullptr;
+  L.vocab = 0;
 }
 
-// Prepares the single-row context for V columns on the current device.
-pz_status legacy_ready(int V) {
+// The current device's staging area, ready for V columns (its lock held by
+// the caller through `lk`).
+pz_status legacy_ready(int V, LegacyState **out, std::unique_lock<std::mutex> &lk) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return PZ_ERR_NO_DEVICE;
-  if (g_legacy.ctx && g_legacy.vocab >= V && g_legacy.device == dev) return PZ_OK;
-  legacy_free();
-  if (!g_legacy.st && cudaStreamCreateWithFlags(&g_legacy.st, cudaStreamNonBlocking) != cudaSuccess)
+  if (dev < 0 || dev >= kMaxDevices) return PZ_ERR_UNSUPPORTED;
+  LegacyState &L = g_legacy[dev];
+  lk = std::unique_lock<std::mutex>(L.mu);
+  *out = &L;
+  if (L.ctx && L.vocab >= V) return PZ_OK;
+  legacy_free(L);
+  if (!L.st && cudaStreamCreateWithFlags(&L.st, cudaStreamNonBlocking) != cudaSuccess)
     return PZ_ERR_CUDA;
-  pz_ctx_limits L{};
-  L.max_batch = 1;
-  L.max_vocab = std::max(V, 1024);
-  L.max_top_k = PZ_TOP_K_MAX;
-  L.max_history = 0;
-  pz_status s = pz_ctx_create(&g_legacy.ctx, dev, &L);
+  pz_ctx_limits lim{};
+  lim.max_batch = 1;
+  lim.max_vocab = std::max(V, 1024);
+  lim.max_top_k = PZ_TOP_K_MAX;
+  lim.max_history = 0;
+  pz_status s = pz_ctx_create(&L.ctx, dev, &lim);
   if (s != PZ_OK) return s;
-  if (cudaMalloc(&g_legacy.d_logits, sizeof(float) * L.max_vocab) != cudaSuccess ||
-      cudaMalloc(&g_legacy.d_cfg, sizeof(pz_sampler_config)) != cudaSuccess ||
-      cudaMalloc(&g_legacy.d_rng, sizeof(unsigned long long)) != cudaSuccess ||
-      cudaMalloc(&g_legacy.d_out, sizeof(int32_t)) != cudaSuccess) {
-    legacy_free();
+  if (cudaMalloc(&L.d_logits, sizeof(float) * lim.max_vocab) != cudaSuccess ||
+      cudaMalloc(&L.d_cfg, sizeof(pz_sampler_config)) != cudaSuccess ||
+      cudaMalloc(&L.d_rng, sizeof(unsigned long long)) != cudaSuccess ||
+      cudaMalloc(&L.d_out, sizeof(int32_t)) != cudaSuccess) {
+    legacy_free(L);
     return PZ_ERR_OOM;
   }
-  g_legacy.vocab = L.max_vocab;
-  g_legacy.device = dev;
+  L.vocab = lim.max_vocab;
   return PZ_OK;
 }
 
@@ -764,29 +953,31 @@ int legacy_row(const float *logits, int V, const pz_sampler_config &cfg,
     g_last_error = PZ_ERR_INVALID_ARGS;
     return -1;
   }
-  std::lock_guard<std::mutex> lk(g_legacy.mu);
-  pz_status s = legacy_ready(V);
+  LegacyState *Lp = nullptr;
+  std::unique_lock<std::mutex> lk;
+  pz_status s = legacy_ready(V, &Lp, lk);
   if (s != PZ_OK) {
     g_last_error = s;
     return -1;
   }
-  cudaStream_t st = g_legacy.st;
+  LegacyState &L = *Lp;
+  cudaStream_t st = L.st;
   unsigned long long state = rng_state ? *rng_state : 1ull;
   int32_t tok = -1;
-  if (cudaMemcpyAsync(g_legacy.d_logits, logits, sizeof(float) * V, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-      cudaMemcpyAsync(g_legacy.d_cfg, &cfg, sizeof cfg, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-      cudaMemcpyAsync(g_legacy.d_rng, &state, sizeof state, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+  if (cudaMemcpyAsync(L.d_logits, logits, sizeof(float) * V, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(L.d_cfg, &cfg, sizeof cfg, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(L.d_rng, &state, sizeof state, cudaMemcpyHostToDevice, st) != cudaSuccess) {
     g_last_error = PZ_ERR_CUDA;
     return -1;
   }
-  s = pz_sample_batch(g_legacy.ctx, g_legacy.d_logits, PZ_DTYPE_F32, 1, V, V, g_legacy.d_cfg,
-                      nullptr, nullptr, g_legacy.d_rng, g_legacy.d_out, nullptr, nullptr, st);
+  s = pz_sample_batch(L.ctx, L.d_logits, PZ_DTYPE_F32, 1, V, V, L.d_cfg, nullptr, nullptr, L.d_rng,
+                      L.d_out, nullptr, nullptr, st);
   if (s != PZ_OK) {
     g_last_error = s;
     return -1;
   }
-  if (cudaMemcpyAsync(&tok, g_legacy.d_out, sizeof tok, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-      cudaMemcpyAsync(&state, g_legacy.d_rng, sizeof state, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+  if (cudaMemcpyAsync(&tok, L.d_out, sizeof tok, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaMemcpyAsync(&state, L.d_rng, sizeof state, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
       cudaStreamSynchronize(st) != cudaSuccess) {
     g_last_error = PZ_ERR_CUDA;
     return -1;
@@ -817,16 +1008,18 @@ void pz_apply_temperature(float *logits, int vocab_size, float temperature) {
     g_last_error = PZ_ERR_INVALID_ARGS;
     return;
   }
-  std::lock_guard<std::mutex> lk(g_legacy.mu);
-  pz_status s = legacy_ready(vocab_size);
+  LegacyState *Lp = nullptr;
+  std::unique_lock<std::mutex> lk;
+  pz_status s = legacy_ready(vocab_size, &Lp, lk);
   if (s != PZ_OK) {
     g_last_error = s;
     return;
   }
-  cudaStream_t st = g_legacy.st;
-  if (cudaMemcpyAsync(g_legacy.d_logits, logits, sizeof(float) * vocab_size, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-      pz::launch_temperature(g_legacy.d_logits, vocab_size, temperature, st) != cudaSuccess ||
-      cudaMemcpyAsync(logits, g_legacy.d_logits, sizeof(float) * vocab_size, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+  cudaStream_t st = Lp->st;
+  float *d = Lp->d_logits;
+  if (cudaMemcpyAsync(d, logits, sizeof(float) * vocab_size, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      pz::launch_temperature(d, vocab_size, temperature, st) != cudaSuccess ||
+      cudaMemcpyAsync(logits, d, sizeof(float) * vocab_size, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
       cudaStreamSynchronize(st) != cudaSuccess) {
     g_last_error = PZ_ERR_CUDA;
     return;

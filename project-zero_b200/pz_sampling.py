@@ -39,6 +39,8 @@ if not os.path.exists(LIB_PATH):
 _lib = ctypes.CDLL(LIB_PATH)
 
 PZ_OK = 0
+PZ_ERR_NCCL = 4
+PZ_ERR_TIMEOUT = 5
 PZ_ERR_UNSUPPORTED = 6
 PZ_DTYPE_F32, PZ_DTYPE_BF16 = 0, 1
 PZ_CFG_TEMP_DIVIDE = 0x1
@@ -117,6 +119,12 @@ _sig("pz_ctx_profile", ctypes.c_int, [_vp, ctypes.c_int])
 _sig("pz_ctx_profile_read", ctypes.c_int,
      [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int),
       ctypes.POINTER(ctypes.c_int)])
+_sig("pz_ctx_profile_phases", ctypes.c_int,
+     [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)])
+_sig("pz_ctx_init_nccl_timeout", ctypes.c_int,
+     [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_size_t, ctypes.c_int])
+_sig("pz_ctx_wait", ctypes.c_int, [_vp, _vp, ctypes.c_int])
+_sig("pz_ctx_abort_nccl", ctypes.c_int, [_vp])
 _sig("pz_sample_batch_static", ctypes.c_int,
      [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp,
       ctypes.POINTER(BatchOutputs), _vp])
@@ -324,6 +332,23 @@ class Sampler:
                                         ctypes.byref(k)), "pz_ctx_profile_read")
         return a.value, b.value, n.value, k.value
 
+    def profile_phases(self):
+        """({'slice', 'full', 'allgather', 'merge'} ms summed over the timed
+        calls, calls, kernels launched) since the last read."""
+        ph = (ctypes.c_double * 4)()
+        n, k = ctypes.c_int(), ctypes.c_int()
+        _check(_lib.pz_ctx_profile_phases(self._h, ph, ctypes.byref(n), ctypes.byref(k)),
+               "pz_ctx_profile_phases")
+        return dict(zip(("slice", "full", "allgather", "merge"), list(ph))), n.value, k.value
+
+    def wait(self, timeout_ms, stream=None):
+        """Bounded wait for the stream's work (NCCL errors and the deadline
+        abort the communicator and raise)."""
+        _check(_lib.pz_ctx_wait(self._h, _stream_handle(stream), int(timeout_ms)), "pz_ctx_wait")
+
+    def abort_nccl(self):
+        _check(_lib.pz_ctx_abort_nccl(self._h), "pz_ctx_abort_nccl")
+
     # ---- vocab sharding --------------------------------------------------
     @staticmethod
     def nccl_unique_id() -> bytes:
@@ -331,9 +356,10 @@ class Sampler:
         _check(_lib.pz_nccl_get_unique_id(buf, 128), "pz_nccl_get_unique_id")
         return buf.raw
 
-    def init_nccl(self, world, rank, unique_id: bytes):
+    def init_nccl(self, world, rank, unique_id: bytes, timeout_ms=60000):
         buf = ctypes.create_string_buffer(unique_id, 128)
-        _check(_lib.pz_ctx_init_nccl(self._h, world, rank, buf, 128), "pz_ctx_init_nccl")
+        _check(_lib.pz_ctx_init_nccl_timeout(self._h, world, rank, buf, 128, int(timeout_ms)),
+               "pz_ctx_init_nccl")
         self.world, self.rank = world, rank
 
     def sample_vocab_sharded(self, logits_slice, v_offset, V_global, cfg, rng_state, out,

@@ -41,3 +41,21 @@ def cuda():
 def pz(cuda):
     import pz_sampling
     return pz_sampling
+
+
+def pytest_terminal_summary(terminalreporter):
+    """Reports the boundary cases (draws within 1e-6 of a CDF edge that gave
+    a different id than the oracle) counted by the parity tests."""
+    try:
+        from gpu_helpers import BOUNDARY_LOG
+    except ImportError:
+        return
+    if not BOUNDARY_LOG:
+        return
+    rows = sum(n for _, n, _ in BOUNDARY_LOG)
+    cases = sum(c for _, _, c in BOUNDARY_LOG)
+    terminalreporter.write_line(f"parity: {cases} boundary case(s) in {rows} sampled rows "
+                                f"({len(BOUNDARY_LOG)} comparisons)")
+    for label, n, c in BOUNDARY_LOG:
+        if c:
+            terminalreporter.write_line(f"  {label or '?'}: {c} of {n} rows")

@@ -82,3 +82,80 @@ def test_vocab_sharded_two_gpus(tmp_path, oracle_lib):
     tok, rng, *_ = oracle_lib.sample_batch(d["logits"], d["cfg"], d["rng"])
     assert res[0][0] == tok.tolist()
     assert res[0][1] == [int(v) for v in rng]
+
+
+def test_contexts_on_two_devices_in_one_process(oracle_lib):
+    """Kernel attributes (the opt-in to large dynamic shared memory) are set
+    per device: contexts on cuda:0 and cuda:1 in one process both sample a
+    config-3 batch exactly."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import pz_sampling as pz
+    from gpu_helpers import compare_with_oracle
+    spec = dict(seed=62, B=64, V=128256, sd=2.5, boosts=[8, 5.0, 15.0], hist_len=1024,
+                cfg=dict(temperature=0.7, top_k=50, top_p=0.9, rep=1.1, freq=0.2, pres=0.1))
+    d = cases.build(spec)
+    torch.cuda.set_device(0)
+    for dev in (1, 0):
+        x = torch.from_numpy(d["logits"]).to(f"cuda:{dev}")
+        cfg = torch.from_numpy(np.ascontiguousarray(d["cfg"]).view(np.uint8).copy()).to(f"cuda:{dev}")
+        rng = torch.from_numpy(d["rng"].view(np.int64).copy()).to(f"cuda:{dev}")
+        hist = torch.from_numpy(d["hist"]).to(f"cuda:{dev}")
+        hoff = torch.from_numpy(d["hist_off"]).to(f"cuda:{dev}")
+        s = pz.Sampler(dev, max_batch=64, max_vocab=128256, max_top_k=64, max_history=1024)
+        out = torch.full((64,), -7, dtype=torch.int32, device=f"cuda:{dev}")
+        cid = torch.full((64, 64), -9, dtype=torch.int32, device=f"cuda:{dev}")
+        cpr = torch.full((64, 64), -9.0, dtype=torch.float32, device=f"cuda:{dev}")
+        ncd = torch.full((64,), -9, dtype=torch.int32, device=f"cuda:{dev}")
+        with torch.cuda.device(dev):
+            s.sample(x, cfg, rng, out, hist, hoff, max_top_k=64, max_history=1024, no_full_vocab=True,
+                     cand_ids=cid, cand_probs=cpr, n_cand=ncd)
+        torch.cuda.synchronize(dev)
+        g = dict(tokens=out.cpu().numpy(), rng=rng.cpu().numpy().view(np.uint64), cand_ids=cid.cpu().numpy(),
+                 cand_probs=cpr.cpu().numpy(), n_cand=ncd.cpu().numpy())
+        s.close()
+        mism, _, _ = compare_with_oracle(oracle_lib, d, g, 1e-6, label=f"context on cuda:{dev}")
+        assert mism == 0
+        # the legacy single-row calls keep one staging area per device
+        with torch.cuda.device(dev):
+            t = pz.sample_argmax(d["logits"][0])
+        assert t == int(np.argmax(d["logits"][0]))
+
+
+def _lonely_rank(q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import sys
+    import time
+    sys.path.insert(0, os.path.join(os.path.dirname(TESTS), "project-zero_b200"))
+    try:
+        import pz_sampling as pz
+        torch.cuda.set_device(0)
+        s = pz.Sampler(0, max_batch=8, max_vocab=4096, max_top_k=64, max_history=0)
+        uid = pz.Sampler.nccl_unique_id()
+        t0 = time.time()
+        try:
+            s.init_nccl(2, 0, uid, timeout_ms=3000)  # rank 1 never joins
+            q.put(("joined", time.time() - t0))
+        except pz.PZError as e:
+            q.put((e.status, time.time() - t0))
+        s.close()
+    except Exception as e:  # report, never hang the parent
+        q.put(("err", repr(e)))
+
+
+def test_nccl_init_times_out_when_a_rank_never_joins():
+    """A communicator of two ranks whose second rank never arrives: the
+    non-blocking set-up is polled against its 3 s deadline and comes back
+    PZ_ERR_TIMEOUT (the communicator aborted) instead of waiting for ever.
+    Nothing is launched on the GPU while the rank waits."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    import pz_sampling as pz
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_lonely_rank, args=(q,))
+    p.start()
+    status, took = q.get(timeout=120)
+    p.join(timeout=60)
+    assert status == pz.PZ_ERR_TIMEOUT, (status, took)
+    assert 2.5 < took < 30.0

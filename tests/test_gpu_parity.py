@@ -24,7 +24,7 @@ def test_golden_pipeline(cuda, pz, golden, oracle_lib, name):
     assert g["tokens"].tolist() == case["tokens"]
     assert [int(v) for v in g["rng"]] == case["rng_out"]
     assert (g["status"] == 0).all()
-    mism, _, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+    mism, _, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL, label=f"golden {name}")
     assert mism == 0
 
 
@@ -79,9 +79,17 @@ def test_config3_full_size(cuda, pz, oracle_lib):
                 cfg=dict(temperature=0.7, top_k=50, top_p=0.9, rep=1.1, freq=0.2, pres=0.1))
     d = cases.build(spec)
     g = run_gpu(cuda, pz, d, max_top_k=50, max_history=1024, no_full_vocab=True)
-    mism, n, maxrel = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+    mism, n, maxrel = compare_with_oracle(oracle_lib, d, g, PROB_RTOL, label="config3 B=1024")
     print(f"config3: {mism} boundary mismatches in {n} rows, max prob rel err {maxrel:.2e}")
     assert mism == 0
+    # and against the reference's own compiled sampler (oracle/_ref)
+    import oracle
+    if not oracle.reference_available():
+        pytest.skip("the reference build (oracle/_ref) is not present")
+    tok_ref, rng_ref = oracle.Reference().sample_batch(d["logits"], d["cfg"], d["rng"], d["hist"],
+                                                       d["hist_off"])
+    assert (g["tokens"] == tok_ref).all()
+    assert (g["rng"] == rng_ref).all()
 
 
 def test_config2_full_size_greedy(cuda, pz, oracle_lib):
@@ -97,9 +105,8 @@ def test_config4_heterogeneous(cuda, pz, oracle_lib):
     spec = dict(seed=41, B=256, V=151936, sd=2.0, zipf=[256, 10.0], dtype="bf16", cfg="hetero")
     d = cases.build(spec)
     g = run_gpu(cuda, pz, d)
-    mism, n, maxrel = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
-    print(f"config4: {mism} mismatches in {n} rows, max prob rel err {maxrel:.2e}")
-    assert mism <= 1
+    mism, n, maxrel = compare_with_oracle(oracle_lib, d, g, PROB_RTOL, label="config4 B=256")
+    print(f"config4: {mism} boundary cases in {n} rows, max prob rel err {maxrel:.2e}")
 
 
 def test_full_vocab_rows_exact(cuda, pz, oracle_lib):
@@ -113,8 +120,9 @@ def test_full_vocab_rows_exact(cuda, pz, oracle_lib):
                       cfg=dict(temperature=1.0, top_k=0, top_p=1.0, rep=1.2))]:
         d = cases.build(spec)
         g = run_gpu(cuda, pz, d)
-        mism, n, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
-        assert mism <= 1, (spec["seed"], mism)
+        # every mismatch is proved to be a boundary case inside; the sums
+        # replay the reference's exactly, so only an expf ulp can move an edge
+        compare_with_oracle(oracle_lib, d, g, PROB_RTOL, label=f"full-vocab seed {spec['seed']}")
 
 
 def test_strided_and_unaligned_rows(cuda, pz, oracle_lib):
@@ -259,15 +267,14 @@ def test_last_wave_rows_split(cuda, pz, oracle_lib, B):
     d = cases.build(spec)
     s = pz.Sampler(0, max_batch=B, max_vocab=50000, max_top_k=1024, max_history=2048)
     g = run_gpu(cuda, pz, d, sampler=s)
-    mism, n, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
-    assert mism <= 1, (B, mism)
+    compare_with_oracle(oracle_lib, d, g, PROB_RTOL, label=f"last wave B={B} hetero")
     again = run_gpu(cuda, pz, d, sampler=s)
     assert (again["tokens"] == g["tokens"]).all() and (again["rng"] == g["rng"]).all()
     spec = dict(seed=92 + B, B=B, V=50000, sd=2.0, boosts=[8, 3.0, 6.0], hist_len=200,
                 cfg=dict(temperature=0.0, rep=1.3))
     d = cases.build(spec)
     g = run_gpu(cuda, pz, d, sampler=s, max_top_k=1, max_history=256)
-    mism, n, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL)
+    mism, n, _ = compare_with_oracle(oracle_lib, d, g, PROB_RTOL, label=f"last wave B={B} greedy")
     assert mism == 0, (B, mism)
     again = run_gpu(cuda, pz, d, sampler=s, max_top_k=1, max_history=256)
     assert (again["tokens"] == g["tokens"]).all()
