@@ -148,6 +148,7 @@ struct pz_sampler_ctx {
   int32_t *n_full = nullptr;
   uint32_t *sort_a = nullptr;
   uint32_t *sort_b = nullptr;
+  float *full_e = nullptr;
   int64_t sort_stride = 0;
   int full_grid = 0;
   // vocab sharding
@@ -280,7 +281,8 @@ pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
             c->alloc(&c->row_flags, B) && c->alloc(&c->row_tau, B) && c->alloc(&c->row_best, B) &&
             c->alloc(&c->full_rows, B) && c->alloc(&c->n_full, 1) &&
             c->alloc(&c->sort_a, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
-            c->alloc(&c->sort_b, static_cast<size_t>(c->full_grid) * c->sort_stride);
+            c->alloc(&c->sort_b, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
+            c->alloc(&c->full_e, static_cast<size_t>(c->full_grid) * L.max_vocab);
   if (!ok) {
     c->release();
     delete c;
@@ -517,10 +519,13 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     f.sort_a = ctx->sort_a;
     f.sort_b = ctx->sort_b;
     f.sort_stride = ctx->sort_stride;
+    f.escr = ctx->full_e;
     f.rng = rng_state;
     f.out = out;
     const size_t fsmem = pz::full_smem_bytes(V, f.hcap);
     if (fsmem > static_cast<size_t>(pz::max_dynamic_smem())) return fail(PZ_ERR_UNSUPPORTED);
+    const size_t fixed = (pz::full_smem_fixed(V, f.hcap) + 15) / 16 * 16;
+    f.smem_sort_cap = static_cast<int>((fsmem - fixed) / 16);
     const int grid = std::min(ctx->full_grid, B);
     ce = pz::launch_full(f, dtype, grid, fsmem, st);
     if (ce != cudaSuccess) return fail_cuda(ce);

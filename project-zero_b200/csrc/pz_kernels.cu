@@ -1532,17 +1532,57 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
 
 
 // ---------------------------------------------------------------------------
-// full_kernel: rows that need the whole row's distribution.
+// full_kernel: rows that need the whole row's distribution (k = 0).
+//
+// One CTA per row (the grid loops over the rows slice_kernel handed over).
+//   pass 1   index order: e_i = exp(v_i - max) for the values the max-20
+//            filter keeps (top_p.c:57-65) or for every value (softmax.c:12-16),
+//            stored to scratch; the reference's sequential float normaliser
+//            replayed exactly (pz_seqsum.cuh); top-p rows also count the e
+//            values into 512 bins (16 per binade).
+//   softmax  the CDF walk in index order over fl(e_i * inv)
+//            (generate.c:159-167), a second exact replay.
+//   top-p    a probability bound P whose mass (a lower bound from the bins)
+//            clears top_p with room to spare; the entries with
+//            prob = fl(e_i * inv) >= P are exactly a prefix of the
+//            reference's stable sort (prob desc, index asc, top_p.c:77), so
+//            only they are collected (in index order) and sorted (stable
+//            radix sort, in shared memory when they fit).  The cumulative
+//            cutoff (:80-88), the truncated sum (:91-93) and the draw
+//            (:96-105) are replayed over that prefix; if the cutoff is not
+//            inside it (the bound was not conservative enough), every entry
+//            is collected instead.
 // ---------------------------------------------------------------------------
-size_t full_smem_bytes(int V, int hcap) {
-  const size_t bm_words = static_cast<size_t>(V) / 32 + 2;
-  return sizeof(uint32_t) * bm_words + sizeof(int32_t) * static_cast<size_t>(hcap) +
-         sizeof(uint32_t) * (kFullThreads / 32) * 256 + sizeof(uint32_t) * 256 * 2;
+constexpr int kEBins = 512;
+constexpr int kSeqHead = 1024;  // terms of each sum added in order by one thread
+// Bin of a positive e value: 16 bins per binade, from 2^-32 up (e <= 1).
+__device__ __forceinline__ int ebin(float e) {
+  const int b = static_cast<int>(__float_as_uint(e) >> 19) - (95 << 4);
+  return b < 0 ? 0 : (b >= kEBins ? kEBins - 1 : b);
+}
+// Smallest e of bin b (bin 0 also holds everything below 2^-32).
+__device__ __forceinline__ float ebin_low(int b) {
+  return b == 0 ? 0.0f : __uint_as_float(static_cast<uint32_t>(b + (95 << 4)) << 19);
 }
 
-// Stable LSD radix sort of (key, value) u32 pairs ascending by key, in
-// global scratch, by one block.  Each warp owns a contiguous segment; within
-// a segment elements keep their order, so equal keys keep input order.
+__host__ __device__ size_t full_smem_fixed(int V, int hcap) {
+  const size_t bm_words = static_cast<size_t>(V) / 32 + 2;
+  return sizeof(uint32_t) * bm_words + sizeof(int32_t) * static_cast<size_t>(hcap) +
+         sizeof(uint32_t) * (kFullThreads / 32) * 256 + sizeof(uint32_t) * 256 * 2 +
+         sizeof(uint32_t) * kEBins + sizeof(float) * kSeqHead;
+}
+
+size_t full_smem_bytes(int V, int hcap) {
+  // the fixed part, then as much room for in-smem sorts as fits
+  const size_t fixed = (full_smem_fixed(V, hcap) + 15) / 16 * 16;
+  const size_t cap = static_cast<size_t>(max_dynamic_smem());
+  return fixed < cap ? cap : fixed;
+}
+
+// Stable LSD radix sort of (key, value) u32 pairs ascending by key, by one
+// block, in shared or global memory (generic pointers).  Each warp owns a
+// contiguous segment; within a segment elements keep their order, so equal
+// keys keep input order.  Digits on which every key agrees are skipped.
 // Returns true when the result is in (k1, v1).
 template <int NT>
 __device__ __noinline__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32_t *k1,
@@ -1559,7 +1599,7 @@ __device__ __noinline__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32
     for (int i = tid; i < NW * 256; i += NT) whist[i] = 0u;
     __syncthreads();
     for (int j = s0 + lane; j < s1; j += 32)
-      atomicAdd(&whist[warp * 256 + ((__ldcg(ki + j) >> shift) & 255u)], 1u);
+      atomicAdd(&whist[warp * 256 + ((ki[j] >> shift) & 255u)], 1u);
     __syncthreads();
     if (tid < 256) {
       uint32_t run = 0;
@@ -1592,8 +1632,8 @@ __device__ __noinline__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32
     for (int j0 = s0; j0 < s1; j0 += 32) {
       const int j = j0 + lane;
       const bool act = j < s1;
-      const uint32_t key = act ? __ldcg(ki + j) : 0u;
-      const uint32_t val = act ? __ldcg(vi + j) : 0u;
+      const uint32_t key = act ? ki[j] : 0u;
+      const uint32_t val = act ? vi[j] : 0u;
       const uint32_t d = act ? ((key >> shift) & 255u) : (256u + lane);
       const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
       uint32_t pos = 0;
@@ -1613,6 +1653,48 @@ __device__ __noinline__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32
   return in1;
 }
 
+// Collects, in index order, the entries i < V with e[i] > 0 and
+// prob = fl(e[i] * inv) >= pmin as (~prob bits, i) into (ko, vo); returns
+// their number.  Block-wide.
+template <int NT>
+__device__ int collect_prefix(const float *e, int V, float inv, float pmin, uint32_t *ko, uint32_t *vo,
+                              int *red) {
+  int nf = 0;
+  for (int c0 = 0; c0 < V; c0 += NT * 4) {
+    float pv[4];
+    int cnt = 0;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int i = c0 + threadIdx.x * 4 + q;
+      pv[q] = -1.0f;
+      if (i < V) {
+        const float ei = e[i];
+        if (ei > 0.0f) {
+          const float pr = __fmul_rn(ei, inv);                   // top_p.c:73-74
+          if (pr >= pmin) {
+            pv[q] = pr;
+            cnt++;
+          }
+        }
+      }
+    }
+    int total;
+    int pos = nf + block_exscan_int<NT>(cnt, total, red);
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      if (pv[q] >= 0.0f) {
+        ko[pos] = ~__float_as_uint(pv[q]);
+        vo[pos] = static_cast<uint32_t>(c0 + threadIdx.x * 4 + q);
+        pos++;
+      }
+    }
+    nf += total;
+  }
+  __threadfence_block();
+  __syncthreads();
+  return nf;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kFullThreads, 1) full_kernel(const FullArgs A) {
   constexpr int NT = kFullThreads;
@@ -1620,16 +1702,26 @@ __global__ void __launch_bounds__(kFullThreads, 1) full_kernel(const FullArgs A)
   __shared__ SeqShared ssh;
   __shared__ int s_red[NT / 32];
   __shared__ int s_nh, s_flag;
+  __shared__ float s_pmin;
   const int tid = threadIdx.x;
   const int bm_words = A.V / 32 + 2;
   uint32_t *bitmap = reinterpret_cast<uint32_t *>(smem);
   int32_t *hl = reinterpret_cast<int32_t *>(bitmap + bm_words);
   uint32_t *whist = reinterpret_cast<uint32_t *>(hl + A.hcap);
   uint32_t *tot = whist + (NT / 32) * 256;
-  uint32_t *k0 = A.sort_a + static_cast<size_t>(blockIdx.x) * A.sort_stride;
-  uint32_t *v0 = k0 + A.sort_stride / 2;
-  uint32_t *k1 = A.sort_b + static_cast<size_t>(blockIdx.x) * A.sort_stride;
-  uint32_t *v1 = k1 + A.sort_stride / 2;
+  uint32_t *bins = tot + 256 * 2;
+  float *head = reinterpret_cast<float *>(bins + kEBins);
+  // in-smem sort room: two (key, value) buffers of sm_cap entries
+  const size_t fixed = (full_smem_fixed(A.V, A.hcap) + 15) / 16 * 16;
+  uint32_t *sm_k0 = reinterpret_cast<uint32_t *>(smem + fixed);
+  const int sm_cap = A.smem_sort_cap;
+  uint32_t *sm_v0 = sm_k0 + sm_cap, *sm_k1 = sm_v0 + sm_cap, *sm_v1 = sm_k1 + sm_cap;
+  // global scratch of this CTA: e values, then two (key, value) buffers
+  float *E = A.escr + static_cast<size_t>(blockIdx.x) * A.sort_stride / 2;
+  uint32_t *g_k0 = A.sort_a + static_cast<size_t>(blockIdx.x) * A.sort_stride;
+  uint32_t *g_v0 = g_k0 + A.sort_stride / 2;
+  uint32_t *g_k1 = A.sort_b + static_cast<size_t>(blockIdx.x) * A.sort_stride;
+  uint32_t *g_v1 = g_k1 + A.sort_stride / 2;
   const int n_full = *A.n_full;
 
   for (int w = blockIdx.x; w < n_full; w += gridDim.x) {
@@ -1651,6 +1743,7 @@ __global__ void __launch_bounds__(kFullThreads, 1) full_kernel(const FullArgs A)
     if (tid == 0) s_nh = 0;
     if (hist_on)
       for (int i = tid; i < bm_words; i += NT) bitmap[i] = 0u;
+    for (int i = tid; i < kEBins; i += NT) bins[i] = 0u;
     __syncthreads();
     int nh = 0;
     if (hist_on) {
@@ -1676,71 +1769,88 @@ __global__ void __launch_bounds__(kFullThreads, 1) full_kernel(const FullArgs A)
     };
     const float mx = key_val(A.row_best[row]);
     unsigned long long rs = A.rng[row];
+    const bool topp = P.mode != kModeSoftmaxFull;
+    const float thr = __fsub_rn(mx, 20.0f);                             // top_p.c:53
+    // pass 1: e values (stored), the exact normaliser, the bins
+    const SeqResult s1 = seq_scan<NT, 4>(
+        V,
+        [&](int i) {
+          const float v = vof(i);
+          float e = 0.0f;
+          if (!topp || v >= thr) {                                       // :58
+            e = cr_expf(__fsub_rn(v, mx));                               // :59, softmax.c:13
+            if (topp) atomicAdd(&bins[ebin(e)], 1u);
+          }
+          E[i] = e;
+          return e;
+        },
+        kSeqNone, 0.0f, ssh, head, kSeqHead);
+    const float inv = __fdiv_rn(1.0f, s1.s);                            // :72, softmax.c:18
     int tok;
-    if (P.mode == kModeSoftmaxFull) {
-      // softmax.c:12-22 then generate.c:159-167
-      const SeqResult s1 = seq_scan<NT, 4>(
-          V, [&](int i) { return cr_expf(__fsub_rn(vof(i), mx)); }, kSeqNone, 0.0f, ssh);
-      const float inv = __fdiv_rn(1.0f, s1.s);
+    if (!topp) {
+      // generate.c:159-167: r = rng_float(), first i with r < cdf
       const float r = rng_next(rs);
       const SeqResult s2 = seq_scan<NT, 4>(
-          V, [&](int i) { return __fmul_rn(cr_expf(__fsub_rn(vof(i), mx)), inv); },
-          kSeqGT, r, ssh);
+          V, [&](int i) { return __fmul_rn(E[i], inv); }, kSeqGT, r, ssh, head, kSeqHead);
       tok = s2.hit >= 0 ? s2.hit : V - 1;
     } else {
-      // top_p.c:53-105 over the whole row
-      const float thr = __fsub_rn(mx, 20.0f);
-      const SeqResult s1 = seq_scan<NT, 4>(
-          V,
-          [&](int i) {
-            const float v = vof(i);
-            return v >= thr ? cr_expf(__fsub_rn(v, mx)) : 0.0f;
-          },
-          kSeqNone, 0.0f, ssh);
-      const float inv = __fdiv_rn(1.0f, s1.s);
-      // candidates in index order: (~prob bits, index)
-      int nf = 0;
-      for (int c0 = 0; c0 < V; c0 += NT * 4) {
-        float pv[4];
-        int cnt = 0;
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const int i = c0 + tid * 4 + e;
-          pv[e] = -1.0f;
-          if (i < V) {
-            const float v = vof(i);
-            if (v >= thr) {
-              pv[e] = __fmul_rn(cr_expf(__fsub_rn(v, mx)), inv);
-              cnt++;
+      // the probability bound: bins from the top until a lower bound of the
+      // float cumulative over them clears top_p (with margin)
+      if (tid == 0) {
+        double mass = 0.0, cnt = 0.0;
+        float pmin = 0.0f;
+        const double want = static_cast<double>(P.p) + 1e-3;
+        if (want < 0.999) {
+          for (int b = kEBins - 1; b > 0; b--) {
+            const uint32_t c = bins[b];
+            if (c == 0u) continue;
+            cnt += c;
+            mass += static_cast<double>(c) * static_cast<double>(ebin_low(b)) * static_cast<double>(inv);
+            const double bound = mass * (1.0 - 5.97e-8) * (1.0 - (cnt + 1.0) * 5.97e-8);
+            if (bound >= want) {
+              pmin = __fmul_rn(ebin_low(b), inv);
+              break;
             }
           }
         }
-        int total;
-        int pos = nf + block_exscan_int<NT>(cnt, total, s_red);
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          if (pv[e] >= 0.0f) {
-            k0[pos] = ~__float_as_uint(pv[e]);
-            v0[pos] = static_cast<uint32_t>(c0 + tid * 4 + e);
-            pos++;
-          }
-        }
-        nf += total;
+        s_pmin = pmin;
       }
-      __threadfence_block();
       __syncthreads();
-      const bool in1 = block_radix_sort<NT>(k0, v0, k1, v1, nf, whist, tot, &s_flag);
-      const uint32_t *ks = in1 ? k1 : k0;
-      const uint32_t *vs = in1 ? v1 : v0;
-      // cumulative to the cutoff (:80-88), truncated sum (:91-93)
-      const SeqResult s3 = seq_scan<NT, 4>(
-          nf, [&](int j) { return __uint_as_float(~__ldcg(ks + j)); }, kSeqGE, P.p, ssh);
-      const int cutoff = s3.hit >= 0 ? s3.hit + 1 : nf;
-      const float r = __fmul_rn(rng_next(rs), s3.s);
-      const SeqResult s4 = seq_scan<NT, 4>(
-          cutoff, [&](int j) { return __uint_as_float(~__ldcg(ks + j)); }, kSeqGT, r, ssh);
-      const int pos = s4.hit >= 0 ? s4.hit : 0;
-      tok = nf > 0 ? static_cast<int>(__ldcg(vs + pos)) : key_idx(A.row_best[row]);
+      float pmin = s_pmin;
+      int cutoff = 0, pos = 0, nf = 0;
+      const uint32_t *ks = nullptr, *vs = nullptr;
+      for (int attempt = 0; attempt < 2; attempt++) {
+        nf = collect_prefix<NT>(E, V, inv, pmin, g_k0, g_v0, s_red);
+        bool in1;
+        if (nf <= sm_cap) {
+          for (int i = tid; i < nf; i += NT) {
+            sm_k0[i] = g_k0[i];
+            sm_v0[i] = g_v0[i];
+          }
+          __syncthreads();
+          in1 = block_radix_sort<NT>(sm_k0, sm_v0, sm_k1, sm_v1, nf, whist, tot, &s_flag);
+          ks = in1 ? sm_k1 : sm_k0;
+          vs = in1 ? sm_v1 : sm_v0;
+        } else {
+          in1 = block_radix_sort<NT>(g_k0, g_v0, g_k1, g_v1, nf, whist, tot, &s_flag);
+          ks = in1 ? g_k1 : g_k0;
+          vs = in1 ? g_v1 : g_v0;
+        }
+        // cumulative to the cutoff (:80-88) and the truncated sum (:91-93)
+        const SeqResult s3 = seq_scan<NT, 4>(
+            nf, [&](int j) { return __uint_as_float(~ks[j]); }, kSeqGE, P.p, ssh, head, kSeqHead);
+        if (s3.hit < 0 && pmin > 0.0f) {  // not inside the prefix: take every entry
+          pmin = 0.0f;
+          continue;
+        }
+        cutoff = s3.hit >= 0 ? s3.hit + 1 : nf;
+        const float r = __fmul_rn(rng_next(rs), s3.s);                  // :96
+        const SeqResult s4 = seq_scan<NT, 4>(
+            cutoff, [&](int j) { return __uint_as_float(~ks[j]); }, kSeqGT, r, ssh, head, kSeqHead);
+        pos = s4.hit >= 0 ? s4.hit : 0;                                 // :98-105
+        break;
+      }
+      tok = nf > 0 ? static_cast<int>(vs[pos]) : key_idx(A.row_best[row]);
     }
     if (tid == 0) {
       A.out[row] = tok;

@@ -84,6 +84,8 @@ struct FullArgs {
   uint32_t *sort_a;     // [gridDim][2*maxV] (prob key, index) pairs
   uint32_t *sort_b;
   int64_t sort_stride;  // uint32 elements per CTA in sort_a/sort_b
+  float *escr;          // [gridDim][maxV] e values of the CTA's row
+  int smem_sort_cap;    // (key, value) entries an in-smem sort holds
   unsigned long long *rng;
   int32_t *out;
 };
@@ -113,6 +115,7 @@ int slice_stages(int kcap, int hts);
 cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem,
                         cudaStream_t st);
 size_t full_smem_bytes(int V, int hcap);
+__host__ __device__ size_t full_smem_fixed(int V, int hcap);
 cudaError_t launch_merge(const MergeArgs &a, size_t smem, cudaStream_t st);
 size_t merge_smem_bytes(int kcap);
 cudaError_t launch_temperature(float *x, int n, float T, cudaStream_t st);

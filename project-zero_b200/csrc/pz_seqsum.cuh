@@ -163,18 +163,36 @@ struct SeqResult {
 
 // Replays s = fl(s + x_j) for j = 0..n-1 (x_j = get(j) >= 0) starting from
 // s = 0.  With a target, stops at the first j where s_j >= target (kSeqGE)
-// or s_j > target (kSeqGT).  Block-wide call; E consecutive terms per
-// thread per chunk.
+// or s_j > target (kSeqGT).  Block-wide call; get(j) is called once for
+// every j the scan reaches.
+//
+// The first head_cap terms (the running sum doubles, and so leaves its
+// binade, most often early on: about once per doubling of the terms seen)
+// are evaluated by all threads into head_buf and added in order by one
+// thread; the rest go E consecutive terms per thread per chunk through the
+// parallel replay, which restarts only at the few binade crossings left.
 template <int NT, int E, typename Get>
 __device__ SeqResult seq_scan(int n, Get get, int kind, float target,
-                              SeqShared &sh) {
+                              SeqShared &sh, float *head_buf, int head_cap) {
   const int tid = threadIdx.x;
+  const int K = n < head_cap ? n : head_cap;
+  for (int j = tid; j < K; j += NT) head_buf[j] = get(j);
+  __syncthreads();
   if (tid == 0) {
-    sh.s = 0.0f;
-    sh.done_pos = -1;
+    float s = 0.0f;
+    int done = -1;
+    for (int j = 0; j < K; j++) {
+      s = __fadd_rn(s, head_buf[j]);
+      if ((kind == kSeqGE && s >= target) || (kind == kSeqGT && s > target)) {
+        done = j;
+        break;
+      }
+    }
+    sh.s = s;
+    sh.done_pos = done;
   }
   __syncthreads();
-  for (int c0 = 0; c0 < n; c0 += NT * E) {
+  for (int c0 = K; c0 < n && sh.done_pos < 0; c0 += NT * E) {
     float x[E];
 #pragma unroll
     for (int e = 0; e < E; e++) {
