@@ -327,6 +327,41 @@ pz_status pz_sample_batch_vocab_sharded(
     const int32_t *hist_off, unsigned long long *rng_state,
     int32_t *out_tokens, const pz_batch_outputs *outputs, void *stream);
 
+/* ------------------------------------------------------------------------ */
+/* Settings from the front ends of the generate loop.                       */
+
+/* One request's sampler settings as the front ends give them: the config a
+ * row of pz_sample_batch takes, the RNG seed (-1: none given; the caller
+ * picks one, as the reference does with time(NULL) at generate.c:126) and
+ * the OpenAI-style logprob request. */
+#define PZ_TOP_LOGPROBS_MAX 20
+typedef struct pz_sampling_params {
+  pz_sampler_config cfg;
+  int64_t seed;
+  int32_t logprobs;      /* 1: the sampled id's log-probability is wanted   */
+  int32_t top_logprobs;  /* 0..PZ_TOP_LOGPROBS_MAX most likely ids as well   */
+} pz_sampling_params;
+
+/* Defaults of the command line (reference src/cli/args.c:82-89: T 0.7,
+ * top-p 0.9, seed -1) and of an API request (src/api/json_parse.c:299-300:
+ * T 1.0, top-p 1.0); no top-k, no penalties. */
+void pz_params_init_cli(pz_sampling_params *p);
+void pz_params_init_api(pz_sampling_params *p);
+/* Command-line flags over the CLI defaults: the reference's --temperature,
+ * --top-p (args.c:117-120) and --seed (args.c:125-126, which the reference
+ * parses but never uses), plus --top-k, --repeat-penalty,
+ * --frequency-penalty, --presence-penalty, --logprobs and --top-logprobs N.
+ * Other flags are left to the caller's own parser. */
+pz_status pz_params_from_args(pz_sampling_params *p, int argc, char **argv);
+/* A chat-completions JSON body over the API defaults: "temperature" and
+ * "top_p" (json_parse.c:344-347), plus "top_k", "repetition_penalty",
+ * "frequency_penalty", "presence_penalty", "seed", "logprobs" and
+ * "top_logprobs"; other keys are skipped.  Then the API's clamps
+ * (http_server.c:415-417: T to [0, 2], top-p outside [0, 1] -> 1) and the
+ * OpenAI ranges of the added fields (penalties to [-2, 2], top_logprobs to
+ * [0, 20]).  PZ_ERR_INVALID_ARGS for a body that is not a JSON object. */
+pz_status pz_params_from_json(pz_sampling_params *p, const char *json);
+
 /* Library version string. */
 const char *pz_version(void);
 

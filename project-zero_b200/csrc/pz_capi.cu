@@ -878,7 +878,7 @@ pz_status pz_sample_batch_vocab_sharded(
     m.row_status = outputs->row_status;
     m.cand_stride = outputs->cand_stride;
   }
-  const cudaError_t ce = pz::launch_merge(m, pz::merge_smem_bytes(kcap), st);
+  const cudaError_t ce = pz::launch_merge(m, st);
   if (ce != cudaSuccess) return fail_cuda(ce);
   if (ev) {
     cudaEventRecord(ev[4], st);

@@ -1861,126 +1861,134 @@ __global__ void __launch_bounds__(kFullThreads, 1) full_kernel(const FullArgs A)
 }
 
 // ---------------------------------------------------------------------------
-// merge_kernel: vocab-sharded rows after the allgather (one block per row).
+// merge_kernel: vocab-sharded rows after the allgather, one warp per row.
+// The G gathered lists of a row (each sorted, at most kcap keys, distinct
+// keys across ranks) are merged into the exact global top-k (the k-th
+// largest key by a warp radix select, then the keys at or above it, ranked),
+// and the row is decided as in slice_kernel (top_p.c:37-105 or
+// top_k.c:50-72 over the list, argmax for greedy rows).
 // ---------------------------------------------------------------------------
-size_t merge_smem_bytes(int kcap) {
-  return sizeof(unsigned long long) * static_cast<size_t>(kcap + kCapB) +
-         (sizeof(float) * 2 + sizeof(int)) * static_cast<size_t>(kcap);
+size_t merge_warp_bytes(int kcap, int G) {
+  const size_t b = sizeof(unsigned long long) * static_cast<size_t>(G) * static_cast<size_t>(kcap) +
+                   12 * static_cast<size_t>(kcap) + 16;
+  return (b + 15) / 16 * 16;
 }
 
-__global__ void __launch_bounds__(kSliceThreads) merge_kernel(const MergeArgs A) {
-  constexpr int NT = kSliceThreads;
-  constexpr int EPT = 16;
-  constexpr int MAXPER = (PZ_TOP_K_MAX + kCapB) / NT;
+int merge_rows_per_block(int kcap, int G) {
+  const size_t per = merge_warp_bytes(kcap, G);
+  const size_t budget = static_cast<size_t>(max_dynamic_smem());
+  int r = static_cast<int>(budget / per);
+  return r < 1 ? 1 : (r > kSliceWarps ? kSliceWarps : r);
+}
+
+__global__ void __launch_bounds__(kSliceThreads) merge_kernel(const MergeArgs A, int rows_per_block,
+                                                              int warp_bytes) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ SelShared sh;
-  __shared__ unsigned long long s_red[NT / 32];
-  __shared__ int s_tok, s_flags;
-  const int tid = threadIdx.x;
-  const int row = blockIdx.x;
-  const int cap = A.kcap + kCapB;
-  const int hwm = A.kcap + kCapB / 2;
-  unsigned long long *cand = reinterpret_cast<unsigned long long *>(smem);
-  float *fe = reinterpret_cast<float *>(cand + cap);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * rows_per_block + warp;
+  if (warp >= rows_per_block || row >= A.B) return;  // whole warps; no block barrier below
+  unsigned char *ws = smem + static_cast<size_t>(warp) * warp_bytes;
+  unsigned long long *lst = reinterpret_cast<unsigned long long *>(ws);
+  float *fe = reinterpret_cast<float *>(lst + static_cast<size_t>(A.G) * A.kcap);
   float *fp = fe + A.kcap;
   int *ford = reinterpret_cast<int *>(fp + A.kcap);
+  int *s_tok = ford + A.kcap;
   const RowPlan P = plan_row(A.cfg[row], A.V_global);
   const bool k_fits = P.keff <= A.kcap && P.keff <= A.kmax;
-  const bool use_buf = P.mode == kModeTopK && P.keff > 1 && k_fits;
-  const int k_sel = (P.mode == kModeTopK && k_fits) ? P.keff : 1;
-  const unsigned long long tau0 = (P.mode == kModeTopK) ? key_topk_floor() : 0ull;
-  if (tid == 0) {
-    sh.n = 0;
-    sh.tau = tau0;
-    s_flags = 0;
-  }
-  __syncthreads();
+  const bool topk = P.mode == kModeTopK;
+  const int k_sel = (topk && k_fits) ? P.keff : 1;
+  const unsigned long long tau0 = topk ? key_topk_floor() : 0ull;
   const size_t stride = static_cast<size_t>(A.kcap) + 1;
-  auto gcount = [&](int g) -> int {
-    return static_cast<int>(A.gathered[(static_cast<size_t>(g) * A.B + row) * stride + A.kcap]);
+  auto gslot = [&](int g) -> const unsigned long long * {
+    return A.gathered + (static_cast<size_t>(g) * A.B + row) * stride;
   };
-  auto gn = [&](int g) -> int { return min(gcount(g) & ((1 << 27) - 1), A.kcap); };
-  if (tid < A.G) atomicOr(&s_flags, gcount(tid) & (15 << 27));
+  // each rank's count and flags (slot kcap): count | x0nan<<30 | too_long<<29 | bad_k<<28 | timeout<<27
+  int flags = 0;
+  for (int g = lane; g < A.G; g += 32) flags |= static_cast<int>(gslot(g)[A.kcap]) & (15 << 27);
+  flags = __reduce_or_sync(0xFFFFFFFFu, flags);
   int n_sel = 0;
   unsigned long long gbest = 0ull;
-  if (use_buf) {
-    const int total = A.G * A.kcap;
-    for (int base = 0; base < total; base += NT * EPT) {
-      unsigned long long keys[EPT];
-      uint32_t valid = 0;
-#pragma unroll
-      for (int e = 0; e < EPT; e++) {
-        keys[e] = 0ull;
-        const int it = base + e * NT + tid;
-        if (it < total) {
-          const int g = it / A.kcap, j = it - g * A.kcap;
-          const int cnt = gn(g);
-          if (j < cnt) {
-            keys[e] = A.gathered[(static_cast<size_t>(g) * A.B + row) * stride + j];
-            valid |= 1u << e;
-          }
-        }
-      }
-      offer_round<NT, MAXPER, EPT>(cand, cap, hwm, k_sel, sh, keys, valid);
+  if (topk && k_sel > 1) {
+    int n = 0;
+    for (int g = 0; g < A.G; g++) {
+      const unsigned long long *src = gslot(g);
+      const int c = min(static_cast<int>(src[A.kcap]) & ((1 << 27) - 1), A.kcap);
+      for (int i = lane; i < c; i += 32) lst[n + i] = src[i];
+      n += c;
     }
-    __syncthreads();
-    int n = sh.n < cap ? sh.n : cap;
-    __syncthreads();
+    __syncwarp();
     if (n > k_sel) {
-      block_select<NT, MAXPER>(cand, n, k_sel, sh);
-      n = k_sel;
+      const unsigned long long kth = warp_kth(lst, n, k_sel);
+      n = warp_compact_ge(lst, n, kth);
     }
     n_sel = n;
-    for (int i = n_sel + tid; i < A.kcap; i += NT) cand[i] = 0ull;
-    block_sort_desc<NT>(cand, A.kcap);
+    if (A.kcap <= 64) {
+      warp_rank_sort_desc(lst, n_sel);
+      for (int i = n_sel + lane; i < A.kcap; i += 32) lst[i] = 0ull;
+      __syncwarp();
+    } else {
+      for (int i = n_sel + lane; i < A.kcap; i += 32) lst[i] = 0ull;
+      warp_sort_desc(lst, A.kcap);
+    }
   } else {
     unsigned long long bl = 0ull;
-    for (int g = tid; g < A.G; g += NT) {
-      const int cnt = gn(g);
-      if (cnt > 0) {
-        const unsigned long long k = A.gathered[(static_cast<size_t>(g) * A.B + row) * stride];
-        bl = k > bl ? k : bl;
-      }
+    for (int g = lane; g < A.G; g += 32) {
+      const unsigned long long *src = gslot(g);
+      if ((static_cast<int>(src[A.kcap]) & ((1 << 27) - 1)) > 0) bl = src[0] > bl ? src[0] : bl;
     }
-    gbest = block_max_u64<NT>(bl, s_red);
-    if (P.mode == kModeTopK) {  // k_eff == 1: the single best admitted key
+    gbest = warp_max_u64(bl);
+    if (topk) {  // k_eff == 1: the single best admitted key
       n_sel = gbest > tau0 ? 1 : 0;
-      if (tid == 0) cand[0] = gbest;
-      for (int i = 1 + tid; i < A.kcap; i += NT) cand[i] = 0ull;
-      __syncthreads();
+      if (lane == 0) lst[0] = gbest;
+      for (int i = 1 + lane; i < A.kcap; i += 32) lst[i] = 0ull;
+      __syncwarp();
     }
   }
-  const bool x0nan = (s_flags >> 30) & 1;
-  const bool too_long = (s_flags >> 29) & 1;
-  const bool bad_k = ((s_flags >> 28) & 1) || (P.mode == kModeTopK && !k_fits);
-  const bool timed_out = (s_flags >> 27) & 1;
+  const bool x0nan = (flags >> 30) & 1;
+  const bool too_long = (flags >> 29) & 1;
+  const bool bad_k = ((flags >> 28) & 1) || (topk && !k_fits);
+  const bool timed_out = (flags >> 27) & 1;
   unsigned long long rs = A.rng[row];
   int tok = -1;
   int status = too_long ? PZ_ROW_HISTORY_TOO_LONG : PZ_ROW_OK;
   const bool want_cand = A.cand_ids != nullptr || A.cand_probs != nullptr;
+  int32_t *cids = A.cand_ids ? A.cand_ids + static_cast<size_t>(row) * A.cand_stride : nullptr;
+  float *cprobs = A.cand_probs ? A.cand_probs + static_cast<size_t>(row) * A.cand_stride : nullptr;
+  bool listed = false;
   if (timed_out) {
-    tok = -1;
     status = PZ_ROW_TIMEOUT;
   } else if (too_long) {
     tok = -1;
   } else if (bad_k) {
-    tok = -1;
     status = PZ_ROW_HINT_VIOLATED;
   } else if (P.mode == kModeGreedy) {
     tok = x0nan ? 0 : (gbest ? key_idx(gbest) : 0);
-  } else if (P.mode == kModeTopK) {
-    int32_t *cids = A.cand_ids ? A.cand_ids + static_cast<size_t>(row) * A.cand_stride : nullptr;
-    float *cprobs = A.cand_probs ? A.cand_probs + static_cast<size_t>(row) * A.cand_stride : nullptr;
-    tok = sample_list<NT>(cand, n_sel, P, rs, fe, fp, ford, &s_tok,
-                          want_cand ? cids : nullptr, want_cand ? cprobs : nullptr);
+  } else if (topk) {
+    int t = INT_MIN;
+    if (P.keff <= 64) {
+      t = warp_sample_small(lst, n_sel, P, rs, fe, fp, want_cand ? cprobs : nullptr);
+      if (t != INT_MIN && cids != nullptr)
+        for (int i = lane; i < P.keff; i += 32) cids[i] = i < n_sel ? key_idx(lst[i]) : -1;
+    }
+    if (t == INT_MIN)
+      t = sample_list<32>(lst, n_sel, P, rs, fe, fp, ford, s_tok, want_cand ? cids : nullptr,
+                          want_cand ? cprobs : nullptr);
+    tok = t;
+    listed = true;
   } else {
     status = PZ_ROW_HINT_VIOLATED;
   }
-  if (tid == 0) {
+  if (lane == 0) {
     A.out[row] = tok;
     A.rng[row] = rs;
-    if (A.n_cand) A.n_cand[row] = P.mode == kModeTopK ? P.keff : 0;
+    if (A.n_cand) A.n_cand[row] = listed ? P.keff : 0;
     if (A.row_status) A.row_status[row] = status;
+  }
+  if (want_cand && !listed) {
+    for (int i = lane; i < A.cand_stride; i += 32) {
+      if (cids) cids[i] = -1;
+      if (cprobs) cprobs[i] = 0.0f;
+    }
   }
 }
 
@@ -2047,8 +2055,12 @@ cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem, cud
   return cudaGetLastError();
 }
 
-cudaError_t launch_merge(const MergeArgs &a, size_t smem, cudaStream_t st) {
-  merge_kernel<<<a.B, kSliceThreads, smem, st>>>(a);
+cudaError_t launch_merge(const MergeArgs &a, cudaStream_t st) {
+  const int r = merge_rows_per_block(a.kcap, a.G);
+  const size_t wb = merge_warp_bytes(a.kcap, a.G);
+  if (wb * static_cast<size_t>(r) > static_cast<size_t>(max_dynamic_smem())) return cudaErrorInvalidValue;
+  const unsigned grid = static_cast<unsigned>((a.B + r - 1) / r);
+  merge_kernel<<<grid, kSliceThreads, wb * r, st>>>(a, r, static_cast<int>(wb));
   return cudaGetLastError();
 }
 

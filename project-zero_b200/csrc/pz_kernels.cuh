@@ -116,8 +116,7 @@ cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem,
                         cudaStream_t st);
 size_t full_smem_bytes(int V, int hcap);
 __host__ __device__ size_t full_smem_fixed(int V, int hcap);
-cudaError_t launch_merge(const MergeArgs &a, size_t smem, cudaStream_t st);
-size_t merge_smem_bytes(int kcap);
+cudaError_t launch_merge(const MergeArgs &a, cudaStream_t st);
 cudaError_t launch_temperature(float *x, int n, float T, cudaStream_t st);
 cudaError_t launch_rng_seed(unsigned long long *s, int B,
                             unsigned long long base,

@@ -68,6 +68,26 @@ class BatchOutputs(ctypes.Structure):
                 ("reserved", ctypes.c_int32)]
 
 
+class SamplerConfigC(ctypes.Structure):
+    """pz_sampler_config as a ctypes structure (32 bytes)."""
+    _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_int32), ("top_p", ctypes.c_float),
+                ("repetition_penalty", ctypes.c_float), ("frequency_penalty", ctypes.c_float),
+                ("presence_penalty", ctypes.c_float), ("flags", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+
+
+class SamplingParams(ctypes.Structure):
+    """pz_sampling_params: a request's settings from the command line or a
+    chat-completions JSON body."""
+    _fields_ = [("cfg", SamplerConfigC), ("seed", ctypes.c_int64), ("logprobs", ctypes.c_int32),
+                ("top_logprobs", ctypes.c_int32)]
+
+    def as_config(self, B=1):
+        """The config as a CONFIG_DTYPE array of B identical rows."""
+        c = self.cfg
+        return make_configs(B, c.temperature, c.top_k, c.top_p, c.repetition_penalty,
+                            c.frequency_penalty, c.presence_penalty, c.flags)
+
+
 # pz_sampler_config, 32 bytes
 CONFIG_DTYPE = np.dtype([
     ("temperature", "<f4"), ("top_k", "<i4"), ("top_p", "<f4"),
@@ -135,6 +155,13 @@ _sig("pz_ctx_init_nccl", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, ct
 _sig("pz_sample_batch_vocab_sharded", ctypes.c_int,
      [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
       ctypes.c_int, _vp, _vp, _vp, _vp, _vp, ctypes.POINTER(BatchOutputs), _vp])
+
+
+_sig("pz_params_init_cli", None, [ctypes.POINTER(SamplingParams)])
+_sig("pz_params_init_api", None, [ctypes.POINTER(SamplingParams)])
+_sig("pz_params_from_args", ctypes.c_int,
+     [ctypes.POINTER(SamplingParams), ctypes.c_int, ctypes.POINTER(ctypes.c_char_p)])
+_sig("pz_params_from_json", ctypes.c_int, [ctypes.POINTER(SamplingParams), ctypes.c_char_p])
 
 
 class PZError(RuntimeError):
@@ -222,6 +249,22 @@ def rng_float(state):
     s = ctypes.c_ulonglong(state)
     v = _lib.pz_rng_float(ctypes.byref(s))
     return float(np.float32(v)), s.value
+
+
+def params_from_args(argv):
+    """pz_params_from_args over a command line (argv[0] is the program)."""
+    p = SamplingParams()
+    arr = (ctypes.c_char_p * len(argv))(*[a.encode() for a in argv])
+    _check(_lib.pz_params_from_args(ctypes.byref(p), len(argv), arr), "pz_params_from_args")
+    return p
+
+
+def params_from_json(body):
+    """pz_params_from_json over a chat-completions request body."""
+    p = SamplingParams()
+    _check(_lib.pz_params_from_json(ctypes.byref(p), body.encode() if isinstance(body, str) else body),
+           "pz_params_from_json")
+    return p
 
 
 def row_shard(B, world, rank):

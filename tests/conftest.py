@@ -43,6 +43,13 @@ def pz(cuda):
     return pz_sampling
 
 
+@pytest.fixture(scope="session")
+def pz_cpu():
+    """The library's host-only entry points (no kernel is launched)."""
+    import pz_sampling
+    return pz_sampling
+
+
 def pytest_terminal_summary(terminalreporter):
     """Reports the boundary cases (draws within 1e-6 of a CDF edge that gave
     a different id than the oracle) counted by the parity tests."""
