@@ -150,6 +150,7 @@ struct pz_sampler_ctx {
   uint32_t *sort_b = nullptr;
   float *full_e = nullptr;
   int64_t sort_stride = 0;
+  int64_t e_stride = 0;
   int full_grid = 0;
   // vocab sharding
   ncclComm_t comm = nullptr;
@@ -273,7 +274,9 @@ pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
   c->kcap_max = next_pow2(std::max(L.max_top_k, 1));
   c->hcap_max = L.max_history > 0 ? next_pow2(L.max_history) : 0;
   c->slices_cap = std::max(L.max_batch, 8192);
-  c->full_grid = c->num_sms;
+  // full_kernel: kFullCtasPerSm rows in flight per SM (no more CTAs than rows)
+  c->full_grid = std::min(c->num_sms * pz::kFullCtasPerSm, L.max_batch);
+  c->e_stride = (static_cast<int64_t>(L.max_vocab) + 63) / 64 * 64;
   c->sort_stride = 2 * static_cast<int64_t>(L.max_vocab);
   const int B = L.max_batch;
   bool ok = c->alloc(&c->slice_keys, static_cast<size_t>(c->slices_cap) * c->kcap_max) &&
@@ -282,7 +285,7 @@ pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
             c->alloc(&c->full_rows, B) && c->alloc(&c->n_full, 1) &&
             c->alloc(&c->sort_a, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
             c->alloc(&c->sort_b, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
-            c->alloc(&c->full_e, static_cast<size_t>(c->full_grid) * L.max_vocab);
+            c->alloc(&c->full_e, static_cast<size_t>(c->full_grid) * c->e_stride);
   if (!ok) {
     c->release();
     delete c;
@@ -520,6 +523,7 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     f.sort_b = ctx->sort_b;
     f.sort_stride = ctx->sort_stride;
     f.escr = ctx->full_e;
+    f.e_stride = ctx->e_stride;
     f.rng = rng_state;
     f.out = out;
     const size_t fsmem = pz::full_smem_bytes(V, f.hcap);

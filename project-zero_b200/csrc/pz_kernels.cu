@@ -1573,9 +1573,17 @@ __host__ __device__ size_t full_smem_fixed(int V, int hcap) {
 }
 
 size_t full_smem_bytes(int V, int hcap) {
-  // the fixed part, then as much room for in-smem sorts as fits
+  // the fixed part, then as much room for in-smem sorts as fits with
+  // kFullCtasPerSm CTAs on an SM (each also holds ~1 KB static and the
+  // 1 KB the hardware reserves per CTA)
   const size_t fixed = (full_smem_fixed(V, hcap) + 15) / 16 * 16;
-  const size_t cap = static_cast<size_t>(max_dynamic_smem());
+  int dev = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  size_t cap = static_cast<size_t>(per_sm) / kFullCtasPerSm - 4096;
+  cap = cap / 16 * 16;
+  const size_t mx = static_cast<size_t>(max_dynamic_smem());
+  if (cap > mx) cap = mx;
   return fixed < cap ? cap : fixed;
 }
 
@@ -1655,40 +1663,49 @@ __device__ __noinline__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32
 
 // Collects, in index order, the entries i < V with e[i] > 0 and
 // prob = fl(e[i] * inv) >= pmin as (~prob bits, i) into (ko, vo); returns
-// their number.  Block-wide.
+// their number.  Block-wide; e is 16-byte aligned and readable up to V
+// rounded up to a multiple of 8.
 template <int NT>
 __device__ int collect_prefix(const float *e, int V, float inv, float pmin, uint32_t *ko, uint32_t *vo,
                               int *red) {
+  constexpr int PT = 8;
   int nf = 0;
-  for (int c0 = 0; c0 < V; c0 += NT * 4) {
-    float pv[4];
-    int cnt = 0;
+  float4 a, b, an, bn;
+  auto fetch = [&](int c, float4 &x0, float4 &x1) {
+    const int i = c + threadIdx.x * PT;
+    if (i < V) {
+      x0 = *reinterpret_cast<const float4 *>(e + i);
+      x1 = *reinterpret_cast<const float4 *>(e + i + 4);
+    }
+  };
+  fetch(0, a, b);
+  for (int c0 = 0; c0 < V; c0 += NT * PT) {
+    if (c0 + NT * PT < V) fetch(c0 + NT * PT, an, bn);
+    const float ev[PT] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const int i0 = c0 + threadIdx.x * PT;
+    uint32_t keep = 0;
+    float pv[PT];
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int i = c0 + threadIdx.x * 4 + q;
-      pv[q] = -1.0f;
-      if (i < V) {
-        const float ei = e[i];
-        if (ei > 0.0f) {
-          const float pr = __fmul_rn(ei, inv);                   // top_p.c:73-74
-          if (pr >= pmin) {
-            pv[q] = pr;
-            cnt++;
-          }
-        }
+    for (int q = 0; q < PT; q++) {
+      pv[q] = 0.0f;
+      if (i0 + q < V && ev[q] > 0.0f) {
+        pv[q] = __fmul_rn(ev[q], inv);                                  // top_p.c:73-74
+        if (pv[q] >= pmin) keep |= 1u << q;
       }
     }
     int total;
-    int pos = nf + block_exscan_int<NT>(cnt, total, red);
+    int pos = nf + block_exscan_int<NT>(__popc(keep), total, red);
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      if (pv[q] >= 0.0f) {
+    for (int q = 0; q < PT; q++) {
+      if ((keep >> q) & 1u) {
         ko[pos] = ~__float_as_uint(pv[q]);
-        vo[pos] = static_cast<uint32_t>(c0 + threadIdx.x * 4 + q);
+        vo[pos] = static_cast<uint32_t>(i0 + q);
         pos++;
       }
     }
     nf += total;
+    a = an;
+    b = bn;
   }
   __threadfence_block();
   __syncthreads();
@@ -1696,7 +1713,7 @@ __device__ int collect_prefix(const float *e, int V, float inv, float pmin, uint
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kFullThreads, 1) full_kernel(const FullArgs A) {
+__global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(const FullArgs A) {
   constexpr int NT = kFullThreads;
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ SeqShared ssh;
@@ -1717,7 +1734,7 @@ __global__ void __launch_bounds__(kFullThreads, 1) full_kernel(const FullArgs A)
   const int sm_cap = A.smem_sort_cap;
   uint32_t *sm_v0 = sm_k0 + sm_cap, *sm_k1 = sm_v0 + sm_cap, *sm_v1 = sm_k1 + sm_cap;
   // global scratch of this CTA: e values, then two (key, value) buffers
-  float *E = A.escr + static_cast<size_t>(blockIdx.x) * A.sort_stride / 2;
+  float *E = A.escr + static_cast<size_t>(blockIdx.x) * A.e_stride;
   uint32_t *g_k0 = A.sort_a + static_cast<size_t>(blockIdx.x) * A.sort_stride;
   uint32_t *g_v0 = g_k0 + A.sort_stride / 2;
   uint32_t *g_k1 = A.sort_b + static_cast<size_t>(blockIdx.x) * A.sort_stride;
@@ -1771,20 +1788,40 @@ __global__ void __launch_bounds__(kFullThreads, 1) full_kernel(const FullArgs A)
     unsigned long long rs = A.rng[row];
     const bool topp = P.mode != kModeSoftmaxFull;
     const float thr = __fsub_rn(mx, 20.0f);                             // top_p.c:53
-    // pass 1: e values (stored), the exact normaliser, the bins
-    const SeqResult s1 = seq_scan<NT, 4>(
-        V,
-        [&](int i) {
-          const float v = vof(i);
-          float e = 0.0f;
-          if (!topp || v >= thr) {                                       // :58
-            e = cr_expf(__fsub_rn(v, mx));                               // :59, softmax.c:13
-            if (topp) atomicAdd(&bins[ebin(e)], 1u);
-          }
-          E[i] = e;
-          return e;
-        },
-        kSeqNone, 0.0f, ssh, head, kSeqHead);
+    // pass 1a: e values (stored) and the bins, the row read with 16-byte
+    // loads, no barriers
+    {
+      auto elem = [&](int i, float x) {
+        if (hist_on && ((bitmap[i >> 5] >> (i & 31)) & 1u)) x = penalize(x, sorted_count(hl, nh, i), P);
+        const float v = temper(x, P);
+        float e = 0.0f;
+        if (!topp || v >= thr) {                                         // top_p.c:58
+          e = cr_expf(__fsub_rn(v, mx));                                 // :59, softmax.c:13
+          if (topp) atomicAdd(&bins[ebin(e)], 1u);
+        }
+        E[i] = e;
+      };
+      constexpr int VEC = Vec16<T>::N;
+      const uintptr_t addr = reinterpret_cast<uintptr_t>(rowp);
+      int lead = static_cast<int>(((16u - (addr & 15u)) & 15u) / sizeof(T));
+      if (lead > V) lead = V;
+      const int nvec = (V - lead) / VEC;
+      const int body_end = lead + nvec * VEC;
+      for (int i = tid; i < lead; i += NT) elem(i, load_scalar<T>(rowp, i));
+      for (int i = body_end + tid; i < V; i += NT) elem(i, load_scalar<T>(rowp, i));
+      const T *body = rowp + lead;
+#pragma unroll 2
+      for (int q = tid; q < nvec; q += NT) {
+        float xv[VEC];
+        Vec16<T>::load(body, q, xv);
+#pragma unroll
+        for (int w = 0; w < VEC; w++) elem(lead + q * VEC + w, xv[w]);
+      }
+    }
+    __syncthreads();
+    // pass 1b: the exact normaliser over the stored e values
+    const SeqResult s1 = seq_scan<NT, 4>(V, [&](int i) { return E[i]; }, kSeqNone, 0.0f, ssh, head,
+                                         kSeqHead);
     const float inv = __fdiv_rn(1.0f, s1.s);                            // :72, softmax.c:18
     int tok;
     if (!topp) {

@@ -18,7 +18,8 @@
 namespace pz {
 
 constexpr int kSliceThreads = 256;
-constexpr int kFullThreads = 1024;
+constexpr int kFullThreads = 512;
+constexpr int kFullCtasPerSm = 2;   // full_kernel rows in flight per SM
 constexpr int kCapB = 1024;   // candidate buffer room above the list length
 constexpr int kRowBits = 2;   // row_flags bits
 
@@ -84,7 +85,8 @@ struct FullArgs {
   uint32_t *sort_a;     // [gridDim][2*maxV] (prob key, index) pairs
   uint32_t *sort_b;
   int64_t sort_stride;  // uint32 elements per CTA in sort_a/sort_b
-  float *escr;          // [gridDim][maxV] e values of the CTA's row
+  float *escr;          // [gridDim][e_stride] e values of the CTA's row
+  int64_t e_stride;     // floats per CTA in escr (a multiple of 64)
   int smem_sort_cap;    // (key, value) entries an in-smem sort holds
   unsigned long long *rng;
   int32_t *out;

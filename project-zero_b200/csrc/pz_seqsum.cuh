@@ -163,14 +163,17 @@ struct SeqResult {
 
 // Replays s = fl(s + x_j) for j = 0..n-1 (x_j = get(j) >= 0) starting from
 // s = 0.  With a target, stops at the first j where s_j >= target (kSeqGE)
-// or s_j > target (kSeqGT).  Block-wide call; get(j) is called once for
-// every j the scan reaches.
+// or s_j > target (kSeqGT).  Block-wide call.  get must be a pure function
+// of j (the next chunk's terms are fetched while the current one is
+// scanned).
 //
 // The first head_cap terms (the running sum doubles, and so leaves its
 // binade, most often early on: about once per doubling of the terms seen)
 // are evaluated by all threads into head_buf and added in order by one
 // thread; the rest go E consecutive terms per thread per chunk through the
 // parallel replay, which restarts only at the few binade crossings left.
+// The maps of a thread's terms are not kept: they are recomputed from the
+// terms (a few integer operations) where the prefixes are needed.
 template <int NT, int E, typename Get>
 __device__ SeqResult seq_scan(int n, Get get, int kind, float target,
                               SeqShared &sh, float *head_buf, int head_cap) {
@@ -192,13 +195,17 @@ __device__ SeqResult seq_scan(int n, Get get, int kind, float target,
     sh.done_pos = done;
   }
   __syncthreads();
-  for (int c0 = K; c0 < n && sh.done_pos < 0; c0 += NT * E) {
-    float x[E];
+  float x[E], xn[E];
+  auto fetch = [&](int c, float(&dst)[E]) {
 #pragma unroll
     for (int e = 0; e < E; e++) {
-      const int j = c0 + tid * E + e;
-      x[e] = j < n ? get(j) : 0.0f;
+      const int j = c + tid * E + e;
+      dst[e] = j < n ? get(j) : 0.0f;
     }
+  };
+  if (K < n && sh.done_pos < 0) fetch(K, x);
+  for (int c0 = K; c0 < n && sh.done_pos < 0; c0 += NT * E) {
+    if (c0 + NT * E < n) fetch(c0 + NT * E, xn);  // in flight during this chunk
     int start = c0;
     bool chunk_done = false;
     while (!chunk_done) {
@@ -219,13 +226,11 @@ __device__ SeqResult seq_scan(int n, Get get, int kind, float target,
           thrN = (q != q) ? ~0ull : (f < 0.0 ? 0ull : (f >= 1e15 ? ~0ull : static_cast<unsigned long long>(f) + 1ull));
         }
       }
-      SeqMap f[E];
       SeqMap F = seq_identity();
 #pragma unroll
       for (int e = 0; e < E; e++) {
         const int j = c0 + tid * E + e;
-        f[e] = (j >= start && j < n) ? seq_elem(x[e], eu) : seq_identity();
-        F = seq_compose(F, f[e]);
+        if (j >= start && j < n) F = seq_compose(F, seq_elem(x[e], eu));
       }
       if (tid == 0) {
         sh.cross = 0x7FFFFFFF;
@@ -241,7 +246,7 @@ __device__ SeqResult seq_scan(int n, Get get, int kind, float target,
       for (int e = 0; e < E; e++) {
         const int j = c0 + tid * E + e;
         if (j >= start && j < n && mycross == 0x7FFFFFFF && myhit == 0x7FFFFFFF) {
-          const unsigned long long Nn = seq_apply(f[e], N);
+          const unsigned long long Nn = seq_apply(seq_elem(x[e], eu), N);
           if (Nn >= kSeqLimit) {
             mycross = j;
             Nc = N;
@@ -279,7 +284,8 @@ __device__ SeqResult seq_scan(int n, Get get, int kind, float target,
       __syncthreads();
       if (sh.done_pos >= 0) break;
     }
-    if (sh.done_pos >= 0) break;
+#pragma unroll
+    for (int e = 0; e < E; e++) x[e] = xn[e];
   }
   SeqResult r;
   r.s = sh.s;
