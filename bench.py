@@ -735,6 +735,24 @@ def leg_config1(C):
         tot, _ = C.timed(graph.replay, 3, 1)
         res[f"{name}_device_graph_us_per_draw"] = tot / 3 / N * 1000.0
         del graph
+    # the library's own decode step (pz_decode_step_*): fresh logits copied
+    # into the fixed buffer, then the step graph (sample, window append)
+    buf = torch.empty(1, V, device=C.dev)
+    cfg = pz.configs_to_device(make_configs(1, 0.8, 40, 0.95, 1.1), C.dev)
+    rng = torch.tensor([42], dtype=torch.int64, device=C.dev)
+    out1 = torch.empty(1, dtype=torch.int32, device=C.dev)
+    ring = hist.view(1, 64)
+    step = pz.DecodeStep(s, buf, cfg, rng, out1, ring, max_top_k=40, max_history=64, no_full_vocab=True)
+    it = [0]
+
+    def one():
+        buf.copy_(xs[it[0] % N:it[0] % N + 1])
+        step.launch()
+        it[0] += 1
+
+    tot, _ = C.timed(one, N, 5)
+    res["pipeline_decode_step_us_per_draw"] = tot / N * 1000.0
+    step.close()
     s.close()
     # the drop-in host calls of the reference's generate loop (generate.c:154-156)
     xh = xs[:16].cpu().numpy()

@@ -283,6 +283,43 @@ pz_status pz_rng_seed_batch(unsigned long long *rng_state, int B,
                             const unsigned long long *seeds, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* The generate loop on the device.                                          */
+
+/* Appends each row's sampled id to its history window: tokens[r] goes to
+ * hist_ring[r * W + (*counter % W)], then *counter advances by one (all on
+ * `stream`, device pointers).  Penalties count the ids of a row's window, so
+ * the ring order does not matter; slots holding -1 (or any id outside
+ * [0, V)) are ignored, so a window starts as -1s or the prompt's last ids.
+ * The window is passed to pz_sample_batch as hist = hist_ring, hist_off[r] =
+ * r * W.  (The reference keeps no history: its loop only draws, generate.c
+ * :137-170.) */
+pz_status pz_history_append(int32_t *hist_ring, int B, int W, const int32_t *tokens,
+                            int32_t *counter, void *stream);
+
+/* One sampling step of the generate loop (reference
+ * src/transformer/generate.c:137-170) recorded once as a CUDA graph and
+ * replayed every step: sample the B rows of the fixed logits buffer the LM
+ * head writes (as RunState.logits is rewritten each step in the reference,
+ * forward.c:221), advance the rows' RNG states in place, and append the
+ * sampled ids to the history window (hist_ring of W slots per row, or NULL
+ * and W = 0 for no penalty window).  Device pointers, fixed for the step's
+ * life.  Seed the states once with pz_rng_seed_batch (for instance from
+ * pz_sampling_params.seed: the reference parses --seed but seeds with
+ * time(NULL), generate.c:126).  Creation captures on a private stream and
+ * allocates; launches allocate nothing. */
+typedef struct pz_decode_step pz_decode_step;
+pz_status pz_decode_step_create(pz_sampler_ctx *ctx, const void *logits, pz_dtype dtype,
+                                int B, int V, int64_t ld,
+                                const pz_sampler_config *cfg, int32_t *hist_ring,
+                                int W, unsigned long long *rng_state,
+                                int32_t *out_tokens, const pz_batch_hints *hints,
+                                pz_decode_step **step);
+pz_status pz_decode_step_launch(pz_decode_step *step, void *stream);
+/* Steps launched so far (synchronous read of the device counter). */
+pz_status pz_decode_step_count(const pz_decode_step *step, int32_t *steps);
+pz_status pz_decode_step_destroy(pz_decode_step *step);
+
+/* ------------------------------------------------------------------------ */
 /* Multi-GPU.                                                                */
 
 /* Row sharding: the contiguous row range [*begin, *begin + *count) that rank

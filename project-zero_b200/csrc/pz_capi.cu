@@ -396,8 +396,11 @@ constexpr int kProfEvents = 5;
 
 // The next profiling slot of the context (nullptr when timing is off or
 // its slots are used up).
-static cudaEvent_t *next_prof_slot(pz_sampler_ctx *ctx) {
+static cudaEvent_t *next_prof_slot(pz_sampler_ctx *ctx, cudaStream_t st) {
   if ((ctx->prof_used + 1) * kProfEvents > static_cast<int>(ctx->prof.size())) return nullptr;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+    return nullptr;  // no timing events inside a captured graph
   cudaEvent_t *ev = &ctx->prof[ctx->prof_used * kProfEvents];
   ctx->prof_used++;
   return ev;
@@ -499,7 +502,7 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   const bool full_pass = !emit && !no_full;
   if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t), st) != cudaSuccess)
     return fail(PZ_ERR_CUDA);
-  cudaEvent_t *ev = next_prof_slot(ctx);
+  cudaEvent_t *ev = next_prof_slot(ctx, st);
   if (ev) cudaEventRecord(ev[0], st);
   cudaError_t ce = pz::launch_slice(a, dtype, smem, st);
   if (ce != cudaSuccess) return fail_cuda(ce);
@@ -736,6 +739,120 @@ pz_status pz_rng_seed_batch(unsigned long long *rng_state, int B,
   if (pz::launch_rng_seed(rng_state, B, seed_base, seeds,
                           static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return fail(PZ_ERR_CUDA);
+  return PZ_OK;
+}
+
+pz_status pz_history_append(int32_t *hist_ring, int B, int W, const int32_t *tokens,
+                            int32_t *counter, void *stream) {
+  if (!hist_ring || !tokens || !counter || B < 0 || W <= 0) return fail(PZ_ERR_INVALID_ARGS);
+  if (B == 0) return PZ_OK;
+  const cudaError_t e =
+      pz::launch_history_append(hist_ring, B, W, tokens, counter, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PZ_OK : fail_cuda(e);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// The generate loop's sampling step as one CUDA graph (reference
+// src/transformer/generate.c:137-170, per step: sample, then the sampled id
+// joins the penalty window), with the RNG states and the window on the
+// device from one step to the next.
+// ---------------------------------------------------------------------------
+struct pz_decode_step {
+  pz_sampler_ctx *ctx = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int32_t *counter = nullptr;   // steps taken (device)
+  int32_t *hist_off = nullptr;  // r * W (device)
+};
+
+namespace {
+__global__ void ring_offsets_kernel(int32_t *off, int B, int W) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r <= B) off[r] = r * W;
+}
+void step_release(pz_decode_step *s) {
+  if (s->exec) cudaGraphExecDestroy(s->exec);
+  if (s->graph) cudaGraphDestroy(s->graph);
+  if (s->counter) cudaFree(s->counter);
+  if (s->hist_off) cudaFree(s->hist_off);
+  delete s;
+}
+}  // namespace
+
+extern "C" {
+
+pz_status pz_decode_step_create(pz_sampler_ctx *ctx, const void *logits, pz_dtype dtype, int B, int V,
+                                int64_t ld, const pz_sampler_config *cfg, int32_t *hist_ring, int W,
+                                unsigned long long *rng_state, int32_t *out_tokens,
+                                const pz_batch_hints *hints, pz_decode_step **step) {
+  if (!ctx || !step || !logits || !cfg || !rng_state || !out_tokens || B <= 0 || V <= 0 ||
+      (hist_ring != nullptr) != (W > 0) || W < 0)
+    return fail(PZ_ERR_INVALID_ARGS);
+  *step = nullptr;
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(PZ_ERR_CUDA);
+  pz_decode_step *s = new pz_decode_step();
+  s->ctx = ctx;
+  cudaStream_t cs = nullptr;
+  cudaError_t e = cudaMalloc(&s->counter, sizeof(int32_t));
+  if (e == cudaSuccess) e = cudaMemset(s->counter, 0, sizeof(int32_t));
+  if (e == cudaSuccess && hist_ring) {
+    e = cudaMalloc(&s->hist_off, sizeof(int32_t) * (B + 1));
+    if (e == cudaSuccess) {
+      ring_offsets_kernel<<<(B + 256) / 256, 256>>>(s->hist_off, B, W);
+      e = cudaGetLastError();
+    }
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    step_release(s);
+    return fail_cuda(e);
+  }
+  // one sampling call and the window update, recorded as a graph
+  e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+  pz_status ps = PZ_OK;
+  if (e == cudaSuccess) {
+    ps = sample_impl(ctx, logits, dtype, B, V, ld, 0, V, cfg, hist_ring, s->hist_off, rng_state,
+                     out_tokens, hints, nullptr, cs, false);
+    if (ps == PZ_OK && hist_ring)
+      e = pz::launch_history_append(hist_ring, B, W, out_tokens, s->counter, cs);
+    else if (ps == PZ_OK)
+      e = pz::launch_history_append(out_tokens, 0, 1, out_tokens, s->counter, cs);  // the step count only
+    const cudaError_t e2 = cudaStreamEndCapture(cs, &s->graph);
+    if (e == cudaSuccess) e = e2;
+  }
+  if (ps == PZ_OK && e == cudaSuccess) e = cudaGraphInstantiate(&s->exec, s->graph, 0);
+  cudaStreamDestroy(cs);
+  if (ps != PZ_OK || e != cudaSuccess) {
+    step_release(s);
+    return ps != PZ_OK ? ps : fail_cuda(e);
+  }
+  *step = s;
+  return PZ_OK;
+}
+
+pz_status pz_decode_step_launch(pz_decode_step *step, void *stream) {
+  if (!step) return fail(PZ_ERR_INVALID_ARGS);
+  DeviceGuard g(step->ctx->device);
+  const cudaError_t e = cudaGraphLaunch(step->exec, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PZ_OK : fail_cuda(e);
+}
+
+pz_status pz_decode_step_count(const pz_decode_step *step, int32_t *steps) {
+  if (!step || !steps) return fail(PZ_ERR_INVALID_ARGS);
+  DeviceGuard g(step->ctx->device);
+  const cudaError_t e = cudaMemcpy(steps, step->counter, sizeof(int32_t), cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? PZ_OK : fail_cuda(e);
+}
+
+pz_status pz_decode_step_destroy(pz_decode_step *step) {
+  if (!step) return PZ_OK;
+  DeviceGuard g(step->ctx->device);
+  cudaDeviceSynchronize();
+  step_release(step);
   return PZ_OK;
 }
 

@@ -2037,6 +2037,21 @@ __global__ void temperature_kernel(float *x, int n, float inv) {
   if (i < n) x[i] = __fmul_rn(x[i], inv);   // temperature.c:11-20
 }
 
+// The generate loop's history window: each row's sampled id goes to slot
+// (*counter % W) of its W-slot ring (penalties count ids, so the ring's
+// order does not matter; slots never written hold -1, which the contract
+// ignores).  counter_step_kernel then moves to the next slot.
+__global__ void history_append_kernel(int32_t *ring, int B, int W, const int32_t *tokens,
+                                      const int32_t *counter) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < B) {
+    const int pos = *counter % W;
+    ring[static_cast<size_t>(r) * W + pos] = tokens[r];
+  }
+}
+
+__global__ void counter_step_kernel(int32_t *counter) { *counter += 1; }
+
 __global__ void rng_seed_kernel(unsigned long long *s, int B,
                                 unsigned long long base,
                                 const unsigned long long *seeds) {
@@ -2105,6 +2120,17 @@ cudaError_t launch_temperature(float *x, int n, float T, cudaStream_t st) {
   if (T < 1e-6f) T = 1e-6f;                 // temperature.c:10
   const float inv = 1.0f / T;
   temperature_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, n, inv);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_history_append(int32_t *ring, int B, int W, const int32_t *tokens,
+                                  int32_t *counter, cudaStream_t st) {
+  if (B > 0) {
+    history_append_kernel<<<(B + 255) / 256, 256, 0, st>>>(ring, B, W, tokens, counter);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  counter_step_kernel<<<1, 1, 0, st>>>(counter);
   return cudaGetLastError();
 }
 

@@ -120,6 +120,8 @@ size_t full_smem_bytes(int V, int hcap);
 __host__ __device__ size_t full_smem_fixed(int V, int hcap);
 cudaError_t launch_merge(const MergeArgs &a, cudaStream_t st);
 cudaError_t launch_temperature(float *x, int n, float T, cudaStream_t st);
+cudaError_t launch_history_append(int32_t *ring, int B, int W, const int32_t *tokens,
+                                  int32_t *counter, cudaStream_t st);
 cudaError_t launch_rng_seed(unsigned long long *s, int B,
                             unsigned long long base,
                             const unsigned long long *seeds, cudaStream_t st);

@@ -164,6 +164,15 @@ _sig("pz_params_from_args", ctypes.c_int,
 _sig("pz_params_from_json", ctypes.c_int, [ctypes.POINTER(SamplingParams), ctypes.c_char_p])
 
 
+_sig("pz_history_append", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp])
+_sig("pz_decode_step_create", ctypes.c_int,
+     [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp, ctypes.c_int, _vp, _vp,
+      ctypes.POINTER(BatchHints), ctypes.POINTER(_vp)])
+_sig("pz_decode_step_launch", ctypes.c_int, [_vp, _vp])
+_sig("pz_decode_step_count", ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int32)])
+_sig("pz_decode_step_destroy", ctypes.c_int, [_vp])
+
+
 class PZError(RuntimeError):
     def __init__(self, status, what=""):
         self.status = status
@@ -417,6 +426,52 @@ class Sampler:
             _stream_handle(stream))
         _check(st, "pz_sample_batch_vocab_sharded")
         return out
+
+
+class DecodeStep:
+    """One sampling step of the generate loop as a CUDA graph
+    (pz_decode_step_*): the fixed logits buffer sampled, the RNG states
+    advanced and each sampled id appended to its row's history window, all
+    on the device.  The tensors given here stay bound to the step."""
+
+    def __init__(self, sampler, logits, cfg, rng_state, out, hist_ring=None, *, max_top_k=0,
+                 max_history=0, no_full_vocab=False):
+        B, V = logits.shape
+        W = 0 if hist_ring is None else hist_ring.shape[1]
+        hints = BatchHints(max_top_k, max_history, 1 if no_full_vocab else 0, 0)
+        h = _vp()
+        _check(_lib.pz_decode_step_create(sampler._h, _ptr(logits), Sampler._dtype_code(logits), B, V,
+                                          logits.stride(0), _ptr(cfg), _ptr(hist_ring), W, _ptr(rng_state),
+                                          _ptr(out), ctypes.byref(hints), ctypes.byref(h)),
+               "pz_decode_step_create")
+        self._h = h
+        self._keep = (sampler, logits, cfg, rng_state, out, hist_ring)
+
+    def launch(self, stream=None):
+        _check(_lib.pz_decode_step_launch(self._h, _stream_handle(stream)), "pz_decode_step_launch")
+
+    def steps(self):
+        n = ctypes.c_int32()
+        _check(_lib.pz_decode_step_count(self._h, ctypes.byref(n)), "pz_decode_step_count")
+        return n.value
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.pz_decode_step_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def history_append(hist_ring, tokens, counter, stream=None):
+    """pz_history_append: tokens[r] into hist_ring[r, counter % W], counter += 1."""
+    B, W = hist_ring.shape
+    _check(_lib.pz_history_append(_ptr(hist_ring), B, W, _ptr(tokens), _ptr(counter), _stream_handle(stream)),
+           "pz_history_append")
 
 
 STATIC_MAX_BATCH = 1024
