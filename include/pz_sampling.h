@@ -196,7 +196,16 @@ typedef struct pz_batch_hints {
  *       for it (A5 steps: e*inv in list order, 0 for entries the max-20
  *       filter dropped; A4: e/sum); other rows get -1 / 0.
  *   n_cand: [B] number of list entries written (k_eff, or 0).
- *   row_status: [B] PZ_ROW_* codes. */
+ *   row_status: [B] PZ_ROW_* codes.
+ *   token_logprob: [B] OpenAI-style log-probability of the sampled id: its
+ *       value minus the log-sum-exp of the whole row, over the penalised,
+ *       tempered values (greedy rows: penalised, untempered) — the
+ *       distribution before top-k / top-p truncation; NaN for a row with no
+ *       token.  No counterpart in the reference.
+ *   cand_logprobs: [B x cand_stride] the same for the list entries (the
+ *       row's most likely ids, in order: OpenAI's top_logprobs), -inf past
+ *       n_cand.  Asking for either costs one more read of each row; fp32
+ *       accuracy (~1e-5).  Not available from the vocab-sharded call. */
 typedef struct pz_batch_outputs {
   int32_t *cand_ids;
   float *cand_probs;
@@ -204,6 +213,8 @@ typedef struct pz_batch_outputs {
   int32_t *row_status;
   int32_t cand_stride;
   int32_t reserved;
+  float *token_logprob;
+  float *cand_logprobs;
 } pz_batch_outputs;
 
 /* Samples B rows.  All pointers are DEVICE pointers on the ctx's device.
@@ -295,6 +306,25 @@ pz_status pz_rng_seed_batch(unsigned long long *rng_state, int B,
  * :137-170.) */
 pz_status pz_history_append(int32_t *hist_ring, int B, int W, const int32_t *tokens,
                             int32_t *counter, void *stream);
+
+/* The hand-off from the LM head.  pz_lm_head_logits is the classifier of
+ * reference src/transformer/forward.c:102-165 in its bf16 form
+ * (parallel_matmul_bf16): logits[b][v] = sum_d hidden[b][d] * w_cls[v][d],
+ * hidden fp32 [B x dim], w_cls bf16 bits [V x dim] (row v = token v's
+ * classifier row), logits fp32 rows of stride ld, all device pointers, on
+ * `stream` (dim a multiple of 8, hidden and w_cls 16-byte aligned).
+ * pz_sample_from_hidden runs it and pz_sample_batch on that buffer back to
+ * back on the stream: the logits never leave the device.  (fp32 sums in an
+ * order of its own: the LM head is outside the sampler's parity contract.) */
+pz_status pz_lm_head_logits(pz_sampler_ctx *ctx, const float *hidden, int B, int dim,
+                            const uint16_t *w_cls, int V, float *logits, int64_t ld,
+                            void *stream);
+pz_status pz_sample_from_hidden(pz_sampler_ctx *ctx, const float *hidden, int B, int dim,
+                                const uint16_t *w_cls, int V, float *logits, int64_t ld,
+                                const pz_sampler_config *cfg, const int32_t *hist,
+                                const int32_t *hist_off, unsigned long long *rng_state,
+                                int32_t *out_tokens, const pz_batch_hints *hints,
+                                const pz_batch_outputs *outputs, void *stream);
 
 /* One sampling step of the generate loop (reference
  * src/transformer/generate.c:137-170) recorded once as a CUDA graph and

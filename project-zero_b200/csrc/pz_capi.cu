@@ -425,7 +425,11 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   if ((hist == nullptr) != (hist_off == nullptr)) return fail(PZ_ERR_INVALID_ARGS);
   if (B == 0) return PZ_OK;
   if (B > ctx->lim.max_batch || V > ctx->lim.max_vocab) return fail(PZ_ERR_UNSUPPORTED);
-  if (outputs && (outputs->cand_ids || outputs->cand_probs) && outputs->cand_stride < 1)
+  if (outputs && (outputs->cand_ids || outputs->cand_probs || outputs->cand_logprobs) &&
+      outputs->cand_stride < 1)
+    return fail(PZ_ERR_INVALID_ARGS);
+  // list log-probabilities need the list: its ids and length
+  if (outputs && outputs->cand_logprobs && (!outputs->cand_ids || !outputs->n_cand))
     return fail(PZ_ERR_INVALID_ARGS);
   int kmax = ctx->lim.max_top_k, hmax = ctx->lim.max_history, no_full = 0;
   if (hints) {
@@ -535,6 +539,28 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     f.smem_sort_cap = static_cast<int>((fsmem - fixed) / 16);
     const int grid = std::min(ctx->full_grid, B);
     ce = pz::launch_full(f, dtype, grid, fsmem, st);
+    if (ce != cudaSuccess) return fail_cuda(ce);
+    kernels++;
+  }
+  if (!emit && outputs && (outputs->token_logprob || outputs->cand_logprobs)) {
+    pz::LogprobArgs l{};
+    l.logits = logits;
+    l.ld = ld;
+    l.V = V;
+    l.B = B;
+    l.cfg = cfg;
+    l.hist = hist;
+    l.hist_off = hist_off;
+    l.hcap = a.hcap > 0 ? next_pow2(a.hcap) : 0;
+    l.tokens = out;
+    l.cand_ids = outputs->cand_ids;
+    l.n_cand = outputs->n_cand;
+    l.cand_stride = outputs->cand_stride;
+    l.token_logprob = outputs->token_logprob;
+    l.cand_logprobs = outputs->cand_logprobs;
+    if (pz::logprob_smem_bytes(V, l.hcap) > static_cast<size_t>(pz::max_dynamic_smem()))
+      return fail(PZ_ERR_UNSUPPORTED);
+    ce = pz::launch_logprob(l, dtype, st);
     if (ce != cudaSuccess) return fail_cuda(ce);
     kernels++;
   }
@@ -740,6 +766,33 @@ pz_status pz_rng_seed_batch(unsigned long long *rng_state, int B,
                           static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return fail(PZ_ERR_CUDA);
   return PZ_OK;
+}
+
+pz_status pz_lm_head_logits(pz_sampler_ctx *ctx, const float *hidden, int B, int dim,
+                            const uint16_t *w_cls, int V, float *logits, int64_t ld, void *stream) {
+  if (!ctx || !hidden || !w_cls || !logits || B <= 0 || dim <= 0 || V <= 0 || ld < V || dim % 8 != 0)
+    return fail(PZ_ERR_INVALID_ARGS);
+  if (sizeof(float) * 8 * static_cast<size_t>(dim) > static_cast<size_t>(pz::max_dynamic_smem()))
+    return fail(PZ_ERR_UNSUPPORTED);
+  if ((reinterpret_cast<uintptr_t>(w_cls) & 15u) != 0 || (reinterpret_cast<uintptr_t>(hidden) & 15u) != 0)
+    return fail(PZ_ERR_INVALID_ARGS);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(PZ_ERR_CUDA);
+  const cudaError_t e = pz::launch_lm_head(hidden, B, dim, w_cls, V, logits, ld, ctx->num_sms,
+                                           static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PZ_OK : fail_cuda(e);
+}
+
+pz_status pz_sample_from_hidden(pz_sampler_ctx *ctx, const float *hidden, int B, int dim,
+                                const uint16_t *w_cls, int V, float *logits, int64_t ld,
+                                const pz_sampler_config *cfg, const int32_t *hist,
+                                const int32_t *hist_off, unsigned long long *rng_state,
+                                int32_t *out_tokens, const pz_batch_hints *hints,
+                                const pz_batch_outputs *outputs, void *stream) {
+  const pz_status s = pz_lm_head_logits(ctx, hidden, B, dim, w_cls, V, logits, ld, stream);
+  if (s != PZ_OK) return s;
+  return pz_sample_batch(ctx, logits, PZ_DTYPE_F32, B, V, ld, cfg, hist, hist_off, rng_state, out_tokens,
+                         hints, outputs, stream);
 }
 
 pz_status pz_history_append(int32_t *hist_ring, int B, int W, const int32_t *tokens,
@@ -956,6 +1009,7 @@ pz_status pz_sample_batch_vocab_sharded(
     const pz_batch_outputs *outputs, void *stream) {
   if (!ctx || !rng_state || !out_tokens) return fail(PZ_ERR_INVALID_ARGS);
   if (!ctx->comm) return fail(ctx->comm_failed ? PZ_ERR_NCCL : PZ_ERR_INVALID_ARGS);
+  if (outputs && (outputs->token_logprob || outputs->cand_logprobs)) return fail(PZ_ERR_UNSUPPORTED);
   if (outputs && (outputs->cand_ids || outputs->cand_probs) &&
       outputs->cand_stride < std::max(ctx->lim.max_top_k, 1))
     return fail(PZ_ERR_INVALID_ARGS);

@@ -2030,6 +2030,204 @@ __global__ void __launch_bounds__(kSliceThreads) merge_kernel(const MergeArgs A,
 }
 
 // ---------------------------------------------------------------------------
+// logprob_kernel: OpenAI-style log-probabilities from the same row (no
+// counterpart in the reference, whose loop returns ids only).  The
+// distribution is the one the sampler draws from before any truncation:
+// softmax over the whole row of the penalised, tempered values (greedy rows:
+// of the penalised values).  One CTA per row: the row read once with 16-byte
+// loads, an online log-sum-exp per thread (running maximum, rescaled sum),
+// combined in double; then v_token - LSE and v_entry - LSE for the row's
+// list.  fp32 exps, so the outputs are accurate to ~1e-5 (not bit-exact
+// with anything: the reference has no such output).
+// ---------------------------------------------------------------------------
+size_t logprob_smem_bytes(int V, int hcap) {
+  return sizeof(uint32_t) * (static_cast<size_t>(V) / 32 + 2) + sizeof(int32_t) * static_cast<size_t>(hcap);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSliceThreads) logprob_kernel(const LogprobArgs A) {
+  constexpr int NT = kSliceThreads;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ double s_m[NT / 32], s_s[NT / 32];
+  __shared__ int s_nh;
+  __shared__ float s_lse;
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int V = A.V;
+  const int bm_words = V / 32 + 2;
+  uint32_t *bitmap = reinterpret_cast<uint32_t *>(smem);
+  int32_t *hl = reinterpret_cast<int32_t *>(bitmap + bm_words);
+  const RowPlan P = plan_row(A.cfg[row], V);
+  const bool greedy = P.mode == kModeGreedy;
+  const T *rowp = static_cast<const T *>(A.logits) + static_cast<size_t>(row) * static_cast<size_t>(A.ld);
+  int H = 0;
+  const int32_t *hrow = nullptr;
+  if (A.hist != nullptr && A.hist_off != nullptr && P.pen_on) {
+    const int h0 = A.hist_off[row];
+    H = A.hist_off[row + 1] - h0;
+    hrow = A.hist + h0;
+  }
+  const bool hist_on = H > 0 && H <= A.hcap;
+  if (tid == 0) s_nh = 0;
+  if (hist_on)
+    for (int i = tid; i < bm_words; i += NT) bitmap[i] = 0u;
+  __syncthreads();
+  int nh = 0;
+  if (hist_on) {
+    for (int j = tid; j < H; j += NT) {
+      const int t = hrow[j];
+      if (t >= 0 && t < V) {
+        hl[atomicAdd(&s_nh, 1)] = t;
+        atomicOr(&bitmap[t >> 5], 1u << (t & 31));
+      }
+    }
+    __syncthreads();
+    nh = s_nh;
+    int np2 = 1;
+    while (np2 < nh) np2 <<= 1;
+    for (int i = nh + tid; i < np2; i += NT) hl[i] = INT_MAX;
+    block_sort_asc_i32<NT>(hl, np2);
+  }
+  auto value = [&](int i, float x) -> float {  // the drawn-from value of column i
+    if (hist_on && ((bitmap[i >> 5] >> (i & 31)) & 1u)) x = penalize(x, sorted_count(hl, nh, i), P);
+    return greedy ? x : temper(x, P);
+  };
+  float m = -INFINITY, sum = 0.0f;
+  auto add = [&](float v) {
+    if (!(v > -INFINITY)) return;  // -inf adds nothing; NaN is left out
+    if (v > m) {
+      sum = sum * expf(m - v) + 1.0f;
+      m = v;
+    } else {
+      sum += expf(v - m);
+    }
+  };
+  constexpr int VEC = Vec16<T>::N;
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(rowp);
+  int lead = static_cast<int>(((16u - (addr & 15u)) & 15u) / sizeof(T));
+  if (lead > V) lead = V;
+  const int nvec = (V - lead) / VEC;
+  const int body_end = lead + nvec * VEC;
+  for (int i = tid; i < lead; i += NT) add(value(i, load_scalar<T>(rowp, i)));
+  for (int i = body_end + tid; i < V; i += NT) add(value(i, load_scalar<T>(rowp, i)));
+  const T *body = rowp + lead;
+  for (int q = tid; q < nvec; q += NT) {
+    float xv[VEC];
+    Vec16<T>::load(body, q, xv);
+#pragma unroll
+    for (int w = 0; w < VEC; w++) add(value(lead + q * VEC + w, xv[w]));
+  }
+  // combine (m, sum) pairs: warp, then block, in double
+  double dm = m, ds = sum;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double om = __shfl_xor_sync(0xFFFFFFFFu, dm, o), os = __shfl_xor_sync(0xFFFFFFFFu, ds, o);
+    const double nm = dm > om ? dm : om;
+    ds = (nm == -INFINITY) ? 0.0 : ds * exp(dm - nm) + os * exp(om - nm);
+    dm = nm;
+  }
+  if (lane == 0) {
+    s_m[warp] = dm;
+    s_s[warp] = ds;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double M = -INFINITY, S = 0.0;
+    for (int w = 0; w < NT / 32; w++) {
+      const double nm = M > s_m[w] ? M : s_m[w];
+      S = (nm == -INFINITY) ? 0.0 : S * exp(M - nm) + s_s[w] * exp(s_m[w] - nm);
+      M = nm;
+    }
+    s_lse = static_cast<float>(M + log(S));
+  }
+  __syncthreads();
+  const float lse = s_lse;
+  auto logp = [&](int id) -> float {
+    if (id < 0 || id >= V) return -INFINITY;
+    return __fsub_rn(value(id, load_scalar<T>(rowp, id)), lse);
+  };
+  if (A.token_logprob != nullptr && tid == 0) {
+    const int tok = A.tokens[row];
+    A.token_logprob[row] = tok >= 0 ? logp(tok) : __int_as_float(0x7FC00000);
+  }
+  if (A.cand_logprobs != nullptr) {
+    const int n = A.n_cand ? A.n_cand[row] : 0;
+    for (int j = tid; j < A.cand_stride; j += NT) {
+      const int id = (j < n && A.cand_ids) ? A.cand_ids[static_cast<size_t>(row) * A.cand_stride + j] : -1;
+      A.cand_logprobs[static_cast<size_t>(row) * A.cand_stride + j] = j < n ? logp(id) : -INFINITY;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// lm_head_kernel: the classifier of reference src/transformer/forward.c
+// :102-165 (parallel_matmul_bf16: fp32 activations x bf16 weight rows ->
+// fp32 logits), producing the sampler's logits buffer on the same stream.
+// logits[b][v] = sum_d x[b][d] * w[v][d], the bf16 weights widened exactly,
+// fp32 fused multiply-adds (its sum order is not the reference's: the LM
+// head is outside the sampler's parity contract).  HBM-bound on the weights
+// (V x dim x 2 bytes per launch): each warp takes one weight row at a time
+// with 16-byte loads and dots it with kLmRows activation rows staged in
+// shared memory.
+// ---------------------------------------------------------------------------
+constexpr int kLmRows = 8;   // activation rows per pass over the weights
+
+__global__ void __launch_bounds__(kSliceThreads) lm_head_kernel(const float *x, int B, int dim,
+                                                                const uint16_t *w, int V,
+                                                                float *logits, int64_t ld) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float *xs = reinterpret_cast<float *>(smem);  // [kLmRows][dim]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nvec = dim / 8;                     // dim % 8 == 0 (host-checked)
+  for (int b0 = 0; b0 < B; b0 += kLmRows) {
+    const int nb = min(kLmRows, B - b0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nb * dim; i += blockDim.x) xs[i] = x[static_cast<size_t>(b0) * dim + i];
+    __syncthreads();
+    for (int v = blockIdx.x * kSliceWarps + warp; v < V; v += gridDim.x * kSliceWarps) {
+      const uint4 *wr = reinterpret_cast<const uint4 *>(w + static_cast<size_t>(v) * dim);
+      float acc[kLmRows];
+#pragma unroll
+      for (int r = 0; r < kLmRows; r++) acc[r] = 0.0f;
+      for (int q = lane; q < nvec; q += 32) {
+        const uint4 u = __ldg(wr + q);
+        const uint32_t ww[4] = {u.x, u.y, u.z, u.w};
+        float wf[8];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          wf[2 * j] = __uint_as_float(ww[j] << 16);
+          wf[2 * j + 1] = __uint_as_float(ww[j] & 0xFFFF0000u);
+        }
+#pragma unroll
+        for (int r = 0; r < kLmRows; r++) {
+          if (r < nb) {
+            const float4 a0 = reinterpret_cast<const float4 *>(xs + r * dim)[2 * q];
+            const float4 a1 = reinterpret_cast<const float4 *>(xs + r * dim)[2 * q + 1];
+            float t = acc[r];
+            t = __fmaf_rn(a0.x, wf[0], t);
+            t = __fmaf_rn(a0.y, wf[1], t);
+            t = __fmaf_rn(a0.z, wf[2], t);
+            t = __fmaf_rn(a0.w, wf[3], t);
+            t = __fmaf_rn(a1.x, wf[4], t);
+            t = __fmaf_rn(a1.y, wf[5], t);
+            t = __fmaf_rn(a1.z, wf[6], t);
+            t = __fmaf_rn(a1.w, wf[7], t);
+            acc[r] = t;
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kLmRows; r++) {
+        float t = acc[r];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xFFFFFFFFu, t, o);
+        if (lane == 0 && r < nb) logits[static_cast<size_t>(b0 + r) * ld + v] = t;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // small kernels
 // ---------------------------------------------------------------------------
 __global__ void temperature_kernel(float *x, int n, float inv) {
@@ -2086,6 +2284,12 @@ cudaError_t set_kernel_attributes() {
   e = cudaFuncSetAttribute(full_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(logprob_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(logprob_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   return e;
 }
 
@@ -2120,6 +2324,23 @@ cudaError_t launch_temperature(float *x, int n, float T, cudaStream_t st) {
   if (T < 1e-6f) T = 1e-6f;                 // temperature.c:10
   const float inv = 1.0f / T;
   temperature_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, n, inv);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_logprob(const LogprobArgs &a, int dtype, cudaStream_t st) {
+  const size_t smem = logprob_smem_bytes(a.V, a.hcap);
+  if (dtype == PZ_DTYPE_F32)
+    logprob_kernel<float><<<a.B, kSliceThreads, smem, st>>>(a);
+  else
+    logprob_kernel<uint16_t><<<a.B, kSliceThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lm_head(const float *x, int B, int dim, const uint16_t *w, int V, float *logits,
+                           int64_t ld, int num_sms, cudaStream_t st) {
+  const size_t smem = sizeof(float) * kLmRows * static_cast<size_t>(dim);
+  const int grid = min(num_sms * 8, (V + kSliceWarps - 1) / kSliceWarps);
+  lm_head_kernel<<<grid, kSliceThreads, smem, st>>>(x, B, dim, w, V, logits, ld);
   return cudaGetLastError();
 }
 

@@ -109,7 +109,28 @@ struct MergeArgs {               // vocab-sharded merge after the allgather
   int cand_stride;
 };
 
+struct LogprobArgs {              // logprob_kernel
+  const void *logits;
+  int64_t ld;
+  int V;
+  int B;
+  const pz_sampler_config *cfg;
+  const int32_t *hist;
+  const int32_t *hist_off;
+  int hcap;                      // longest history applied (a power of two >= it)
+  const int32_t *tokens;
+  const int32_t *cand_ids;
+  const int32_t *n_cand;
+  int cand_stride;
+  float *token_logprob;
+  float *cand_logprobs;
+};
+
 // Launchers (pz_kernels.cu).  Return cudaGetLastError() after the launch.
+cudaError_t launch_logprob(const LogprobArgs &a, int dtype, cudaStream_t st);
+cudaError_t launch_lm_head(const float *x, int B, int dim, const uint16_t *w, int V, float *logits,
+                           int64_t ld, int num_sms, cudaStream_t st);
+size_t logprob_smem_bytes(int V, int hcap);
 cudaError_t launch_slice(const SliceArgs &a, int dtype, size_t smem,
                          cudaStream_t st);
 size_t slice_smem_bytes(int kcap, int hts, int nstages, int V, int elem_bytes);

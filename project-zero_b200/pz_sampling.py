@@ -65,7 +65,7 @@ class BatchHints(ctypes.Structure):
 class BatchOutputs(ctypes.Structure):
     _fields_ = [("cand_ids", _vp), ("cand_probs", _vp), ("n_cand", _vp),
                 ("row_status", _vp), ("cand_stride", ctypes.c_int32),
-                ("reserved", ctypes.c_int32)]
+                ("reserved", ctypes.c_int32), ("token_logprob", _vp), ("cand_logprobs", _vp)]
 
 
 class SamplerConfigC(ctypes.Structure):
@@ -165,6 +165,11 @@ _sig("pz_params_from_json", ctypes.c_int, [ctypes.POINTER(SamplingParams), ctype
 
 
 _sig("pz_history_append", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp])
+_sig("pz_lm_head_logits", ctypes.c_int,
+     [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int64, _vp])
+_sig("pz_sample_from_hidden", ctypes.c_int,
+     [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp,
+      ctypes.POINTER(BatchHints), ctypes.POINTER(BatchOutputs), _vp])
 _sig("pz_decode_step_create", ctypes.c_int,
      [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, _vp, _vp, ctypes.c_int, _vp, _vp,
       ctypes.POINTER(BatchHints), ctypes.POINTER(_vp)])
@@ -342,19 +347,22 @@ class Sampler:
         raise TypeError(f"logits dtype {logits.dtype} (want float32 or bfloat16)")
 
     @staticmethod
-    def _outputs(cand_ids=None, cand_probs=None, n_cand=None, row_status=None):
-        if cand_ids is None and cand_probs is None and n_cand is None and row_status is None:
+    def _outputs(cand_ids=None, cand_probs=None, n_cand=None, row_status=None, token_logprob=None,
+                 cand_logprobs=None):
+        if all(t is None for t in (cand_ids, cand_probs, n_cand, row_status, token_logprob, cand_logprobs)):
             return None
         stride = 0
-        if cand_ids is not None:
-            stride = cand_ids.shape[1]
-        elif cand_probs is not None:
-            stride = cand_probs.shape[1]
-        return BatchOutputs(_ptr(cand_ids), _ptr(cand_probs), _ptr(n_cand), _ptr(row_status), stride, 0)
+        for t in (cand_ids, cand_probs, cand_logprobs):
+            if t is not None:
+                stride = t.shape[1]
+                break
+        return BatchOutputs(_ptr(cand_ids), _ptr(cand_probs), _ptr(n_cand), _ptr(row_status), stride, 0,
+                            _ptr(token_logprob), _ptr(cand_logprobs))
 
     def sample(self, logits, cfg, rng_state, out, hist=None, hist_off=None, *,
                max_top_k=0, max_history=0, no_full_vocab=False, cand_ids=None,
-               cand_probs=None, n_cand=None, row_status=None, stream=None):
+               cand_probs=None, n_cand=None, row_status=None, token_logprob=None,
+               cand_logprobs=None, stream=None):
         """logits: [B, V] (row stride = logits.stride(0)) float32/bfloat16 CUDA
         tensor; cfg: device tensor holding B pz_sampler_config (32 bytes each);
         rng_state: [B] int64 device tensor (xorshift64* words, advanced in
@@ -362,13 +370,35 @@ class Sampler:
         tensors or None."""
         B, V = logits.shape
         hints = BatchHints(max_top_k, max_history, 1 if no_full_vocab else 0, 0)
-        outs = self._outputs(cand_ids, cand_probs, n_cand, row_status)
+        outs = self._outputs(cand_ids, cand_probs, n_cand, row_status, token_logprob, cand_logprobs)
         st = _lib.pz_sample_batch(
             self._h, _ptr(logits), self._dtype_code(logits), B, V, logits.stride(0),
             _ptr(cfg), _ptr(hist), _ptr(hist_off), _ptr(rng_state), _ptr(out),
             ctypes.byref(hints), ctypes.byref(outs) if outs is not None else None,
             _stream_handle(stream))
         _check(st, "pz_sample_batch")
+        return out
+
+    def lm_head(self, hidden, w_cls, logits, stream=None):
+        """pz_lm_head_logits: logits[B, V] = hidden[B, dim] (fp32) @ w_cls[V, dim]^T
+        (bf16), on the device."""
+        B, dim = hidden.shape
+        V = w_cls.shape[0]
+        _check(_lib.pz_lm_head_logits(self._h, _ptr(hidden), B, dim, _ptr(w_cls), V, _ptr(logits),
+                                      logits.stride(0), _stream_handle(stream)), "pz_lm_head_logits")
+        return logits
+
+    def sample_from_hidden(self, hidden, w_cls, logits, cfg, rng_state, out, hist=None, hist_off=None, *,
+                           max_top_k=0, max_history=0, no_full_vocab=False, stream=None):
+        """pz_sample_from_hidden: the classifier into `logits`, then the batch
+        sampler on it, both on the stream."""
+        B, dim = hidden.shape
+        V = w_cls.shape[0]
+        hints = BatchHints(max_top_k, max_history, 1 if no_full_vocab else 0, 0)
+        _check(_lib.pz_sample_from_hidden(self._h, _ptr(hidden), B, dim, _ptr(w_cls), V, _ptr(logits),
+                                          logits.stride(0), _ptr(cfg), _ptr(hist), _ptr(hist_off),
+                                          _ptr(rng_state), _ptr(out), ctypes.byref(hints), None,
+                                          _stream_handle(stream)), "pz_sample_from_hidden")
         return out
 
     def profile(self, n_calls):
