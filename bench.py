@@ -592,10 +592,11 @@ def leg_config2(C, peak):
             "inputs": "156 MB/GPU > L2", "scaling": "weak"}
 
 
-def leg_config4(C, peak):
-    """Heterogeneous bf16 batch B=8192 x V=151936, row-sharded over the ranks."""
+def leg_config4(C, peak, rows=8192):
+    """Heterogeneous bf16 batch B=8192 x V=151936, row-sharded over the ranks
+    (rows < 8192 only for profiling)."""
     torch, pz = C.torch, C.pz
-    Bg, V = 8192, 151936
+    Bg, V = rows, 151936
     b0, B = pz.row_shard(Bg, C.world, C.rank)
     cfg_np, H = config4_configs(Bg)
     cfg_np, H = cfg_np[b0:b0 + B], H[b0:b0 + B]
@@ -775,6 +776,19 @@ def run_ours(args):
     C = Ctx()
     torch = C.torch
     peak, peak_kind = hbm_peak()
+    if args.only_leg:
+        # one leg alone (profiling): its JSON object, no headline line
+        fn = {"config2_greedy": lambda: leg_config2(C, peak),
+              "config4_hetero": lambda: leg_config4(C, peak, args.c4_rows),
+              "config5_vocab": lambda: leg_config5(C, peak),
+              "config1_sequential": lambda: leg_config1(C)}[args.only_leg]
+        r = fn()
+        if C.rank == 0:
+            print(json.dumps({"leg": args.only_leg, **r}), flush=True)
+        if C.dist:
+            C.barrier()
+            C.dist.destroy_process_group()
+        return 0
     res, keep = headline(C, args, peak, peak_kind)
     B = args.rows
     legs = {}
@@ -838,6 +852,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline legs")
     ap.add_argument("--no-legs", action="store_true", help="headline config 3 only")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--only-leg", default="", choices=["", "config2_greedy", "config4_hetero",
+                                                        "config5_vocab", "config1_sequential"],
+                    help="run one leg alone (profiling)")
+    ap.add_argument("--c4-rows", type=int, default=8192, help="config-4 rows (profiling a smaller case)")
     ap.add_argument("--rows", type=int, default=W3["B"],
                     help="rows per GPU (profiling a smaller case; the bench line is quoted at 1024)")
     args = ap.parse_args()

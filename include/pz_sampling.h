@@ -283,8 +283,11 @@ pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms,
                               double *rest_ms, int *calls, int *kernels);
 /* The same timing split by phase: phase_ms[0] slice_kernel, [1] the
  * full-vocabulary pass (full_kernel), [2] the vocab-sharded allgather,
- * [3] merge_kernel; summed over the timed calls.  Starts a new count. */
-pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double phase_ms[4],
+ * [3] merge_kernel, and [4] the streaming launch alone (part of [0]: in a
+ * call that decides its list rows in a second slice_kernel launch, the
+ * first launch; otherwise all of [0]); summed over the timed calls.
+ * Starts a new count. */
+pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double phase_ms[5],
                                 int *calls, int *kernels);
 
 /* Seeds B RNG states on the device: state[r] = seed_base + r (0 -> 1, as
@@ -393,6 +396,55 @@ pz_status pz_sample_batch_vocab_sharded(
     const pz_sampler_config *cfg, const int32_t *hist,
     const int32_t *hist_off, unsigned long long *rng_state,
     int32_t *out_tokens, const pz_batch_outputs *outputs, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Several GPUs driven by one host thread.  The reference samples one row on
+ * the CPU of a single process (src/transformer/generate.c:143-170); a server
+ * that owns all of a node's GPUs in one process shards the batch over them
+ * with these two calls instead of one process per GPU. */
+
+/* One device's part of a multi-device call: a context on that device, the
+ * stream to queue on (a stream of that device) and DEVICE pointers on it. */
+typedef struct pz_shard {
+  pz_sampler_ctx *ctx;
+  const void *logits;      /* rows (row mode) or column slice (vocab mode)    */
+  int64_t ld;              /* elements between rows                           */
+  int32_t B;               /* rows held here (vocab mode: the same on all)    */
+  int32_t V;               /* columns held here                               */
+  int64_t v_offset;        /* vocab mode: global id of column 0; row mode: 0  */
+  const pz_sampler_config *cfg;
+  const int32_t *hist;     /* CSR history in GLOBAL ids, or NULL              */
+  const int32_t *hist_off;
+  unsigned long long *rng_state;
+  int32_t *out_tokens;
+  const pz_batch_outputs *outputs;  /* may be NULL                           */
+  void *stream;
+} pz_shard;
+
+#define PZ_SHARD_ROWS 0
+#define PZ_SHARD_VOCAB 1
+
+/* Joins n contexts, on n distinct devices of this process, to one
+ * communicator: ctxs[i] becomes rank i of n.  Non-blocking and bound by
+ * timeout_ms, as pz_ctx_init_nccl_timeout. */
+pz_status pz_multi_init_nccl(pz_sampler_ctx *const *ctxs, int n, int timeout_ms);
+
+/* Samples a batch spread over n devices, from one host thread.
+ *   PZ_SHARD_ROWS: shard i holds its own rows (pz_row_shard gives the even
+ *     split); each is sampled exactly as pz_sample_batch(shard.ctx, ...)
+ *     with `hints`; no communication.  Every shard has V == V_global and
+ *     v_offset == 0.
+ *   PZ_SHARD_VOCAB: every shard holds the same B rows, columns
+ *     [v_offset, v_offset + V) of V_global, and its context was joined as
+ *     rank i by pz_multi_init_nccl.  The local passes, ONE grouped
+ *     allgather of the candidate lists and the merges run as in
+ *     pz_sample_batch_vocab_sharded (same requirements; `hints` unused):
+ *     every shard's out_tokens and rng_state receive the same values.
+ * Asynchronous: returns once every device's work is queued on its stream
+ * (pz_ctx_wait on each shard's context and stream waits for it). */
+pz_status pz_sample_batch_multi(int mode, int n, const pz_shard *shards,
+                                pz_dtype dtype, int V_global,
+                                const pz_batch_hints *hints);
 
 /* ------------------------------------------------------------------------ */
 /* Settings from the front ends of the generate loop.                       */

@@ -99,6 +99,8 @@ struct NcclApi {
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
 };
 std::mutex g_nccl_mu;
 NcclApi g_nccl;
@@ -122,6 +124,8 @@ bool load_nccl() {
   PZ_SYM(CommDestroy, "ncclCommDestroy")
   PZ_SYM(CommAbort, "ncclCommAbort")
   PZ_SYM(CommGetAsyncError, "ncclCommGetAsyncError")
+  PZ_SYM(GroupStart, "ncclGroupStart")
+  PZ_SYM(GroupEnd, "ncclGroupEnd")
 #undef PZ_SYM
   g_nccl.loaded = true;
   return true;
@@ -149,6 +153,8 @@ struct pz_sampler_ctx {
   uint32_t *sort_a = nullptr;
   uint32_t *sort_b = nullptr;
   float *full_e = nullptr;
+  uint16_t *sk_store = nullptr;  // two-phase launches: list rows' sketches
+  uint32_t *sk_max = nullptr;
   int64_t sort_stride = 0;
   int64_t e_stride = 0;
   int full_grid = 0;
@@ -286,6 +292,9 @@ pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
             c->alloc(&c->sort_a, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
             c->alloc(&c->sort_b, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
             c->alloc(&c->full_e, static_cast<size_t>(c->full_grid) * c->e_stride);
+  if (ok && L.max_top_k >= 2)
+    ok = c->alloc(&c->sk_store, static_cast<size_t>(B) * pz::slice_sketch_stride(L.max_vocab, 4)) &&
+         c->alloc(&c->sk_max, B);
   if (!ok) {
     c->release();
     delete c;
@@ -390,9 +399,10 @@ static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
 }
 
 // Events per profiled call: start, after slice_kernel, after full_kernel,
-// after the allgather, end (after merge_kernel).  Phases a call does not
+// after the allgather, end (after merge_kernel), and (index 5) between the
+// two slice_kernel launches of a two-phase call.  Phases a call does not
 // have are recorded back to back and time as zero.
-constexpr int kProfEvents = 5;
+constexpr int kProfEvents = 6;
 
 // The next profiling slot of the context (nullptr when timing is off or
 // its slots are used up).
@@ -503,15 +513,42 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     a.stagger_ctas = slots;
     a.stagger_occ = occ;
   }
+  // Two launches when every row has its own CTA and the rows may keep
+  // lists: the first streams every row and decides all but the list rows,
+  // whose sketches it stores; the second decides the list rows from their
+  // sketches.  A list row's end-of-row work (its bound, the re-read of its
+  // candidate groups, the ranking and the draw) then no longer holds a CTA
+  // slot that the stream of another row could use.
+  static const int two_phase_env = [] {
+    const char *e = std::getenv("PZ_TWO_PHASE");  // tuning override (0: one launch)
+    return e ? std::atoi(e) : -1;
+  }();
+  const bool two_phase = two_phase_env > 0 && a.S == 1 && a.kmax >= 2 && ctx->sk_store != nullptr;
+  if (two_phase) {
+    a.sk_store = ctx->sk_store;
+    a.sk_max = ctx->sk_max;
+    a.sk_stride = pz::slice_sketch_stride(V, dtype == PZ_DTYPE_BF16 ? 2 : 4);
+    a.stagger_ns = 0;  // no CTA of the streaming launch holds its slot for a list's end-of-row work
+  }
   const bool full_pass = !emit && !no_full;
   if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t), st) != cudaSuccess)
     return fail(PZ_ERR_CUDA);
   cudaEvent_t *ev = next_prof_slot(ctx, st);
   if (ev) cudaEventRecord(ev[0], st);
+  a.phase = two_phase ? 1 : 0;
   cudaError_t ce = pz::launch_slice(a, dtype, smem, st);
   if (ce != cudaSuccess) return fail_cuda(ce);
-  if (ev) cudaEventRecord(ev[1], st);
   int kernels = 1;  // slice_kernel decides every row itself
+  if (two_phase) {
+    if (ev) cudaEventRecord(ev[5], st);
+    a.phase = 2;
+    ce = pz::launch_slice(a, dtype, smem, st);
+    if (ce != cudaSuccess) return fail_cuda(ce);
+    kernels = 2;
+  } else if (ev) {
+    cudaEventRecord(ev[5], st);
+  }
+  if (ev) cudaEventRecord(ev[1], st);
   if (full_pass) {
     FullArgs f{};
     f.logits = logits;
@@ -726,20 +763,22 @@ pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double *phase_ms, int *call
   if (!ctx) return fail(PZ_ERR_INVALID_ARGS);
   DeviceGuard g(ctx->device);
   if (!g.ok) return fail(PZ_ERR_CUDA);
-  double sum[kProfEvents - 1] = {0.0, 0.0, 0.0, 0.0};
+  // phases 0..3 between consecutive events 0..4; phase 4 from event 0 to 5
+  constexpr int kPhases = 5;
+  double sum[kPhases] = {0.0, 0.0, 0.0, 0.0, 0.0};
   for (int i = 0; i < ctx->prof_used; i++) {
     cudaEvent_t *ev = &ctx->prof[i * kProfEvents];
-    cudaError_t ce = cudaEventSynchronize(ev[kProfEvents - 1]);
+    cudaError_t ce = cudaEventSynchronize(ev[4]);
     if (ce != cudaSuccess) return fail_cuda(ce);
-    for (int j = 0; j + 1 < kProfEvents; j++) {
+    for (int j = 0; j < kPhases; j++) {
       float t = 0.0f;
-      ce = cudaEventElapsedTime(&t, ev[j], ev[j + 1]);
+      ce = j < 4 ? cudaEventElapsedTime(&t, ev[j], ev[j + 1]) : cudaEventElapsedTime(&t, ev[0], ev[5]);
       if (ce != cudaSuccess) return fail_cuda(ce);
       sum[j] += t;
     }
   }
   if (phase_ms)
-    for (int j = 0; j + 1 < kProfEvents; j++) phase_ms[j] = sum[j];
+    for (int j = 0; j < kPhases; j++) phase_ms[j] = sum[j];
   if (calls) *calls = ctx->prof_used;
   if (kernels) *kernels = ctx->prof_kernels;
   ctx->prof_used = 0;
@@ -749,7 +788,7 @@ pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double *phase_ms, int *call
 
 pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms, double *rest_ms,
                               int *calls, int *kernels) {
-  double ph[kProfEvents - 1];
+  double ph[5];
   const pz_status s = pz_ctx_profile_phases(ctx, ph, calls, kernels);
   if (s != PZ_OK) return s;
   if (slice_ms) *slice_ms = ph[0];
@@ -1001,46 +1040,59 @@ pz_status pz_ctx_abort_nccl(pz_sampler_ctx *ctx) {
   return PZ_OK;
 }
 
-pz_status pz_sample_batch_vocab_sharded(
-    pz_sampler_ctx *ctx, const void *logits_slice, pz_dtype dtype, int B,
-    int V_local, int64_t ld, int64_t v_offset, int V_global,
-    const pz_sampler_config *cfg, const int32_t *hist, const int32_t *hist_off,
-    unsigned long long *rng_state, int32_t *out_tokens,
-    const pz_batch_outputs *outputs, void *stream) {
+}  // extern "C"
+
+namespace {
+
+// The three steps of a vocab-sharded call.  (1) The local pass: this
+// slice's lists, written to ctx->emit as [B][kcap+1] (counts in slot kcap).
+pz_status vocab_check(const pz_sampler_ctx *ctx, int V_local, int64_t v_offset, int V_global,
+                      unsigned long long *rng_state, int32_t *out_tokens,
+                      const pz_batch_outputs *outputs) {
   if (!ctx || !rng_state || !out_tokens) return fail(PZ_ERR_INVALID_ARGS);
   if (!ctx->comm) return fail(ctx->comm_failed ? PZ_ERR_NCCL : PZ_ERR_INVALID_ARGS);
   if (outputs && (outputs->token_logprob || outputs->cand_logprobs)) return fail(PZ_ERR_UNSUPPORTED);
   if (outputs && (outputs->cand_ids || outputs->cand_probs) &&
       outputs->cand_stride < std::max(ctx->lim.max_top_k, 1))
     return fail(PZ_ERR_INVALID_ARGS);
-  if (V_global < V_local || v_offset < 0 || v_offset + V_local > V_global)
+  if (V_local <= 0 || V_global < V_local || v_offset < 0 || v_offset + V_local > V_global)
     return fail(PZ_ERR_INVALID_ARGS);
+  return PZ_OK;
+}
+
+pz_status vocab_local(pz_sampler_ctx *ctx, const void *logits_slice, pz_dtype dtype, int B, int V_local,
+                      int64_t ld, int64_t v_offset, int V_global, const pz_sampler_config *cfg,
+                      const int32_t *hist, const int32_t *hist_off, void *stream, cudaEvent_t **ev) {
   pz_batch_hints h{};
   h.no_full_vocab = 1;
-  cudaEvent_t *ev = nullptr;
-  pz_status s = sample_impl(ctx, logits_slice, dtype, B, V_local, ld, v_offset,
-                            V_global, cfg, hist, hist_off, nullptr, nullptr, &h,
-                            nullptr, stream, true, &ev);
-  if (s != PZ_OK) return s;
+  return sample_impl(ctx, logits_slice, dtype, B, V_local, ld, v_offset, V_global, cfg, hist, hist_off,
+                     nullptr, nullptr, &h, nullptr, stream, true, ev);
+}
+
+size_t vocab_block_words(const pz_sampler_ctx *ctx, int B) {
+  return static_cast<size_t>(B) * (next_pow2(std::max(ctx->lim.max_top_k, 1)) + 1);
+}
+
+// (2) ONE allgather of every rank's list block (enqueued; in a group when
+// one thread drives several communicators).
+ncclResult_t vocab_allgather(pz_sampler_ctx *ctx, int B, void *stream) {
+  return g_nccl.AllGather(ctx->emit, ctx->gathered, vocab_block_words(ctx, B), ncclUint64, ctx->comm,
+                          static_cast<cudaStream_t>(stream));
+}
+
+// (3) The merge of the G blocks and the draw.
+pz_status vocab_merge(pz_sampler_ctx *ctx, int B, int V_global, const pz_sampler_config *cfg,
+                      unsigned long long *rng_state, int32_t *out_tokens, const pz_batch_outputs *outputs,
+                      void *stream, cudaEvent_t *ev) {
   DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(PZ_ERR_CUDA);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int kcap = next_pow2(std::max(ctx->lim.max_top_k, 1));
-  const size_t per_rank = static_cast<size_t>(B) * (kcap + 1);
-  // ONE allgather: every rank's [B][kcap+1] list block, counts included.
-  const double t0 = now_ms();
-  const ncclResult_t r = g_nccl.AllGather(ctx->emit, ctx->gathered, per_rank, ncclUint64, ctx->comm, st);
-  if (r != ncclSuccess && r != ncclInProgress) {
-    abort_comm(ctx);
-    return fail(PZ_ERR_NCCL);
-  }
-  s = nccl_settle(ctx, r, t0);  // the call is enqueued (not finished) when this returns
-  if (s != PZ_OK) return s;
   if (ev) cudaEventRecord(ev[3], st);
   MergeArgs m{};
   m.gathered = ctx->gathered;
   m.G = ctx->world;
   m.B = B;
-  m.kcap = kcap;
+  m.kcap = next_pow2(std::max(ctx->lim.max_top_k, 1));
   m.kmax = std::max(ctx->lim.max_top_k, 1);
   m.V_global = V_global;
   m.cfg = cfg;
@@ -1058,6 +1110,158 @@ pz_status pz_sample_batch_vocab_sharded(
   if (ev) {
     cudaEventRecord(ev[4], st);
     ctx->prof_kernels += 1;
+  }
+  return PZ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+pz_status pz_sample_batch_vocab_sharded(
+    pz_sampler_ctx *ctx, const void *logits_slice, pz_dtype dtype, int B,
+    int V_local, int64_t ld, int64_t v_offset, int V_global,
+    const pz_sampler_config *cfg, const int32_t *hist, const int32_t *hist_off,
+    unsigned long long *rng_state, int32_t *out_tokens,
+    const pz_batch_outputs *outputs, void *stream) {
+  pz_status s = vocab_check(ctx, V_local, v_offset, V_global, rng_state, out_tokens, outputs);
+  if (s != PZ_OK) return s;
+  cudaEvent_t *ev = nullptr;
+  s = vocab_local(ctx, logits_slice, dtype, B, V_local, ld, v_offset, V_global, cfg, hist, hist_off, stream, &ev);
+  if (s != PZ_OK) return s;
+  {
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(PZ_ERR_CUDA);
+    const double t0 = now_ms();
+    const ncclResult_t r = vocab_allgather(ctx, B, stream);
+    if (r != ncclSuccess && r != ncclInProgress) {
+      abort_comm(ctx);
+      return fail(PZ_ERR_NCCL);
+    }
+    s = nccl_settle(ctx, r, t0);  // the call is enqueued (not finished) when this returns
+    if (s != PZ_OK) return s;
+  }
+  return vocab_merge(ctx, B, V_global, cfg, rng_state, out_tokens, outputs, stream, ev);
+}
+
+// ---------------------------------------------------------------------------
+// Several devices from one host thread
+// ---------------------------------------------------------------------------
+pz_status pz_multi_init_nccl(pz_sampler_ctx *const *ctxs, int n, int timeout_ms) {
+  if (!ctxs || n < 1 || n > kMaxDevices || timeout_ms <= 0) return fail(PZ_ERR_INVALID_ARGS);
+  for (int i = 0; i < n; i++) {
+    if (!ctxs[i] || ctxs[i]->comm) return fail(PZ_ERR_INVALID_ARGS);
+    for (int j = 0; j < i; j++)
+      if (ctxs[j]->device == ctxs[i]->device) return fail(PZ_ERR_INVALID_ARGS);
+  }
+  if (!load_nccl()) return fail(PZ_ERR_NCCL);
+  ncclUniqueId id;
+  if (g_nccl.GetUniqueId(&id) != ncclSuccess) return fail(PZ_ERR_NCCL);
+  for (int i = 0; i < n; i++) {
+    pz_sampler_ctx *c = ctxs[i];
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(PZ_ERR_CUDA);
+    const size_t per_rank = static_cast<size_t>(c->lim.max_batch) * (c->kcap_max + 1);
+    if (!c->emit && !c->alloc(&c->emit, per_rank)) return fail(PZ_ERR_OOM);
+    if (!c->gathered && !c->alloc(&c->gathered, per_rank * n)) return fail(PZ_ERR_OOM);
+    c->nccl_timeout_ms = timeout_ms;
+    c->comm_failed = false;
+  }
+  // one thread creates every rank's communicator: a group, so that the
+  // ranks' set-ups do not wait for one another
+  const double t0 = now_ms();
+  std::vector<ncclComm_t> comms(n, nullptr);
+  ncclResult_t r = g_nccl.GroupStart();
+  for (int i = 0; i < n && r == ncclSuccess; i++) {
+    DeviceGuard g(ctxs[i]->device);
+    ncclConfig_t conf = NCCL_CONFIG_INITIALIZER;
+    conf.blocking = 0;
+    const ncclResult_t ri = g_nccl.CommInitRankConfig(&comms[i], n, id, i, &conf);
+    if (ri != ncclSuccess && ri != ncclInProgress) r = ri;
+  }
+  const ncclResult_t re = g_nccl.GroupEnd();
+  if (r == ncclSuccess && re != ncclSuccess && re != ncclInProgress) r = re;
+  if (r != ncclSuccess) {
+    for (int i = 0; i < n; i++)
+      if (comms[i]) g_nccl.CommAbort(comms[i]);
+    return fail(PZ_ERR_NCCL);
+  }
+  pz_status s = PZ_OK;
+  for (int i = 0; i < n; i++) {
+    ctxs[i]->comm = comms[i];
+    ctxs[i]->world = n;
+    ctxs[i]->rank = i;
+  }
+  for (int i = 0; i < n && s == PZ_OK; i++) {
+    DeviceGuard g(ctxs[i]->device);
+    s = nccl_settle(ctxs[i], ncclInProgress, t0);
+  }
+  if (s != PZ_OK)
+    for (int i = 0; i < n; i++)
+      if (ctxs[i]->comm) abort_comm(ctxs[i]);
+  return s;
+}
+
+pz_status pz_sample_batch_multi(int mode, int n, const pz_shard *shards, pz_dtype dtype, int V_global,
+                                const pz_batch_hints *hints) {
+  if (!shards || n < 1 || (mode != PZ_SHARD_ROWS && mode != PZ_SHARD_VOCAB)) return fail(PZ_ERR_INVALID_ARGS);
+  for (int i = 0; i < n; i++)
+    if (!shards[i].ctx) return fail(PZ_ERR_INVALID_ARGS);
+  if (mode == PZ_SHARD_ROWS) {
+    // independent shards: each queued as one pz_sample_batch on its device
+    for (int i = 0; i < n; i++) {
+      const pz_shard &h = shards[i];
+      if (h.v_offset != 0 || h.V != V_global) return fail(PZ_ERR_INVALID_ARGS);
+    }
+    for (int i = 0; i < n; i++) {
+      const pz_shard &h = shards[i];
+      const pz_status s = sample_impl(h.ctx, h.logits, dtype, h.B, h.V, h.ld, 0, h.V, h.cfg, h.hist,
+                                      h.hist_off, h.rng_state, h.out_tokens, hints, h.outputs, h.stream, false);
+      if (s != PZ_OK) return s;
+    }
+    return PZ_OK;
+  }
+  // vocab sharding: every shard holds the same rows; shard i is rank i
+  for (int i = 0; i < n; i++) {
+    const pz_shard &h = shards[i];
+    const pz_status s = vocab_check(h.ctx, h.V, h.v_offset, V_global, h.rng_state, h.out_tokens, h.outputs);
+    if (s != PZ_OK) return s;
+    if (h.ctx->world != n || h.ctx->rank != i || h.B != shards[0].B) return fail(PZ_ERR_INVALID_ARGS);
+  }
+  std::vector<cudaEvent_t *> ev(n, nullptr);
+  for (int i = 0; i < n; i++) {
+    const pz_shard &h = shards[i];
+    const pz_status s = vocab_local(h.ctx, h.logits, dtype, h.B, h.V, h.ld, h.v_offset, V_global, h.cfg,
+                                    h.hist, h.hist_off, h.stream, &ev[i]);
+    if (s != PZ_OK) return s;
+  }
+  const double t0 = now_ms();
+  ncclResult_t r = g_nccl.GroupStart();
+  for (int i = 0; i < n && r == ncclSuccess; i++) {
+    DeviceGuard g(shards[i].ctx->device);
+    const ncclResult_t ri = vocab_allgather(shards[i].ctx, shards[i].B, shards[i].stream);
+    if (ri != ncclSuccess && ri != ncclInProgress) r = ri;
+  }
+  const ncclResult_t re = g_nccl.GroupEnd();
+  if (r == ncclSuccess && re != ncclSuccess && re != ncclInProgress) r = re;
+  if (r != ncclSuccess) {
+    for (int i = 0; i < n; i++) abort_comm(shards[i].ctx);
+    return fail(PZ_ERR_NCCL);
+  }
+  for (int i = 0; i < n; i++) {
+    DeviceGuard g(shards[i].ctx->device);
+    const pz_status s = nccl_settle(shards[i].ctx, ncclInProgress, t0);
+    if (s != PZ_OK) {
+      for (int j = 0; j < n; j++)
+        if (shards[j].ctx->comm) abort_comm(shards[j].ctx);
+      return s;
+    }
+  }
+  for (int i = 0; i < n; i++) {
+    const pz_shard &h = shards[i];
+    const pz_status s = vocab_merge(h.ctx, h.B, V_global, h.cfg, h.rng_state, h.out_tokens, h.outputs, h.stream,
+                                    ev[i]);
+    if (s != PZ_OK) return s;
   }
   return PZ_OK;
 }

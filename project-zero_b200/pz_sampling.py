@@ -68,6 +68,18 @@ class BatchOutputs(ctypes.Structure):
                 ("reserved", ctypes.c_int32), ("token_logprob", _vp), ("cand_logprobs", _vp)]
 
 
+class Shard(ctypes.Structure):
+    """pz_shard: one device's part of a pz_sample_batch_multi call."""
+    _fields_ = [("ctx", ctypes.c_void_p), ("logits", ctypes.c_void_p), ("ld", ctypes.c_int64),
+                ("B", ctypes.c_int32), ("V", ctypes.c_int32), ("v_offset", ctypes.c_int64),
+                ("cfg", ctypes.c_void_p), ("hist", ctypes.c_void_p), ("hist_off", ctypes.c_void_p),
+                ("rng_state", ctypes.c_void_p), ("out_tokens", ctypes.c_void_p),
+                ("outputs", ctypes.c_void_p), ("stream", ctypes.c_void_p)]
+
+
+SHARD_ROWS, SHARD_VOCAB = 0, 1
+
+
 class SamplerConfigC(ctypes.Structure):
     """pz_sampler_config as a ctypes structure (32 bytes)."""
     _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_int32), ("top_p", ctypes.c_float),
@@ -155,6 +167,11 @@ _sig("pz_ctx_init_nccl", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, ct
 _sig("pz_sample_batch_vocab_sharded", ctypes.c_int,
      [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
       ctypes.c_int, _vp, _vp, _vp, _vp, _vp, ctypes.POINTER(BatchOutputs), _vp])
+
+
+_sig("pz_multi_init_nccl", ctypes.c_int, [ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int])
+_sig("pz_sample_batch_multi", ctypes.c_int,
+     [ctypes.c_int, ctypes.c_int, ctypes.POINTER(Shard), ctypes.c_int, ctypes.c_int, ctypes.POINTER(BatchHints)])
 
 
 _sig("pz_params_init_cli", None, [ctypes.POINTER(SamplingParams)])
@@ -415,13 +432,14 @@ class Sampler:
         return a.value, b.value, n.value, k.value
 
     def profile_phases(self):
-        """({'slice', 'full', 'allgather', 'merge'} ms summed over the timed
-        calls, calls, kernels launched) since the last read."""
-        ph = (ctypes.c_double * 4)()
+        """({'slice', 'full', 'allgather', 'merge', 'stream'} ms summed over
+        the timed calls, calls, kernels launched) since the last read;
+        'stream' is the streaming launch alone (part of 'slice')."""
+        ph = (ctypes.c_double * 5)()
         n, k = ctypes.c_int(), ctypes.c_int()
         _check(_lib.pz_ctx_profile_phases(self._h, ph, ctypes.byref(n), ctypes.byref(k)),
                "pz_ctx_profile_phases")
-        return dict(zip(("slice", "full", "allgather", "merge"), list(ph))), n.value, k.value
+        return dict(zip(("slice", "full", "allgather", "merge", "stream"), list(ph))), n.value, k.value
 
     def wait(self, timeout_ms, stream=None):
         """Bounded wait for the stream's work (NCCL errors and the deadline
@@ -456,6 +474,48 @@ class Sampler:
             _stream_handle(stream))
         _check(st, "pz_sample_batch_vocab_sharded")
         return out
+
+
+def multi_init_nccl(samplers, timeout_ms=60000):
+    """pz_multi_init_nccl: joins the samplers (one per device of this
+    process) to one communicator, samplers[i] as rank i."""
+    arr = (_vp * len(samplers))(*[s._h for s in samplers])
+    _check(_lib.pz_multi_init_nccl(arr, len(samplers), int(timeout_ms)), "pz_multi_init_nccl")
+    for i, s in enumerate(samplers):
+        s.world, s.rank = len(samplers), i
+
+
+def sample_multi(mode, parts, V_global, *, max_top_k=0, max_history=0, no_full_vocab=False):
+    """pz_sample_batch_multi from one thread.  parts: one dict per device with
+    keys sampler, logits, cfg, rng_state, out and optionally hist, hist_off,
+    v_offset (vocab mode), stream, and the candidate outputs (cand_ids,
+    cand_probs, n_cand, row_status)."""
+    n = len(parts)
+    arr = (Shard * n)()
+    keep = []
+    dtype = None
+    for i, d in enumerate(parts):
+        x = d["logits"]
+        dt = Sampler._dtype_code(x)
+        if dtype is not None and dt != dtype:
+            raise TypeError("every shard needs the same logits dtype")
+        dtype = dt
+        outs = Sampler._outputs(d.get("cand_ids"), d.get("cand_probs"), d.get("n_cand"), d.get("row_status"))
+        if outs is not None:
+            keep.append(outs)
+        arr[i] = Shard(d["sampler"]._h.value, _ptr(x), x.stride(0), x.shape[0], x.shape[1],
+                       int(d.get("v_offset", 0)), _ptr(d["cfg"]), _ptr(d.get("hist")), _ptr(d.get("hist_off")),
+                       _ptr(d["rng_state"]), _ptr(d["out"]),
+                       ctypes.addressof(outs) if outs is not None else None,
+                       _stream_handle(d.get("stream")) if d.get("stream") is not None else _current_stream(x))
+    hints = BatchHints(max_top_k, max_history, 1 if no_full_vocab else 0, 0)
+    _check(_lib.pz_sample_batch_multi(mode, n, arr, dtype, int(V_global), ctypes.byref(hints)),
+           "pz_sample_batch_multi")
+
+
+def _current_stream(t):
+    import torch
+    return torch.cuda.current_stream(t.device).cuda_stream
 
 
 class DecodeStep:

@@ -159,3 +159,97 @@ def test_nccl_init_times_out_when_a_rank_never_joins():
     p.join(timeout=60)
     assert status == pz.PZ_ERR_TIMEOUT, (status, took)
     assert 2.5 < took < 30.0
+
+
+# ---- pz_sample_batch_multi: several devices from one host thread ----------
+MULTI_SPEC = dict(seed=63, B=96, V=128256, sd=2.5, boosts=[8, 5.0, 15.0], hist_len=512,
+                  cfg=dict(temperature=0.7, top_k=50, top_p=0.9, rep=1.1, freq=0.2, pres=0.1))
+
+
+def _multi_devices(n):
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+    return list(range(n))
+
+
+def _to(d, dev, rows=slice(None)):
+    x = np.ascontiguousarray(d["logits"][rows])
+    if x.dtype == np.uint16:  # bf16 bits
+        x = torch.from_numpy(x.view(np.int16).copy()).to(f"cuda:{dev}").view(torch.bfloat16)
+    else:
+        x = torch.from_numpy(x).to(f"cuda:{dev}")
+    cfg = torch.from_numpy(np.ascontiguousarray(d["cfg"][rows]).view(np.uint8).copy()).to(f"cuda:{dev}")
+    rng = torch.from_numpy(np.ascontiguousarray(d["rng"][rows]).view(np.int64).copy()).to(f"cuda:{dev}")
+    return x, cfg, rng
+
+
+def _csr_rows(d, b, c):
+    """The history CSR of rows [b, b + c), offsets rebased to 0."""
+    off = d["hist_off"]
+    h = d["hist"][off[b]:off[b + c]]
+    o = (off[b:b + c + 1] - off[b]).astype(np.int32)
+    return h, o
+
+
+@pytest.mark.parametrize("n", [1, 2])
+def test_multi_row_sharded(n, oracle_lib):
+    """PZ_SHARD_ROWS: each device samples its pz_row_shard rows; together they
+    give the oracle's tokens and RNG states for the whole batch."""
+    import pz_sampling as pz
+    devs = _multi_devices(n)
+    d = cases.build(MULTI_SPEC)
+    B, V = MULTI_SPEC["B"], MULTI_SPEC["V"]
+    parts, samplers, outs = [], [], []
+    for i, dev in enumerate(devs):
+        b, c = pz.row_shard(B, n, i)
+        x, cfg, rng = _to(d, dev, slice(b, b + c))
+        h, o = _csr_rows(d, b, c)
+        s = pz.Sampler(dev, max_batch=c, max_vocab=V, max_top_k=64, max_history=1024)
+        out = torch.full((c,), -7, dtype=torch.int32, device=f"cuda:{dev}")
+        samplers.append(s)
+        outs.append((b, c, out, rng))
+        parts.append(dict(sampler=s, logits=x, cfg=cfg, rng_state=rng, out=out,
+                          hist=torch.from_numpy(h).to(f"cuda:{dev}"), hist_off=torch.from_numpy(o).to(f"cuda:{dev}")))
+    pz.sample_multi(pz.SHARD_ROWS, parts, V, max_top_k=64, max_history=1024, no_full_vocab=True)
+    for dev in devs:
+        torch.cuda.synchronize(dev)
+    tok = np.zeros(B, dtype=np.int64)
+    rng_all = np.zeros(B, dtype=np.uint64)
+    for b, c, out, rng in outs:
+        tok[b:b + c] = out.cpu().numpy()
+        rng_all[b:b + c] = rng.cpu().numpy().view(np.uint64)
+    for s in samplers:
+        s.close()
+    t_o, r_o, *_ = oracle_lib.sample_batch(d["logits"], d["cfg"], d["rng"], d["hist"], d["hist_off"])
+    assert np.array_equal(tok, t_o)
+    assert np.array_equal(rng_all, np.asarray(r_o, dtype=np.uint64))
+
+
+@pytest.mark.parametrize("n", [1, 2])
+def test_multi_vocab_sharded(n, oracle_lib):
+    """PZ_SHARD_VOCAB from one thread: pz_multi_init_nccl joins the contexts,
+    each device holds a column slice of every row, one grouped allgather
+    exchanges the lists, and every device returns the oracle's tokens."""
+    import pz_sampling as pz
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    devs = _multi_devices(n)
+    d = cases.build(SPEC)
+    B, V = SPEC["B"], SPEC["V"]
+    samplers, parts = [], []
+    for i, dev in enumerate(devs):
+        b, c = pz.row_shard(V, n, i)
+        x, cfg, rng = _to(d, dev)
+        s = pz.Sampler(dev, max_batch=B, max_vocab=c, max_top_k=64, max_history=0)
+        samplers.append(s)
+        parts.append(dict(sampler=s, logits=x[:, b:b + c], v_offset=b, cfg=cfg, rng_state=rng,
+                          out=torch.full((B,), -7, dtype=torch.int32, device=f"cuda:{dev}")))
+    pz.multi_init_nccl(samplers, timeout_ms=60000)
+    pz.sample_multi(pz.SHARD_VOCAB, parts, V)
+    for s, p in zip(samplers, parts):
+        s.wait(60000, stream=torch.cuda.current_stream(p["out"].device))
+    t_o, r_o, *_ = oracle_lib.sample_batch(d["logits"], d["cfg"], d["rng"])
+    for p in parts:
+        assert p["out"].cpu().tolist() == t_o.tolist()
+        assert [int(v) for v in p["rng_state"].cpu().numpy().view(np.uint64)] == [int(v) for v in r_o]
+    for s in samplers:
+        s.close()
