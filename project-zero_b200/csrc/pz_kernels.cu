@@ -1087,6 +1087,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
     // List rows: the stream only records the sketch (each group's raw
     // maximum; temperature is monotone, so it orders the tempered values too).
     int slot = 0;
+    uint32_t run_max = 0u;  // the warp's largest sketch value so far
     for (int i = 0; i < nw; i++) {
       cp_async_wait<NS - 1>();
       const unsigned char *lsb = ldst + slot * kChunkBytes;
@@ -1094,18 +1095,25 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
 #pragma unroll
       for (int u = 0; u < kLaneVecs; u++) mv[u] = LaneVec<T>::vmax(*reinterpret_cast<const uint4 *>(lsb + u * 512));
       float m = max_of(mv);
+      // the lane's vectors of the slot are in registers (m depends on all of
+      // them, and the empty asm orders m's computation before the copies):
+      // refill the slot before the reductions, so that the copy is in flight
+      // that much sooner
+      asm volatile("" ::"f"(m));
+      if (i + NS < nw) issue(i + NS, slot);
+      cp_async_commit();
 #pragma unroll
       for (int o = 1; o < kSkGroupLanes; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
       const uint32_t v16 = sk16(m);
       if ((lane & (kSkGroupLanes - 1)) == 0 && sketch_ok)
         sketch[(warp + NW * i) * kSkPerChunk + lane / kSkGroupLanes] = static_cast<uint16_t>(v16);
-      const uint32_t wmax = __reduce_max_sync(0xFFFFFFFFu, v16);
-      if (lane == 0 && wmax > *reinterpret_cast<volatile uint32_t *>(&s_skmax)) atomicMax(&s_skmax, wmax);
+      run_max = max(run_max, v16);
       if (i == kInsertAt && hist_on && !defer) insert_ids(hid);
-      // this lane has read its vectors of the slot: refill them
-      if (i + NS < nw) issue(i + NS, slot);
-      cp_async_commit();
       slot = slot + 1 == NS ? 0 : slot + 1;
+    }
+    {
+      const uint32_t wmax = __reduce_max_sync(0xFFFFFFFFu, run_max);
+      if (lane == 0 && wmax > 0u) atomicMax(&s_skmax, wmax);
     }
     if (hist_on && !defer && nw <= kInsertAt) insert_ids(hid);  // a warp with too few chunks
   } else if (!use_block) {
