@@ -283,11 +283,8 @@ pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms,
                               double *rest_ms, int *calls, int *kernels);
 /* The same timing split by phase: phase_ms[0] slice_kernel, [1] the
  * full-vocabulary pass (full_kernel), [2] the vocab-sharded allgather,
- * [3] merge_kernel, and [4] the streaming launch alone (part of [0]: in a
- * call that decides its list rows in a second slice_kernel launch, the
- * first launch; otherwise all of [0]); summed over the timed calls.
- * Starts a new count. */
-pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double phase_ms[5],
+ * [3] merge_kernel; summed over the timed calls.  Starts a new count. */
+pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double phase_ms[4],
                                 int *calls, int *kernels);
 
 /* Seeds B RNG states on the device: state[r] = seed_base + r (0 -> 1, as

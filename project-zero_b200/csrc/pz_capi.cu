@@ -153,8 +153,6 @@ struct pz_sampler_ctx {
   uint32_t *sort_a = nullptr;
   uint32_t *sort_b = nullptr;
   float *full_e = nullptr;
-  uint16_t *sk_store = nullptr;  // two-phase launches: list rows' sketches
-  uint32_t *sk_max = nullptr;
   int64_t sort_stride = 0;
   int64_t e_stride = 0;
   int full_grid = 0;
@@ -292,9 +290,6 @@ pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
             c->alloc(&c->sort_a, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
             c->alloc(&c->sort_b, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
             c->alloc(&c->full_e, static_cast<size_t>(c->full_grid) * c->e_stride);
-  if (ok && L.max_top_k >= 2)
-    ok = c->alloc(&c->sk_store, static_cast<size_t>(B) * pz::slice_sketch_stride(L.max_vocab, 4)) &&
-         c->alloc(&c->sk_max, B);
   if (!ok) {
     c->release();
     delete c;
@@ -399,10 +394,9 @@ static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
 }
 
 // Events per profiled call: start, after slice_kernel, after full_kernel,
-// after the allgather, end (after merge_kernel), and (index 5) between the
-// two slice_kernel launches of a two-phase call.  Phases a call does not
+// after the allgather, end (after merge_kernel).  Phases a call does not
 // have are recorded back to back and time as zero.
-constexpr int kProfEvents = 6;
+constexpr int kProfEvents = 5;
 
 // The next profiling slot of the context (nullptr when timing is off or
 // its slots are used up).
@@ -513,41 +507,14 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     a.stagger_ctas = slots;
     a.stagger_occ = occ;
   }
-  // Two launches when every row has its own CTA and the rows may keep
-  // lists: the first streams every row and decides all but the list rows,
-  // whose sketches it stores; the second decides the list rows from their
-  // sketches.  A list row's end-of-row work (its bound, the re-read of its
-  // candidate groups, the ranking and the draw) then no longer holds a CTA
-  // slot that the stream of another row could use.
-  static const int two_phase_env = [] {
-    const char *e = std::getenv("PZ_TWO_PHASE");  // tuning override (0: one launch)
-    return e ? std::atoi(e) : -1;
-  }();
-  const bool two_phase = two_phase_env > 0 && a.S == 1 && a.kmax >= 2 && ctx->sk_store != nullptr;
-  if (two_phase) {
-    a.sk_store = ctx->sk_store;
-    a.sk_max = ctx->sk_max;
-    a.sk_stride = pz::slice_sketch_stride(V, dtype == PZ_DTYPE_BF16 ? 2 : 4);
-    a.stagger_ns = 0;  // no CTA of the streaming launch holds its slot for a list's end-of-row work
-  }
   const bool full_pass = !emit && !no_full;
   if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t), st) != cudaSuccess)
     return fail(PZ_ERR_CUDA);
   cudaEvent_t *ev = next_prof_slot(ctx, st);
   if (ev) cudaEventRecord(ev[0], st);
-  a.phase = two_phase ? 1 : 0;
   cudaError_t ce = pz::launch_slice(a, dtype, smem, st);
   if (ce != cudaSuccess) return fail_cuda(ce);
   int kernels = 1;  // slice_kernel decides every row itself
-  if (two_phase) {
-    if (ev) cudaEventRecord(ev[5], st);
-    a.phase = 2;
-    ce = pz::launch_slice(a, dtype, smem, st);
-    if (ce != cudaSuccess) return fail_cuda(ce);
-    kernels = 2;
-  } else if (ev) {
-    cudaEventRecord(ev[5], st);
-  }
   if (ev) cudaEventRecord(ev[1], st);
   if (full_pass) {
     FullArgs f{};
@@ -763,22 +730,20 @@ pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double *phase_ms, int *call
   if (!ctx) return fail(PZ_ERR_INVALID_ARGS);
   DeviceGuard g(ctx->device);
   if (!g.ok) return fail(PZ_ERR_CUDA);
-  // phases 0..3 between consecutive events 0..4; phase 4 from event 0 to 5
-  constexpr int kPhases = 5;
-  double sum[kPhases] = {0.0, 0.0, 0.0, 0.0, 0.0};
+  double sum[kProfEvents - 1] = {0.0, 0.0, 0.0, 0.0};
   for (int i = 0; i < ctx->prof_used; i++) {
     cudaEvent_t *ev = &ctx->prof[i * kProfEvents];
-    cudaError_t ce = cudaEventSynchronize(ev[4]);
+    cudaError_t ce = cudaEventSynchronize(ev[kProfEvents - 1]);
     if (ce != cudaSuccess) return fail_cuda(ce);
-    for (int j = 0; j < kPhases; j++) {
+    for (int j = 0; j + 1 < kProfEvents; j++) {
       float t = 0.0f;
-      ce = j < 4 ? cudaEventElapsedTime(&t, ev[j], ev[j + 1]) : cudaEventElapsedTime(&t, ev[0], ev[5]);
+      ce = cudaEventElapsedTime(&t, ev[j], ev[j + 1]);
       if (ce != cudaSuccess) return fail_cuda(ce);
       sum[j] += t;
     }
   }
   if (phase_ms)
-    for (int j = 0; j < kPhases; j++) phase_ms[j] = sum[j];
+    for (int j = 0; j + 1 < kProfEvents; j++) phase_ms[j] = sum[j];
   if (calls) *calls = ctx->prof_used;
   if (kernels) *kernels = ctx->prof_kernels;
   ctx->prof_used = 0;
@@ -788,7 +753,7 @@ pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double *phase_ms, int *call
 
 pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms, double *rest_ms,
                               int *calls, int *kernels) {
-  double ph[5];
+  double ph[kProfEvents - 1];
   const pz_status s = pz_ctx_profile_phases(ctx, ph, calls, kernels);
   if (s != PZ_OK) return s;
   if (slice_ms) *slice_ms = ph[0];

@@ -500,7 +500,7 @@ __device__ __noinline__ float raw_floor(float t, const RowPlan P) {
   return -INFINITY;
 }
 
-constexpr int kTQK = kListMaxK;  // lists up to this long use the sketch path
+constexpr int kTQK = 64;        // lists up to this long use the sketch path
 
 // The sketch of a list row's stream: for every chunk, the largest raw value
 // of each group of kSkGroupLanes lanes' vectors (64 f32 or 128 bf16
@@ -666,10 +666,6 @@ __host__ __device__ inline int slice_hbm_words(int V, int hts, int kcap) {
   return hts > 0 && kcap <= 1 ? (V + 127) >> 7 : 0;
 }
 
-int slice_sketch_stride(int V, int elem_bytes) {
-  return (slice_sketch_entries(V, elem_bytes, kTQK) + 7) / 8 * 8;
-}
-
 size_t slice_smem_bytes(int kcap, int hts, int nslots, int V, int elem_bytes) {
   const size_t sk = static_cast<size_t>(slice_sketch_entries(V, elem_bytes, kcap));
   return static_cast<size_t>(nslots) * kSliceWarps * kChunkBytes +
@@ -787,10 +783,8 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   };
   // one copy group per chunk slot, empty past the end, so that "chunk i has
   // landed" is always "at most NS - 1 groups pending"
-  // (phase 2 streams nothing: its list rows work from their stored sketch)
-  const bool ph2 = A.phase == 2;
   for (int i = 0; i < NS; i++) {
-    if (i < nw && !ph2) issue(i, i);
+    if (i < nw) issue(i, i);
     cp_async_commit();
   }
 
@@ -821,10 +815,6 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   const uint32_t goff = static_cast<uint32_t>(A.v_offset);
   const int cap = A.kcap + kCapB;         // block list buffer
   const int hwm = A.kcap + kCapB / 2;
-
-  // phase 2 decides only list rows; phase 1 leaves their decision to it
-  if (ph2 && !use_tq) return;
-  const bool defer = A.phase == 1 && use_tq;
 
   const int H = P0.pen_on ? h1 - h0 : 0;
   const int32_t *hrow = A.hist + h0;
@@ -938,7 +928,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
     insert_rest();
     __syncthreads();
   }
-  if (hist_on && use_tq && !defer) {
+  if (hist_on && use_tq) {
     // list rows: the table is filled during the stream (the first ids at the
     // warp's chunk kInsertAt, when their loads have landed), the rest after it
     init_hist();
@@ -1075,15 +1065,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   // through a raw threshold instead.
   const bool mulT = greedy || !P.divide;
   const float scale = greedy ? 1.0f : P.inv_T;
-  if (use_tq && ph2) {
-    // the sketch phase 1 stored, and the history table
-    const int nwords = sketch_ok ? nchunks * kSkPerChunk / 2 : 0;
-    const uint32_t *src = reinterpret_cast<const uint32_t *>(A.sk_store + static_cast<size_t>(row) * A.sk_stride);
-    uint32_t *dst = reinterpret_cast<uint32_t *>(sketch);
-    for (int i = tid; i < nwords; i += NT) dst[i] = __ldcg(src + i);
-    if (tid == 0) s_skmax = __ldcg(A.sk_max + row);
-    if (hist_on) insert_ids(hid);
-  } else if (use_tq) {
+  if (use_tq) {
     // List rows: the stream only records the sketch (each group's raw
     // maximum; temperature is monotone, so it orders the tempered values too).
     int slot = 0;
@@ -1108,14 +1090,14 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       if ((lane & (kSkGroupLanes - 1)) == 0 && sketch_ok)
         sketch[(warp + NW * i) * kSkPerChunk + lane / kSkGroupLanes] = static_cast<uint16_t>(v16);
       run_max = max(run_max, v16);
-      if (i == kInsertAt && hist_on && !defer) insert_ids(hid);
+      if (i == kInsertAt && hist_on) insert_ids(hid);
       slot = slot + 1 == NS ? 0 : slot + 1;
     }
     {
       const uint32_t wmax = __reduce_max_sync(0xFFFFFFFFu, run_max);
       if (lane == 0 && wmax > 0u) atomicMax(&s_skmax, wmax);
     }
-    if (hist_on && !defer && nw <= kInsertAt) insert_ids(hid);  // a warp with too few chunks
+    if (hist_on && nw <= kInsertAt) insert_ids(hid);  // a warp with too few chunks
   } else if (!use_block) {
     // argmax: the threshold is the block's best value so far (warp-uniform);
     // only a lane's maximum and its ties can beat it
@@ -1236,17 +1218,6 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
     }
   }
   cp_async_wait<0>();
-  if (defer) {
-    // phase 1: the row's sketch (whole 32-bit words: its length is a
-    // multiple of kSkPerChunk) to the store; phase 2 takes it from there
-    __syncthreads();
-    const int nwords = sketch_ok ? nchunks * kSkPerChunk / 2 : 0;
-    uint32_t *dst = reinterpret_cast<uint32_t *>(A.sk_store + static_cast<size_t>(row) * A.sk_stride);
-    const uint32_t *src = reinterpret_cast<const uint32_t *>(sketch);
-    for (int i = tid; i < nwords; i += NT) __stcg(dst + i, src[i]);
-    if (tid == 0) A.sk_max[row] = s_skmax;
-    return;
-  }
   // The CTA that will most likely take this slot next (one wave of CTAs
   // later) finds its row's settings in L2: its setup waits on them.
   if (tid == 0 && !split && A.stagger_ctas > 0) {

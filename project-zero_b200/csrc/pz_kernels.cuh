@@ -49,14 +49,6 @@ struct SliceArgs {
   int stagger_ns;
   int stagger_ctas;
   int stagger_occ;      // CTAs in flight per SM
-  // Two launches per batch (phase 1, then phase 2) instead of one (phase 0):
-  // in phase 1 list rows stream their row, store its sketch and leave (the
-  // other rows are decided as in phase 0); in phase 2 only list rows run,
-  // from the stored sketch, without streaming the row again.
-  int phase;
-  uint16_t *sk_store;   // [B][sk_stride] list rows' sketches (phases 1 and 2)
-  uint32_t *sk_max;     // [B] their largest entry
-  int sk_stride;        // entries per row (a multiple of 8)
   // scratch
   unsigned long long *slice_keys;  // [(B-B1)*S][kcap] split rows' slice lists
   int32_t *slice_cnt;              // [(B-B1)*S]
@@ -142,9 +134,6 @@ size_t logprob_smem_bytes(int V, int hcap);
 cudaError_t launch_slice(const SliceArgs &a, int dtype, size_t smem,
                          cudaStream_t st);
 size_t slice_smem_bytes(int kcap, int hts, int nstages, int V, int elem_bytes);
-// Entries per row of a two-phase launch's sketch store (a multiple of 8).
-int slice_sketch_stride(int V, int elem_bytes);
-constexpr int kListMaxK = 64;  // list rows (k_eff up to this) keep a sketch
 int slice_stages(int kcap, int hts);
 cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem,
                         cudaStream_t st);

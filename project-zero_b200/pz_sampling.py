@@ -432,14 +432,13 @@ class Sampler:
         return a.value, b.value, n.value, k.value
 
     def profile_phases(self):
-        """({'slice', 'full', 'allgather', 'merge', 'stream'} ms summed over
-        the timed calls, calls, kernels launched) since the last read;
-        'stream' is the streaming launch alone (part of 'slice')."""
-        ph = (ctypes.c_double * 5)()
+        """({'slice', 'full', 'allgather', 'merge'} ms summed over the timed
+        calls, calls, kernels launched) since the last read."""
+        ph = (ctypes.c_double * 4)()
         n, k = ctypes.c_int(), ctypes.c_int()
         _check(_lib.pz_ctx_profile_phases(self._h, ph, ctypes.byref(n), ctypes.byref(k)),
                "pz_ctx_profile_phases")
-        return dict(zip(("slice", "full", "allgather", "merge", "stream"), list(ph))), n.value, k.value
+        return dict(zip(("slice", "full", "allgather", "merge"), list(ph))), n.value, k.value
 
     def wait(self, timeout_ms, stream=None):
         """Bounded wait for the stream's work (NCCL errors and the deadline

@@ -72,3 +72,39 @@ def test_decode_step_graph_equals_the_host_loop(cuda, pz, oracle_lib, variant):
     # sequences must match exactly
     assert (got.cpu().numpy() == want).all()
     assert (states_end == st).all()
+
+
+def test_rng_state_checkpoint_resume(cuda, pz):
+    """Checkpoint and resume of the sampler's only state, the per-row RNG words
+    (the reference keeps one word per stream, generate.c:125): a 200-step
+    stream split in two, its RNG array saved to the host after 100 steps and
+    restored into a fresh context and buffer, draws the same tokens as the
+    unbroken stream."""
+    torch = cuda
+    B, V, N = 8, 32000, 200
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    xs = torch.randn(N, B, V, generator=g, device="cuda").mul_(2.5)
+    cfg = pz.configs_to_device(pz.make_configs(B, temperature=0.8, top_k=40, top_p=0.95), "cuda")
+
+    def run(sampler, rng, steps):
+        out = torch.empty(B, dtype=torch.int32, device="cuda")
+        toks = []
+        for i in steps:
+            sampler.sample(xs[i], cfg, rng, out, max_top_k=64, no_full_vocab=True)
+            toks.append(out.clone())
+        return torch.stack(toks)
+
+    s = pz.Sampler(0, max_batch=B, max_vocab=V, max_top_k=64, max_history=0)
+    rng = torch.empty(B, dtype=torch.int64, device="cuda")
+    pz.seed_states(rng, seed_base=42)
+    whole = run(s, rng, range(N))
+    pz.seed_states(rng, seed_base=42)
+    first = run(s, rng, range(N // 2))
+    saved = rng.cpu().numpy().copy()              # the checkpoint
+    s.close()
+    s2 = pz.Sampler(0, max_batch=B, max_vocab=V, max_top_k=64, max_history=0)
+    rng2 = torch.from_numpy(saved).cuda()         # resume
+    second = run(s2, rng2, range(N // 2, N))
+    s2.close()
+    assert torch.equal(torch.cat([first, second]), whole)
