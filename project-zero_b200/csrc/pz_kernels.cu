@@ -520,6 +520,28 @@ __host__ __device__ inline int slice_sketch_entries(int V, int elem_bytes, int k
 }
 __device__ __forceinline__ uint32_t sk16(float m) { return m == m ? f2ord(m) >> 16 : 0u; }
 
+// The smallest sketch value whose 16-bit bucket's largest raw value
+// tempers to tb or above (1 when every nonzero value's does), by
+// bisection.  b16: the bound's sketch value (its bucket qualifies, since
+// tb is the temper of its smallest raw value), or 0 for no bound (tb =
+// -inf).  Nonzero sketch values are at least f2ord(-inf) >> 16, and from
+// there the test is monotone in the value (temperature is monotone).
+__device__ __forceinline__ uint32_t sketch_vmin(uint32_t b16, float tb, const RowPlan &P) {
+  constexpr uint32_t kSkMin = kOrdNegInf >> 16;
+  const uint32_t ord_inf = f2ord(INFINITY);
+  auto qual = [&](uint32_t v) { return !(temper(ord2f(min((v << 16) | 0xFFFFu, ord_inf)), P) < tb); };
+  if (b16 <= kSkMin || qual(kSkMin)) return 1u;
+  uint32_t lo = kSkMin, hi = b16;  // qual(lo) false, qual(hi) true
+  while (hi - lo > 1u) {
+    const uint32_t mid = lo + (hi - lo) / 2u;
+    if (qual(mid))
+      hi = mid;
+    else
+      lo = mid;
+  }
+  return hi;
+}
+
 // A 32-bit global load issued where it stands (volatile asm keeps it ahead
 // of the stream's copies), for a value first used after the stream.
 __device__ __forceinline__ int ld_early(const int32_t *p) {
@@ -715,7 +737,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   __shared__ unsigned long long s_rng;  // the row's RNG state at entry
   __shared__ int s_sel[4];              // radix picks of the sketch bound
   __shared__ uint32_t s_skmax;          // largest sketch value of the slice
-  __shared__ int s_x0nan, s_timeout, s_cnt, s_n;
+  __shared__ int s_x0nan, s_timeout, s_cnt, s_gcnt, s_n;
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
@@ -1269,12 +1291,14 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
     uint32_t *bins = reinterpret_cast<uint32_t *>(ring);  // 2 x 256 counts
     int *glist = reinterpret_cast<int *>(ring + 2048);    // kGCap groups
     unsigned long long *sorted = reinterpret_cast<unsigned long long *>(ring + 6144);
-    const uint32_t ord_inf = f2ord(INFINITY);
     int nc = 0, ngs = 0;
     for (int pass = 0; pass < 2; pass++) {
       const bool all = pass == 0;
       for (int i = tid; i < 512; i += NT) bins[i] = 0u;
-      if (tid == 0) s_cnt = 0;
+      if (tid == 0) {
+        s_cnt = 0;
+        s_gcnt = 0;
+      }
       __syncthreads();
       if (pass == 0) x0_check();  // the history table is complete
       auto eligible = [&](int g) -> bool {
@@ -1322,20 +1346,16 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       const uint32_t bord = b16 << 16;
       tb = bord > kOrdNegInf ? temper(ord2f(bord), P) : -INFINITY;
       // the groups to read again: a maximum below ord2f((v + 1) << 16)
-      // tempers to at most that value's temper
+      // tempers to at most that value's temper, so a group qualifies when
+      // the largest raw value of its 16-bit bucket tempers to tb or above;
+      // that is the groups with sketch value v >= vmin
+      const uint32_t vmin = sketch_vmin(b16, tb, P);
       for (int g0 = 0; g0 < ng; g0 += NT) {
         const int g = g0 + tid;
-        bool sel = false;
-        if (g < ng) {
-          const uint32_t v = sketch[g];
-          if (v != 0u) {
-            const uint32_t up = min((v << 16) | 0xFFFFu, ord_inf);
-            sel = !(temper(ord2f(up), P) < tb);
-          }
-        }
+        const bool sel = g < ng && sketch[g] >= vmin;
         const uint32_t bal = __ballot_sync(0xFFFFFFFFu, sel);
         int base = 0;
-        if (lane == 0 && bal) base = atomicAdd(&s_cnt, __popc(bal));
+        if (lane == 0 && bal) base = atomicAdd(&s_gcnt, __popc(bal));
         base = __shfl_sync(0xFFFFFFFFu, base, 0);
         if (sel) {
           const int p = base + __popc(bal & lanemask_lt());
@@ -1343,10 +1363,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
         }
       }
       __syncthreads();
-      ngs = s_cnt;
-      __syncthreads();
-      if (tid == 0) s_cnt = 0;
-      __syncthreads();
+      ngs = s_gcnt;
       if (ngs <= kGCap) {
         // each group: kSkGroupLanes lanes x kLaneVecs vectors, read from L2
         // or HBM, XG at a time per thread with all loads in flight together
