@@ -107,9 +107,18 @@ def hbm_peak():
         return 6650.0, "fallback"
 
 
+def kernel_source_id():
+    """First 12 hex digits of the SHA-1 of the kernels' source file."""
+    import hashlib
+    with open(os.path.join(REPO, "project-zero_b200", "csrc", "pz_kernels.cu"), "rb") as f:
+        return hashlib.sha1(f.read()).hexdigest()[:12]
+
+
 def profile_traffic():
     """dram bytes per launch of the slice kernel from the committed ncu
-    summary, with the library build it describes."""
+    summary, and the kernel source it was captured from ("build:
+    pz_kernels.cu sha1 <12 hex>").  The traffic is dropped (None) when that
+    source is not the one being benched."""
     p = os.path.join(REPO, "profiles", "slice_kernel_config3.md")
     t, build = None, None
     try:
@@ -120,6 +129,9 @@ def profile_traffic():
                 build = line.split(":", 1)[1].strip()
     except OSError:
         pass
+    live = "pz_kernels.cu sha1 " + kernel_source_id()
+    if build != live:
+        return None, f"stale (capture of {build}, benched {live})"
     return t, build
 
 
@@ -500,20 +512,22 @@ def headline(C, args, peak, peak_kind):
         clocks = Clocks([C.bus_id(i) for i in range(min(n_local, torch.cuda.device_count()))])
         clocks.start()
         time.sleep(0.5)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    s.profile(args.steps)  # CUDA events around the kernels of each timed call
+    # the timed region: one event before the first step and one after the
+    # last (events between steps would add commands between the launches);
+    # inside, the library's own two events bracket each call's kernel
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.profile(args.steps)
     C.barrier()
     torch.cuda.synchronize()
+    start.record()
     for i in range(args.steps):
-        starts[i].record()
         step()
-        ends[i].record()
+    end.record()
     torch.cuda.synchronize()
     phases, n_prof, n_kernels = s.profile_phases()
     s.profile(0)
     C.barrier()
-    my_ms = starts[0].elapsed_time(ends[-1])
+    my_ms = start.elapsed_time(end)
     per_rank = C.gather(my_ms / args.steps)
     total_ms = C.max_over_ranks(my_ms)
     clk = clocks.stop() if clocks else None

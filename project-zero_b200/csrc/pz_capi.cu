@@ -166,6 +166,7 @@ struct pz_sampler_ctx {
   // kernel timing: kProfEvents events per call, bracketing its phases
   // (slice_kernel, full_kernel, the allgather, merge_kernel)
   std::vector<cudaEvent_t> prof;
+  std::vector<uint8_t> prof_short;  // per slot: only events 0 and 1 recorded
   int prof_used = 0;
   int prof_kernels = 0;
 
@@ -406,6 +407,7 @@ static cudaEvent_t *next_prof_slot(pz_sampler_ctx *ctx, cudaStream_t st) {
   if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
     return nullptr;  // no timing events inside a captured graph
   cudaEvent_t *ev = &ctx->prof[ctx->prof_used * kProfEvents];
+  ctx->prof_short[ctx->prof_used] = 0;
   ctx->prof_used++;
   return ev;
 }
@@ -568,7 +570,12 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     if (ce != cudaSuccess) return fail_cuda(ce);
     kernels++;
   }
-  if (ev) {
+  if (ev && kernels == 1 && !ev_out) {
+    // slice_kernel alone: its two events are the call's only ones (fewer
+    // commands between the launches of back-to-back calls)
+    ctx->prof_short[(ev - ctx->prof.data()) / kProfEvents] = 1;
+    ctx->prof_kernels += kernels;
+  } else if (ev) {
     cudaEventRecord(ev[2], st);
     ctx->prof_kernels += kernels;
     if (ev_out) {
@@ -714,6 +721,7 @@ pz_status pz_ctx_profile(pz_sampler_ctx *ctx, int n_calls) {
   if (!g.ok) return fail(PZ_ERR_CUDA);
   for (cudaEvent_t e : ctx->prof) cudaEventDestroy(e);
   ctx->prof.clear();
+  ctx->prof_short.assign(static_cast<size_t>(n_calls), 0);
   ctx->prof_used = 0;
   ctx->prof_kernels = 0;
   for (int i = 0; i < kProfEvents * n_calls; i++) {
@@ -733,9 +741,10 @@ pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double *phase_ms, int *call
   double sum[kProfEvents - 1] = {0.0, 0.0, 0.0, 0.0};
   for (int i = 0; i < ctx->prof_used; i++) {
     cudaEvent_t *ev = &ctx->prof[i * kProfEvents];
-    cudaError_t ce = cudaEventSynchronize(ev[kProfEvents - 1]);
+    const bool shrt = ctx->prof_short[i] != 0;
+    cudaError_t ce = cudaEventSynchronize(ev[shrt ? 1 : kProfEvents - 1]);
     if (ce != cudaSuccess) return fail_cuda(ce);
-    for (int j = 0; j + 1 < kProfEvents; j++) {
+    for (int j = 0; j + 1 < (shrt ? 2 : kProfEvents); j++) {
       float t = 0.0f;
       ce = cudaEventElapsedTime(&t, ev[j], ev[j + 1]);
       if (ce != cudaSuccess) return fail_cuda(ce);
