@@ -508,12 +508,6 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     a.stagger_ns = forced >= 0 ? forced : static_cast<int>(kStaggerFrac * life_ns);
     a.stagger_ctas = slots;
     a.stagger_occ = occ;
-    static const int cap = [] {
-      const char *e = std::getenv("PZ_STREAM_CAP");  // tuning override
-      return e ? std::atoi(e) : 0;
-    }();
-    a.stream_cap = cap;
-    if (cap > 0) a.stagger_ns = 0;
   }
   const bool full_pass = !emit && !no_full;
   if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t), st) != cudaSuccess)

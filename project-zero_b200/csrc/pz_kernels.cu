@@ -706,8 +706,6 @@ int slice_stages(int, int) { return kSlots; }
 // Arrivals of first-wave CTAs per SM (counted across launches; consecutive
 // arrivals on an SM take consecutive slots modulo its CTAs in flight).
 __device__ unsigned g_slot_arrivals[256];
-// List-row CTAs streaming, per SM (each launch returns them to zero).
-__device__ unsigned g_sm_streaming[256];
 
 // One CTA per row (or per slice of L columns of a split row).  The slice's
 // 16-byte-aligned body is cut into chunks of kChunkBytes; warp w streams
@@ -740,7 +738,6 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   __shared__ int s_sel[4];              // radix picks of the sketch bound
   __shared__ uint32_t s_skmax;          // largest sketch value of the slice
   __shared__ int s_x0nan, s_timeout, s_cnt, s_gcnt, s_n;
-  __shared__ unsigned s_sm;             // the SM whose streaming count this row holds
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
@@ -870,23 +867,6 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
           if (t - t0 >= wait) break;
         }
       }
-    }
-    if (use_tq && A.stream_cap > 0) {
-      // a place among the SM's streaming list rows: taken at once when one
-      // is free, else after a bounded wait (past it, taken anyway)
-      unsigned smid;
-      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-      unsigned *cnt = &g_sm_streaming[smid & 255u];
-      unsigned long long t0, t;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-      for (int it = 0;; it++) {
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        const bool give_up = it >= 20000 || t - t0 > 200000ull;
-        if (atomicAdd(cnt, 1u) < static_cast<unsigned>(A.stream_cap) || give_up) break;
-        atomicSub(cnt, 1u);
-        __nanosleep(256);
-      }
-      s_sm = smid & 255u;
     }
     s_plan = P0;
     s_rng = rng0;
@@ -1275,7 +1255,6 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   if (use_block) history_round();
   if (use_tq && hist_on) insert_rest();
   __syncthreads();
-  if (tid == 0 && use_tq && A.stream_cap > 0) atomicSub(&g_sm_streaming[s_sm], 1u);  // every warp's stream is done
   const bool timed_out = s_timeout != 0;
 
   // ---- this slice's list -> scratch ---------------------------------------

@@ -49,9 +49,6 @@ struct SliceArgs {
   int stagger_ns;
   int stagger_ctas;
   int stagger_occ;      // CTAs in flight per SM
-  // At most stream_cap list-row CTAs of an SM stream at once (0: no cap):
-  // the others wait, bounded, for one to finish its stream.
-  int stream_cap;
   // scratch
   unsigned long long *slice_keys;  // [(B-B1)*S][kcap] split rows' slice lists
   int32_t *slice_cnt;              // [(B-B1)*S]
