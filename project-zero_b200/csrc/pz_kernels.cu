@@ -1662,22 +1662,32 @@ __device__ __noinline__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32
     if (tid < 256)
       for (int w = 0; w < NW; w++) whist[w * 256 + tid] += tot[tid];
     __syncthreads();
-    for (int j0 = s0; j0 < s1; j0 += 32) {
-      const int j = j0 + lane;
-      const bool act = j < s1;
-      const uint32_t key = act ? ki[j] : 0u;
-      const uint32_t val = act ? vi[j] : 0u;
-      const uint32_t d = act ? ((key >> shift) & 255u) : (256u + lane);
-      const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
-      uint32_t pos = 0;
-      if (act) {
-        pos = whist[warp * 256 + d] + __popc(peers & lanemask_lt());
-        ko[pos] = key;
-        vo[pos] = val;
+    // the warp's segment in order, 4 x 32 entries a round: the round's
+    // loads first (in flight together), then its 4 groups of 32 in order
+    constexpr int RU = 4;
+    for (int j0 = s0; j0 < s1; j0 += 32 * RU) {
+      uint32_t key[RU], val[RU];
+#pragma unroll
+      for (int u = 0; u < RU; u++) {
+        const int j = j0 + u * 32 + lane;
+        key[u] = j < s1 ? ki[j] : 0u;
+        val[u] = j < s1 ? vi[j] : 0u;
       }
-      __syncwarp();
-      if (act && lane == __ffs(peers) - 1) whist[warp * 256 + d] += __popc(peers);
-      __syncwarp();
+#pragma unroll
+      for (int u = 0; u < RU; u++) {
+        const int j = j0 + u * 32 + lane;
+        const bool act = j < s1;
+        const uint32_t d = act ? ((key[u] >> shift) & 255u) : (256u + lane);
+        const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
+        if (act) {
+          const uint32_t pos = whist[warp * 256 + d] + __popc(peers & lanemask_lt());
+          ko[pos] = key[u];
+          vo[pos] = val[u];
+        }
+        __syncwarp();
+        if (act && lane == __ffs(peers) - 1) whist[warp * 256 + d] += __popc(peers);
+        __syncwarp();
+      }
     }
     __threadfence_block();
     __syncthreads();
