@@ -1631,8 +1631,17 @@ __device__ __noinline__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32
     uint32_t *ko = in1 ? k0 : k1, *vo = in1 ? v0 : v1;
     for (int i = tid; i < NW * 256; i += NT) whist[i] = 0u;
     __syncthreads();
-    for (int j = s0 + lane; j < s1; j += 32)
-      atomicAdd(&whist[warp * 256 + ((ki[j] >> shift) & 255u)], 1u);
+    for (int j0 = s0; j0 < s1; j0 += 32 * 8) {
+      uint32_t kk[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int j = j0 + u * 32 + lane;
+        kk[u] = j < s1 ? ki[j] : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        if (j0 + u * 32 + lane < s1) atomicAdd(&whist[warp * 256 + ((kk[u] >> shift) & 255u)], 1u);
+    }
     __syncthreads();
     if (tid < 256) {
       uint32_t run = 0;
@@ -1664,7 +1673,7 @@ __device__ __noinline__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32
     __syncthreads();
     // the warp's segment in order, 4 x 32 entries a round: the round's
     // loads first (in flight together), then its 4 groups of 32 in order
-    constexpr int RU = 4;
+    constexpr int RU = 8;
     for (int j0 = s0; j0 < s1; j0 += 32 * RU) {
       uint32_t key[RU], val[RU];
 #pragma unroll

@@ -24,23 +24,29 @@
 
 namespace pz {
 
+// Increments are kept in 32 bits, saturating at kSeqClamp: a sum that
+// reaches 2^24 has left the binade (N < 2^24 inside it), so past that only
+// "crossed" matters, never the exact count.
 struct SeqMap {
-  unsigned long long e, o;  // increment of N when N is even / odd
+  uint32_t e, o;  // increment of N when N is even / odd
 };
 
 __device__ __forceinline__ SeqMap seq_identity() { return SeqMap{0ull, 0ull}; }
 
+constexpr uint32_t kSeqClamp = 1u << 30;
+
 // f applied first, then g.
 __device__ __forceinline__ SeqMap seq_compose(SeqMap f, SeqMap g) {
   SeqMap h;
-  h.e = f.e + ((f.e & 1ull) ? g.o : g.e);
-  h.o = f.o + ((f.o & 1ull) ? g.e : g.o);
+  h.e = min(f.e + ((f.e & 1u) ? g.o : g.e), kSeqClamp);
+  h.o = min(f.o + ((f.o & 1u) ? g.e : g.o), kSeqClamp);
   return h;
 }
 
-__device__ __forceinline__ unsigned long long seq_apply(SeqMap f,
-                                                        unsigned long long N) {
-  return N + ((N & 1ull) ? f.o : f.e);
+// N < 2^24 + 2 * kSeqClamp (an applied prefix, then one more element):
+// the result stays below 2^32.
+__device__ __forceinline__ uint32_t seq_apply(SeqMap f, uint32_t N) {
+  return N + ((N & 1u) ? f.o : f.e);
 }
 
 // Grid exponent eu (u = 2^eu) of the binade holding s >= 0.  Zero,
@@ -50,19 +56,18 @@ __device__ __forceinline__ int seq_grid_exp(float s) {
   return (ex == 0 ? 1 : ex) - 150;
 }
 // s = N * 2^eu, with N < 2^24.
-__device__ __forceinline__ unsigned long long seq_N(float s) {
+__device__ __forceinline__ uint32_t seq_N(float s) {
   const uint32_t b = __float_as_uint(s);
   const int ex = (b >> 23) & 0xFF;
   const uint32_t m = b & 0x7FFFFFu;
   return ex == 0 ? m : (m | 0x800000u);
 }
-__device__ __forceinline__ float seq_float(unsigned long long N, int eu) {
+__device__ __forceinline__ float seq_float(uint32_t N, int eu) {
   return __uint_as_float(static_cast<uint32_t>((eu + 149) << 23) +
                          static_cast<uint32_t>(N));
 }
 
-constexpr unsigned long long kSeqLimit = 1ull << 24;
-constexpr unsigned long long kSeqClamp = 1ull << 40;
+constexpr uint32_t kSeqLimit = 1u << 24;
 
 // The map of adding x >= 0 on grid 2^eu.
 __device__ __forceinline__ SeqMap seq_elem(float x, int eu) {
@@ -76,13 +81,13 @@ __device__ __forceinline__ SeqMap seq_elem(float x, int eu) {
     M |= 0x800000u;
     E2 = ex - 150;
   }
-  unsigned long long m = 0;
+  uint32_t m = 0;
   bool tie = false;
   if (M != 0) {
     const int sh = E2 - eu;
     if (sh >= 0) {
-      m = sh >= 40 ? kSeqClamp : (static_cast<unsigned long long>(M) << sh);
-      if (m > kSeqClamp) m = kSeqClamp;
+      // M < 2^24: shifts up to 6 stay below 2^30
+      m = sh >= 7 ? kSeqClamp : min(M << sh, kSeqClamp);
     } else {
       const int q = -sh;
       if (q < 26) {
@@ -98,7 +103,7 @@ __device__ __forceinline__ SeqMap seq_elem(float x, int eu) {
   }
   SeqMap f{m, m};
   if (tie) {
-    if (m & 1ull)
+    if (m & 1u)
       f.e = m + 1;
     else
       f.o = m + 1;
@@ -211,7 +216,7 @@ __device__ SeqResult seq_scan(int n, Get get, int kind, float target,
     while (!chunk_done) {
       const float s = sh.s;
       const int eu = seq_grid_exp(s);
-      const unsigned long long N0 = seq_N(s);
+      const uint32_t N0 = seq_N(s);
       // integer form of the target on this grid
       unsigned long long thrN = ~0ull;
       if (kind != kSeqNone) {
@@ -238,15 +243,15 @@ __device__ SeqResult seq_scan(int n, Get get, int kind, float target,
       }
       SeqMap total;
       const SeqMap P = seq_block_exscan<NT>(F, total, sh);
-      unsigned long long N = seq_apply(P, N0);
+      uint32_t N = seq_apply(P, N0);
       int mycross = 0x7FFFFFFF, myhit = 0x7FFFFFFF;
-      unsigned long long Nc = 0, Nh = 0;
+      uint32_t Nc = 0, Nh = 0;
       float xc = 0.0f;
 #pragma unroll
       for (int e = 0; e < E; e++) {
         const int j = c0 + tid * E + e;
         if (j >= start && j < n && mycross == 0x7FFFFFFF && myhit == 0x7FFFFFFF) {
-          const unsigned long long Nn = seq_apply(seq_elem(x[e], eu), N);
+          const uint32_t Nn = seq_apply(seq_elem(x[e], eu), N);
           if (Nn >= kSeqLimit) {
             mycross = j;
             Nc = N;
