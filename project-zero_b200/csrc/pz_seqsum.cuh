@@ -111,186 +111,369 @@ __device__ __forceinline__ SeqMap seq_elem(float x, int eu) {
   return f;
 }
 
-struct SeqShared {
-  SeqMap warp_tot[32];
-  float s;
-  int cross;
-  int hit;
-  int done_pos;
-  float hit_s;
-};
+// The map of adding x >= 0 on grid 2^eu for a normal running sum
+// (-126 <= eu), in float arithmetic, with sc = 2^-eu:
+//   y = x * sc is exact (a power-of-two scaling; a product below 2^-126 may
+//     round, but it is then far below 1/2 and adds nothing);
+//   rint(y) (ties to even) is read off y + 2^23, exact for 0 <= y < 2^23;
+//   d = rint(y) - y is exact, and |d| = 1/2 exactly at a tie.
+// The even increment rint(y) serves an even N; at a tie an odd N takes the
+// other neighbour, rint(y) - 2d.  On a normal grid N >= 2^23, so y >= 2^23
+// leaves the binade whatever N is: the increment is then reported as 2^24.
+// Agrees with seq_elem wherever seq_elem's increment is below 2^23.
+__device__ __forceinline__ SeqMap seq_elem_fast(float x, float sc, bool &tie) {
+  const float y = __fmul_rn(x, sc);
+  const float r = __fadd_rn(y, 8388608.0f);
+  uint32_t m = __float_as_uint(r) - 0x4B000000u;
+  const float d = __fsub_rn(__fsub_rn(r, 8388608.0f), y);
+  tie = fabsf(d) == 0.5f;
+  if (!(y < 8388608.0f)) {  // also NaN and inf terms
+    m = kSeqLimit;
+    tie = false;
+  }
+  SeqMap f{m, m};
+  if (tie) f.o = d < 0.0f ? m + 1u : m - 1u;
+  return f;
+}
 
-// Exclusive block scan of SeqMap; also returns the block total.
-template <int NT>
-__device__ __forceinline__ SeqMap seq_block_exscan(SeqMap v, SeqMap &total,
-                                                   SeqShared &sh) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  SeqMap incl = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    SeqMap w;
-    w.e = __shfl_up_sync(0xFFFFFFFFu, incl.e, o);
-    w.o = __shfl_up_sync(0xFFFFFFFFu, incl.o, o);
-    if (lane >= o) incl = seq_compose(w, incl);
-  }
-  if (lane == 31) sh.warp_tot[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    constexpr int NW = NT / 32;
-    SeqMap t = lane < NW ? sh.warp_tot[lane] : seq_identity();
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      SeqMap w;
-      w.e = __shfl_up_sync(0xFFFFFFFFu, t.e, o);
-      w.o = __shfl_up_sync(0xFFFFFFFFu, t.o, o);
-      if (lane >= o) t = seq_compose(w, t);
-    }
-    if (lane < NW) sh.warp_tot[lane] = t;  // inclusive over warps
-  }
-  __syncthreads();
-  SeqMap before_warp = warp ? sh.warp_tot[warp - 1] : seq_identity();
-  total = sh.warp_tot[NT / 32 - 1];
-  // exclusive within the warp
-  SeqMap ex;
-  ex.e = __shfl_up_sync(0xFFFFFFFFu, incl.e, 1);
-  ex.o = __shfl_up_sync(0xFFFFFFFFu, incl.o, 1);
-  if (lane == 0) ex = seq_identity();
-  __syncthreads();  // warp_tot may be rewritten by the next scan
-  return seq_compose(before_warp, ex);
+// 2^-eu as a float, for -126 <= eu <= 127.
+__device__ __forceinline__ float seq_scale(int eu) {
+  return __uint_as_float(static_cast<uint32_t>(127 - eu) << 23);
 }
 
 enum SeqTarget : int { kSeqNone = 0, kSeqGE = 1, kSeqGT = 2 };
 
+__device__ __forceinline__ bool seq_meets(float s, int kind, float target) {
+  return (kind == kSeqGE && s >= target) || (kind == kSeqGT && s > target);
+}
+
+// Integer form of the target on grid 2^eu: s = N * 2^eu meets it iff
+// N >= the returned value (0xFFFFFFFF: never on this grid).
+__device__ __forceinline__ uint32_t seq_thr(int kind, float target, int eu) {
+  if (kind == kSeqNone) return 0xFFFFFFFFu;
+  const double q = static_cast<double>(target) *
+                   __longlong_as_double(static_cast<long long>(1023 - eu) << 52);
+  if (q != q) return 0xFFFFFFFFu;
+  if (kind == kSeqGE) {  // N >= q  <=>  N >= ceil(q)
+    const double c = ceil(q);
+    return c <= 0.0 ? 0u : (c >= 4294967295.0 ? 0xFFFFFFFFu : static_cast<uint32_t>(c));
+  }
+  const double f = floor(q);  // N > q  <=>  N >= floor(q) + 1
+  return f < 0.0 ? 0u : (f >= 4294967294.0 ? 0xFFFFFFFFu : static_cast<uint32_t>(f) + 1u);
+}
+
+// Composite map of the warp's terms (lane l holds the 8 consecutive terms
+// x[0..7] that follow lane l-1's) on grid 2^eu; every lane gets it.  On a
+// normal grid a run without ties adds a constant, so the usual case is one
+// integer sum; a run with a tie, or a subnormal grid, composes the maps in
+// order (lane runs first, then an ordered shuffle tree).
+__device__ __forceinline__ SeqMap seq_warp_map(const float (&x)[8], int eu) {
+  const int lane = threadIdx.x & 31;
+  if (eu >= -126) {
+    const float sc = seq_scale(eu);
+    uint32_t sum = 0;
+    bool tie_any = false;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      bool tie;
+      const SeqMap f = seq_elem_fast(x[e], sc, tie);
+      sum += f.e;  // <= 8 * 2^24
+      tie_any |= tie;
+    }
+    if (!__any_sync(0xFFFFFFFFu, tie_any)) {
+      const uint32_t t = __reduce_add_sync(0xFFFFFFFFu, min(sum, kSeqLimit));  // <= 2^29
+      return SeqMap{t, t};
+    }
+  }
+  SeqMap F = seq_identity();
+  if (eu >= -126) {
+    const float sc = seq_scale(eu);
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      bool tie;
+      F = seq_compose(F, seq_elem_fast(x[e], sc, tie));
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; e++) F = seq_compose(F, seq_elem(x[e], eu));
+  }
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    SeqMap g;
+    g.e = __shfl_down_sync(0xFFFFFFFFu, F.e, o);
+    g.o = __shfl_down_sync(0xFFFFFFFFu, F.o, o);
+    if ((lane & (2 * o - 1)) == 0) F = seq_compose(F, g);
+  }
+  F.e = __shfl_sync(0xFFFFFFFFu, F.e, 0);
+  F.o = __shfl_sync(0xFFFFFFFFu, F.o, 0);
+  return F;
+}
+
+// Exact replay, warp-wide, of the terms j in [start, j1) of the tile that
+// starts at term j0 (lane l loads terms j0 + 8l .. j0 + 8l + 7), from the
+// running sum s
+// (uniform arguments).  Returns the sum after the last term replayed;
+// hit = the first j whose sum meets the target (the replay stops there), or
+// -1.  Inside a binade the maps give every prefix (an exclusive warp scan);
+// the one term that leaves the binade is added with a real FADD, and the
+// replay goes on from the next term on the new grid.
 struct SeqResult {
   float s;   // sum of all n terms, or the prefix sum at the hit
   int hit;   // first j whose prefix meets the target, or -1
 };
 
-// Replays s = fl(s + x_j) for j = 0..n-1 (x_j = get(j) >= 0) starting from
-// s = 0.  With a target, stops at the first j where s_j >= target (kSeqGE)
-// or s_j > target (kSeqGT).  Block-wide call.  get must be a pure function
-// of j (the next chunk's terms are fetched while the current one is
-// scanned).
+template <typename Src>
+__device__ __noinline__ SeqResult seq_tile_exact(const Src src, int j0, int start, int j1, float s,
+                                                 int kind, float target) {
+  const int lane = threadIdx.x & 31;
+  float x[8];
+  src.load8(j0 + 8 * lane, j1, x);
+  while (start < j1) {
+    if (!(s <= 3.40282347e38f))  // NaN or +inf: every later sum is s
+      return SeqResult{s, seq_meets(s, kind, target) ? start : -1};
+    const int eu = seq_grid_exp(s);
+    const uint32_t N0 = seq_N(s);
+    const uint32_t thrN = seq_thr(kind, target, eu);
+    SeqMap F = seq_identity();
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int j = j0 + 8 * lane + e;
+      if (j >= start && j < j1) F = seq_compose(F, seq_elem(x[e], eu));
+    }
+    SeqMap incl = F;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      SeqMap w;
+      w.e = __shfl_up_sync(0xFFFFFFFFu, incl.e, o);
+      w.o = __shfl_up_sync(0xFFFFFFFFu, incl.o, o);
+      if (lane >= o) incl = seq_compose(w, incl);
+    }
+    SeqMap ex;
+    ex.e = __shfl_up_sync(0xFFFFFFFFu, incl.e, 1);
+    ex.o = __shfl_up_sync(0xFFFFFFFFu, incl.o, 1);
+    if (lane == 0) ex = seq_identity();
+    uint32_t N = seq_apply(ex, N0);
+    int ev = 0x7FFFFFFF;
+    bool cross = false;
+    uint32_t Nev = 0;
+    float xev = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int j = j0 + 8 * lane + e;
+      if (j >= start && j < j1 && ev == 0x7FFFFFFF) {
+        const uint32_t Nn = seq_apply(seq_elem(x[e], eu), N);
+        if (Nn >= kSeqLimit) {
+          ev = j;
+          cross = true;
+          Nev = N;
+          xev = x[e];
+        } else if (Nn >= thrN) {
+          ev = j;
+          Nev = Nn;
+        }
+        N = Nn;
+      }
+    }
+    const unsigned bal = __ballot_sync(0xFFFFFFFFu, ev != 0x7FFFFFFF);
+    if (bal == 0u) {
+      SeqMap tot;
+      tot.e = __shfl_sync(0xFFFFFFFFu, incl.e, 31);
+      tot.o = __shfl_sync(0xFFFFFFFFu, incl.o, 31);
+      return SeqResult{seq_float(seq_apply(tot, N0), eu), -1};
+    }
+    const int src = __ffs(bal) - 1;  // lanes hold consecutive runs: the lowest lane is first
+    ev = __shfl_sync(0xFFFFFFFFu, ev, src);
+    cross = __shfl_sync(0xFFFFFFFFu, cross, src);
+    Nev = __shfl_sync(0xFFFFFFFFu, Nev, src);
+    xev = __shfl_sync(0xFFFFFFFFu, xev, src);
+    if (!cross) return SeqResult{seq_float(Nev, eu), ev};
+    s = __fadd_rn(seq_float(Nev, eu), xev);
+    if (seq_meets(s, kind, target)) return SeqResult{s, ev};
+    start = ev + 1;
+  }
+  return SeqResult{s, -1};
+}
+
+// Term sources for seq_scan.  at(j) is term j; load8(j, n, x) fills x with
+// terms j..j+7 (0 past n), with 16-byte loads when they are aligned.
+struct SeqSrcF32 {  // x_j = p[j], or fl(p[j] * scale) when scaled
+  const float *p;
+  float scale;
+  bool scaled;
+  __device__ __forceinline__ float at(int j) const {
+    return scaled ? __fmul_rn(p[j], scale) : p[j];
+  }
+  __device__ __forceinline__ void load8(int j, int n, float (&x)[8]) const {
+    if (j + 8 <= n && (reinterpret_cast<uintptr_t>(p + j) & 15u) == 0u) {
+      const float4 a = *reinterpret_cast<const float4 *>(p + j);
+      const float4 b = *reinterpret_cast<const float4 *>(p + j + 4);
+      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+      x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+      if (scaled) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) x[e] = __fmul_rn(x[e], scale);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) x[e] = j + e < n ? at(j + e) : 0.0f;
+    }
+  }
+};
+
+struct SeqSrcKey {  // x_j = the float whose bits are ~k[j]
+  const uint32_t *k;
+  __device__ __forceinline__ float at(int j) const { return __uint_as_float(~k[j]); }
+  __device__ __forceinline__ void load8(int j, int n, float (&x)[8]) const {
+    if (j + 8 <= n && (reinterpret_cast<uintptr_t>(k + j) & 15u) == 0u) {
+      const uint4 a = *reinterpret_cast<const uint4 *>(k + j);
+      const uint4 b = *reinterpret_cast<const uint4 *>(k + j + 4);
+      x[0] = __uint_as_float(~a.x); x[1] = __uint_as_float(~a.y);
+      x[2] = __uint_as_float(~a.z); x[3] = __uint_as_float(~a.w);
+      x[4] = __uint_as_float(~b.x); x[5] = __uint_as_float(~b.y);
+      x[6] = __uint_as_float(~b.z); x[7] = __uint_as_float(~b.w);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) x[e] = j + e < n ? at(j + e) : 0.0f;
+    }
+  }
+};
+
+struct SeqShared {
+  SeqMap map[32];  // one tile's map per warp of the current wave
+  float s;
+  int done_pos;
+  int t0;
+};
+
+constexpr int kSeqTile = 256;  // terms per tile: 8 per lane of a warp
+
+// Replays s = fl(s + x_j) for j = 0..n-1 (x_j >= 0) starting from s = 0.
+// With a target, stops at the first j where s_j >= target (kSeqGE) or
+// s_j > target (kSeqGT).  Block-wide call (NT threads, uniform arguments).
 //
-// The first head_cap terms (the running sum doubles, and so leaves its
-// binade, most often early on: about once per doubling of the terms seen)
-// are evaluated by all threads into head_buf and added in order by one
-// thread; the rest go E consecutive terms per thread per chunk through the
-// parallel replay, which restarts only at the few binade crossings left.
-// The maps of a thread's terms are not kept: they are recomputed from the
-// terms (a few integer operations) where the prefixes are needed.
-template <int NT, int E, typename Get>
-__device__ SeqResult seq_scan(int n, Get get, int kind, float target,
-                              SeqShared &sh, float *head_buf, int head_cap) {
-  const int tid = threadIdx.x;
+// The first head_cap terms (a multiple of 8; the running sum leaves its
+// binade most often early on, about once per doubling of the terms seen)
+// are added in order by one thread.  The rest is cut into tiles of 256
+// terms and walked a wave of NT/32 tiles at a time:
+//   every warp computes its tile's composite map on the grid of the sum at
+//   the wave's start (seq_warp_map) and loads the next wave's terms;
+//   warp 0 then applies the maps in order.  N only grows, so a tile leaves
+//   the binade, or meets the target, iff its end does: such a tile is
+//   replayed exactly by warp 0 (seq_tile_exact), and if the grid changed
+//   the wave ends after it (the remaining maps are on the old grid).
+// Two barriers per wave; sums leave their binade a handful of times after
+// the head, so nearly every tile costs one map and one integer add.
+template <int NT, typename Src>
+__device__ __noinline__ SeqResult seq_scan(int n, const Src src, int kind, float target, SeqShared &sh,
+                              float *head_buf, int head_cap) {
+  constexpr int NW = NT / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = n < head_cap ? n : head_cap;
-  for (int j = tid; j < K; j += NT) head_buf[j] = get(j);
+  for (int j = tid; j < K; j += NT) head_buf[j] = src.at(j);
   __syncthreads();
   if (tid == 0) {
     float s = 0.0f;
     int done = -1;
-    for (int j = 0; j < K; j++) {
-      s = __fadd_rn(s, head_buf[j]);
-      if ((kind == kSeqGE && s >= target) || (kind == kSeqGT && s > target)) {
-        done = j;
-        break;
+    // 8 terms a round: the round's loads first, then the chain of adds
+    // (padding terms are 0: adding 0 leaves s as it is), then the round's
+    // prefixes tested against the target off the chain
+    for (int j0 = 0; j0 < K && done < 0; j0 += 8) {
+      float h[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) h[e] = j0 + e < K ? head_buf[j0 + e] : 0.0f;
+      float ps[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        s = __fadd_rn(s, h[e]);
+        ps[e] = s;
+      }
+      if (kind != kSeqNone) {
+#pragma unroll
+        for (int e = 7; e >= 0; e--)
+          if (j0 + e < K && seq_meets(ps[e], kind, target)) done = j0 + e;
+        if (done >= 0) s = ps[done - j0];
       }
     }
     sh.s = s;
     sh.done_pos = done;
   }
   __syncthreads();
-  float x[E], xn[E];
-  auto fetch = [&](int c, float(&dst)[E]) {
+  const int ntiles = (n - K + kSeqTile - 1) / kSeqTile;
+  auto load_tile = [&](int t, float(&dst)[8]) {
+    if (t < ntiles) {
+      src.load8(K + t * kSeqTile + lane * 8, n, dst);
+    } else {
 #pragma unroll
-    for (int e = 0; e < E; e++) {
-      const int j = c + tid * E + e;
-      dst[e] = j < n ? get(j) : 0.0f;
+      for (int e = 0; e < 8; e++) dst[e] = 0.0f;
     }
   };
-  if (K < n && sh.done_pos < 0) fetch(K, x);
-  for (int c0 = K; c0 < n && sh.done_pos < 0; c0 += NT * E) {
-    if (c0 + NT * E < n) fetch(c0 + NT * E, xn);  // in flight during this chunk
-    int start = c0;
-    bool chunk_done = false;
-    while (!chunk_done) {
-      const float s = sh.s;
-      const int eu = seq_grid_exp(s);
-      const uint32_t N0 = seq_N(s);
-      // integer form of the target on this grid
-      unsigned long long thrN = ~0ull;
-      if (kind != kSeqNone) {
-        const double q = static_cast<double>(target) * exp2(static_cast<double>(-eu));
-        if (kind == kSeqGE) {
-          // s_j >= target  <=>  N_j >= ceil(q)
-          const double c = ceil(q);
-          thrN = (q != q) ? ~0ull : (c <= 0.0 ? 0ull : (c >= 1e15 ? ~0ull : static_cast<unsigned long long>(c)));
-        } else {
-          // s_j > target  <=>  N_j > floor(q)  <=>  N_j >= floor(q) + 1
-          const double f = floor(q);
-          thrN = (q != q) ? ~0ull : (f < 0.0 ? 0ull : (f >= 1e15 ? ~0ull : static_cast<unsigned long long>(f) + 1ull));
-        }
-      }
-      SeqMap F = seq_identity();
-#pragma unroll
-      for (int e = 0; e < E; e++) {
-        const int j = c0 + tid * E + e;
-        if (j >= start && j < n) F = seq_compose(F, seq_elem(x[e], eu));
-      }
-      if (tid == 0) {
-        sh.cross = 0x7FFFFFFF;
-        sh.hit = 0x7FFFFFFF;
-      }
-      SeqMap total;
-      const SeqMap P = seq_block_exscan<NT>(F, total, sh);
-      uint32_t N = seq_apply(P, N0);
-      int mycross = 0x7FFFFFFF, myhit = 0x7FFFFFFF;
-      uint32_t Nc = 0, Nh = 0;
-      float xc = 0.0f;
-#pragma unroll
-      for (int e = 0; e < E; e++) {
-        const int j = c0 + tid * E + e;
-        if (j >= start && j < n && mycross == 0x7FFFFFFF && myhit == 0x7FFFFFFF) {
-          const uint32_t Nn = seq_apply(seq_elem(x[e], eu), N);
-          if (Nn >= kSeqLimit) {
-            mycross = j;
-            Nc = N;
-            xc = x[e];
-          } else if (Nn >= thrN) {
-            myhit = j;
-            Nh = Nn;
-          }
-          N = Nn;
-        }
-      }
-      if (mycross != 0x7FFFFFFF) atomicMin(&sh.cross, mycross);
-      if (myhit != 0x7FFFFFFF) atomicMin(&sh.hit, myhit);
-      __syncthreads();
-      const int cross = sh.cross, hit = sh.hit;
-      __syncthreads();
-      if (hit < cross) {
-        if (myhit == hit) {
-          sh.s = seq_float(Nh, eu);
-          sh.done_pos = hit;
-        }
-        chunk_done = true;
-      } else if (cross != 0x7FFFFFFF) {
-        if (mycross == cross) {
-          const float sn = __fadd_rn(seq_float(Nc, eu), xc);
-          sh.s = sn;
-          if ((kind == kSeqGE && sn >= target) || (kind == kSeqGT && sn > target))
-            sh.done_pos = cross;
-        }
-        start = cross + 1;
-      } else {
-        if (tid == 0) sh.s = seq_float(seq_apply(total, N0), eu);
-        chunk_done = true;
-      }
-      __syncthreads();
-      if (sh.done_pos >= 0) break;
+  float x[8];
+  int t0 = 0;
+  if (ntiles > 0 && sh.done_pos < 0) load_tile(warp, x);
+  while (ntiles > 0) {
+    if (sh.done_pos >= 0 || t0 >= ntiles) break;
+    const float s0 = sh.s;
+    const bool finite = s0 <= 3.40282347e38f;
+    const int eu = seq_grid_exp(s0);
+    if (finite && t0 + warp < ntiles) {
+      const SeqMap f = seq_warp_map(x, eu);
+      if (lane == 0) sh.map[warp] = f;
     }
+    float xn[8];
+    load_tile(t0 + NW + warp, xn);  // the next wave's terms, in flight during the walk
+    __syncthreads();
+    if (warp == 0) {
+      float s = s0;
+      int done = -1, tnext = t0 + NW;
+      const int tend = min(t0 + NW, ntiles);
+      if (!finite) {
+        // NaN or +inf: every later sum is s
+        if (seq_meets(s, kind, target)) done = K + t0 * kSeqTile;
+        tnext = ntiles;
+      } else {
+        uint32_t N = seq_N(s0);
+        const uint32_t thrN = seq_thr(kind, target, eu);
+        bool exact = false;  // s is current (N is not)
+        for (int t = t0; t < tend; t++) {
+          const SeqMap f = sh.map[t - t0];
+          const uint32_t Nn = seq_apply(f, N);
+          if (Nn < kSeqLimit && Nn < thrN) {
+            N = Nn;
+            continue;
+          }
+          // the tile leaves the binade or meets the target: replay it
+          const int j0 = K + t * kSeqTile, j1 = min(n, j0 + kSeqTile);
+          const SeqResult rt = seq_tile_exact(src, j0, j0, j1, seq_float(N, eu), kind, target);
+          s = rt.s;
+          exact = true;
+          if (rt.hit >= 0) {
+            done = rt.hit;
+            break;
+          }
+          if (!(s <= 3.40282347e38f) || seq_grid_exp(s) != eu) {
+            tnext = t + 1;  // the rest of the wave's maps are on the old grid
+            break;
+          }
+          N = seq_N(s);
+          exact = false;
+        }
+        if (!exact) s = seq_float(N, eu);
+      }
+      if (lane == 0) {
+        sh.s = s;
+        sh.done_pos = done;
+        sh.t0 = tnext;
+      }
+    }
+    __syncthreads();
+    const int t0n = sh.t0;
+    if (t0n == t0 + NW) {
 #pragma unroll
-    for (int e = 0; e < E; e++) x[e] = xn[e];
+      for (int e = 0; e < 8; e++) x[e] = xn[e];
+    } else if (t0n < ntiles) {
+      load_tile(t0n + warp, x);
+    }
+    t0 = t0n;
   }
   SeqResult r;
   r.s = sh.s;
