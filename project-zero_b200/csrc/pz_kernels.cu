@@ -1864,15 +1864,17 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
     }
     __syncthreads();
     // pass 1b: the exact normaliser over the stored e values
-    const SeqResult s1 = seq_scan<NT>(V, SeqSrcF32{E, 0.0f, false}, kSeqNone, 0.0f, ssh, head,
-                                      kSeqHead);
+    // the sort room is free until the nucleus is collected: tile workspace
+    const SeqTiles tw1 = seq_tiles_at(sm_k0, static_cast<size_t>(sm_cap) * 16);
+    const SeqResult s1 =
+        seq_scan<NT>(V, SeqSrcF32{E, 0.0f, false}, kSeqNone, 0.0f, ssh, head, kSeqHead, tw1, 0);
     const float inv = __fdiv_rn(1.0f, s1.s);                            // :72, softmax.c:18
     int tok;
     if (!topp) {
       // generate.c:159-167: r = rng_float(), first i with r < cdf
       const float r = rng_next(rs);
       const SeqResult s2 =
-          seq_scan<NT>(V, SeqSrcF32{E, inv, true}, kSeqGT, r, ssh, head, kSeqHead);
+          seq_scan<NT>(V, SeqSrcF32{E, inv, true}, kSeqGT, r, ssh, head, kSeqHead, tw1, 0);
       tok = s2.hit >= 0 ? s2.hit : V - 1;
     } else {
       // the probability bound: bins from the top until a lower bound of the
@@ -1918,14 +1920,19 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
           vs = in1 ? g_v1 : g_v0;
         }
         // cumulative to the cutoff (:80-88) and the truncated sum (:91-93)
-        const SeqResult s3 = seq_scan<NT>(nf, SeqSrcKey{ks}, kSeqGE, P.p, ssh, head, kSeqHead);
+        // tile workspace: the sort room's pair that does not hold the result
+        const SeqTiles tw3 =
+            nf <= sm_cap ? seq_tiles_at(in1 ? sm_k0 : sm_k1, static_cast<size_t>(sm_cap) * 8)
+                         : seq_tiles_at(sm_k0, static_cast<size_t>(sm_cap) * 16);
+        const SeqResult s3 = seq_scan<NT>(nf, SeqSrcKey{ks}, kSeqGE, P.p, ssh, head, kSeqHead, tw3, 0);
         if (s3.hit < 0 && pmin > 0.0f) {  // not inside the prefix: take every entry
           pmin = 0.0f;
           continue;
         }
         cutoff = s3.hit >= 0 ? s3.hit + 1 : nf;
         const float r = __fmul_rn(rng_next(rs), s3.s);                  // :96
-        const SeqResult s4 = seq_scan<NT>(cutoff, SeqSrcKey{ks}, kSeqGT, r, ssh, head, kSeqHead);
+        // the same terms as s3 from term 0: its head and tile maps are reused
+        const SeqResult s4 = seq_scan<NT>(cutoff, SeqSrcKey{ks}, kSeqGT, r, ssh, head, kSeqHead, tw3, nf);
         pos = s4.hit >= 0 ? s4.hit : 0;                                 // :98-105
         break;
       }

@@ -338,14 +338,63 @@ struct SeqSrcKey {  // x_j = the float whose bits are ~k[j]
   }
 };
 
+constexpr int kSeqMinTiles = 16;
+
 struct SeqShared {
-  SeqMap map[32];  // one tile's map per warp of the current wave
+  double warp_tot[32];
+  __align__(16) unsigned char spare[kSeqMinTiles * 16];  // tile workspace when the caller has none
   float s;
   int done_pos;
-  int t0;
 };
 
 constexpr int kSeqTile = 256;  // terms per tile: 8 per lane of a warp
+
+// Per-tile workspace of seq_scan (shared memory, cap tiles; 16 B a tile):
+// the tile's term sum, the predicted grid of the running sum at its start,
+// and its composite map on that grid.
+struct SeqTiles {
+  float *tsum;
+  int *eu;
+  SeqMap *map;
+  int cap;
+};
+
+__device__ __forceinline__ SeqTiles seq_tiles_at(void *base, size_t bytes) {
+  SeqTiles w;
+  const int cap = static_cast<int>(bytes / 16);
+  w.map = reinterpret_cast<SeqMap *>(base);
+  w.tsum = reinterpret_cast<float *>(w.map + cap);
+  w.eu = reinterpret_cast<int *>(w.tsum + cap);
+  w.cap = cap;
+  return w;
+}
+
+// Exclusive block scan of doubles (NT threads).
+template <int NT>
+__device__ __forceinline__ double seq_block_exscan_d(double v, SeqShared &sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double w = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += w;
+  }
+  if (lane == 31) sh.warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    double t = lane < NT / 32 ? sh.warp_tot[lane] : 0.0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double w = __shfl_up_sync(0xFFFFFFFFu, t, o);
+      if (lane >= o) t += w;
+    }
+    if (lane < NT / 32) sh.warp_tot[lane] = t;
+  }
+  __syncthreads();
+  const double r = (warp ? sh.warp_tot[warp - 1] : 0.0) + incl - v;
+  __syncthreads();
+  return r;
+}
 
 // Replays s = fl(s + x_j) for j = 0..n-1 (x_j >= 0) starting from s = 0.
 // With a target, stops at the first j where s_j >= target (kSeqGE) or
@@ -354,22 +403,35 @@ constexpr int kSeqTile = 256;  // terms per tile: 8 per lane of a warp
 // The first head_cap terms (a multiple of 8; the running sum leaves its
 // binade most often early on, about once per doubling of the terms seen)
 // are added in order by one thread.  The rest is cut into tiles of 256
-// terms and walked a wave of NT/32 tiles at a time:
-//   every warp computes its tile's composite map on the grid of the sum at
-//   the wave's start (seq_warp_map) and loads the next wave's terms;
-//   warp 0 then applies the maps in order.  N only grows, so a tile leaves
-//   the binade, or meets the target, iff its end does: such a tile is
-//   replayed exactly by warp 0 (seq_tile_exact), and if the grid changed
-//   the wave ends after it (the remaining maps are on the old grid).
-// Two barriers per wave; sums leave their binade a handful of times after
-// the head, so nearly every tile costs one map and one integer add.
+// terms, with no barrier per tile:
+//   1. every warp sums its tiles' terms (float; an estimate only);
+//   2. a block scan of those sums, from the exact sum after the head,
+//      predicts the running sum at each tile's start, hence its grid;
+//   3. every warp computes its tiles' composite maps on the predicted
+//      grids (seq_warp_map);
+//   4. warp 0 walks the tiles in order: a tile whose predicted grid is the
+//      current one costs one integer add, since N only grows and a tile
+//      leaves the binade, or meets the target, iff its end does; any other
+//      tile (it leaves the binade, meets the target, or was predicted on
+//      another grid) is replayed exactly (seq_tile_exact).
+// The float sum differs from the exact one by far less than a binade, so
+// only tiles where the sum crosses a power of two miss their prediction.
+// With reuse_n > 0 (the n of the previous call, over the same terms from
+// the same term 0, with the same head_cap and tw; reuse_n >= n), the head's
+// terms and, when that call's tiles fitted tw in one segment, its maps are
+// reused: steps 1-3 are skipped and only the walk runs, with this call's
+// target.  A map is only used for a tile that lies wholly below n.
 template <int NT, typename Src>
-__device__ __noinline__ SeqResult seq_scan(int n, const Src src, int kind, float target, SeqShared &sh,
-                              float *head_buf, int head_cap) {
+__device__ __noinline__ SeqResult seq_scan(int n, const Src src, int kind, float target,
+                                           SeqShared &sh, float *head_buf, int head_cap,
+                                           SeqTiles tw, int reuse_n) {
   constexpr int NW = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tw.cap < kSeqMinTiles) tw = seq_tiles_at(sh.spare, sizeof sh.spare);
   const int K = n < head_cap ? n : head_cap;
-  for (int j = tid; j < K; j += NT) head_buf[j] = src.at(j);
+  bool reuse = reuse_n > 0;
+  if (!reuse)
+    for (int j = tid; j < K; j += NT) head_buf[j] = src.at(j);
   __syncthreads();
   if (tid == 0) {
     float s = 0.0f;
@@ -399,85 +461,107 @@ __device__ __noinline__ SeqResult seq_scan(int n, const Src src, int kind, float
   }
   __syncthreads();
   const int ntiles = (n - K + kSeqTile - 1) / kSeqTile;
-  auto load_tile = [&](int t, float(&dst)[8]) {
-    if (t < ntiles) {
-      src.load8(K + t * kSeqTile + lane * 8, n, dst);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; e++) dst[e] = 0.0f;
-    }
-  };
-  float x[8];
-  int t0 = 0;
-  if (ntiles > 0 && sh.done_pos < 0) load_tile(warp, x);
-  while (ntiles > 0) {
-    if (sh.done_pos >= 0 || t0 >= ntiles) break;
-    const float s0 = sh.s;
-    const bool finite = s0 <= 3.40282347e38f;
-    const int eu = seq_grid_exp(s0);
-    if (finite && t0 + warp < ntiles) {
-      const SeqMap f = seq_warp_map(x, eu);
-      if (lane == 0) sh.map[warp] = f;
-    }
-    float xn[8];
-    load_tile(t0 + NW + warp, xn);  // the next wave's terms, in flight during the walk
+  if (sh.done_pos >= 0 || ntiles == 0) {
+    SeqResult r{sh.s, sh.done_pos};
     __syncthreads();
+    return r;
+  }
+  if (reuse) {
+    const int Kp = reuse_n < head_cap ? reuse_n : head_cap;
+    if ((reuse_n - Kp + kSeqTile - 1) / kSeqTile > tw.cap) reuse = false;
+  }
+  for (int g0 = 0; g0 < ntiles; g0 += tw.cap) {
+    const int nt = min(tw.cap, ntiles - g0);
+    if (!reuse) {
+      // 1. tile sums
+      for (int t = warp; t < nt; t += NW) {
+        float x[8];
+        src.load8(K + (g0 + t) * kSeqTile + lane * 8, n, x);
+        float a = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) a += x[e];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+        if (lane == 0) tw.tsum[t] = a;
+      }
+      __syncthreads();
+      // 2. predicted grids: each thread a run of consecutive tiles
+      const int per = (nt + NT - 1) / NT;
+      const int r0 = min(nt, tid * per), r1 = min(nt, r0 + per);
+      double run = 0.0;
+      for (int t = r0; t < r1; t++) run += static_cast<double>(tw.tsum[t]);
+      double pre = static_cast<double>(sh.s) + seq_block_exscan_d<NT>(run, sh);
+      for (int t = r0; t < r1; t++) {
+        tw.eu[t] = seq_grid_exp(static_cast<float>(pre));
+        pre += static_cast<double>(tw.tsum[t]);
+      }
+      __syncthreads();
+      // 3. maps on the predicted grids
+      for (int t = warp; t < nt; t += NW) {
+        float x[8];
+        src.load8(K + (g0 + t) * kSeqTile + lane * 8, n, x);
+        const SeqMap f = seq_warp_map(x, tw.eu[t]);
+        if (lane == 0) tw.map[t] = f;
+      }
+      __syncthreads();
+    }
+    // 4. the walk
     if (warp == 0) {
-      float s = s0;
-      int done = -1, tnext = t0 + NW;
-      const int tend = min(t0 + NW, ntiles);
-      if (!finite) {
-        // NaN or +inf: every later sum is s
-        if (seq_meets(s, kind, target)) done = K + t0 * kSeqTile;
-        tnext = ntiles;
-      } else {
-        uint32_t N = seq_N(s0);
-        const uint32_t thrN = seq_thr(kind, target, eu);
-        bool exact = false;  // s is current (N is not)
-        for (int t = t0; t < tend; t++) {
-          const SeqMap f = sh.map[t - t0];
-          const uint32_t Nn = seq_apply(f, N);
+      float s = sh.s;
+      int done = -1;
+      int eu = seq_grid_exp(s);
+      uint32_t N = seq_N(s);
+      uint32_t thrN = seq_thr(kind, target, eu);
+      bool finite = s <= 3.40282347e38f;
+      bool cur = true;  // s matches (eu, N)
+      SeqMap f = tw.map[0];
+      int ef = tw.eu[0];
+      for (int t = 0; t < nt; t++) {
+        const int j0 = K + (g0 + t) * kSeqTile, j1 = min(n, j0 + kSeqTile);
+        const SeqMap fc = f;
+        const int ec = ef;
+        if (t + 1 < nt) {  // the next tile's map, in flight during this one
+          f = tw.map[t + 1];
+          ef = tw.eu[t + 1];
+        }
+        if (!finite) {  // NaN or +inf: every later sum is s
+          if (seq_meets(s, kind, target)) done = j0;
+          break;
+        }
+        if (ec == eu && (!reuse || j0 + kSeqTile <= n)) {
+          const uint32_t Nn = seq_apply(fc, N);
           if (Nn < kSeqLimit && Nn < thrN) {
             N = Nn;
+            cur = false;
             continue;
           }
-          // the tile leaves the binade or meets the target: replay it
-          const int j0 = K + t * kSeqTile, j1 = min(n, j0 + kSeqTile);
-          const SeqResult rt = seq_tile_exact(src, j0, j0, j1, seq_float(N, eu), kind, target);
-          s = rt.s;
-          exact = true;
-          if (rt.hit >= 0) {
-            done = rt.hit;
-            break;
-          }
-          if (!(s <= 3.40282347e38f) || seq_grid_exp(s) != eu) {
-            tnext = t + 1;  // the rest of the wave's maps are on the old grid
-            break;
-          }
-          N = seq_N(s);
-          exact = false;
         }
-        if (!exact) s = seq_float(N, eu);
+        if (!cur) s = seq_float(N, eu);
+        const SeqResult rt = seq_tile_exact(src, j0, j0, j1, s, kind, target);
+        s = rt.s;
+        cur = true;
+        if (rt.hit >= 0) {
+          done = rt.hit;
+          break;
+        }
+        finite = s <= 3.40282347e38f;
+        const int eun = seq_grid_exp(s);
+        if (eun != eu) {
+          eu = eun;
+          thrN = seq_thr(kind, target, eu);
+        }
+        N = seq_N(s);
       }
+      if (!cur) s = seq_float(N, eu);
       if (lane == 0) {
         sh.s = s;
         sh.done_pos = done;
-        sh.t0 = tnext;
       }
     }
     __syncthreads();
-    const int t0n = sh.t0;
-    if (t0n == t0 + NW) {
-#pragma unroll
-      for (int e = 0; e < 8; e++) x[e] = xn[e];
-    } else if (t0n < ntiles) {
-      load_tile(t0n + warp, x);
-    }
-    t0 = t0n;
+    if (sh.done_pos >= 0) break;
   }
-  SeqResult r;
-  r.s = sh.s;
-  r.hit = sh.done_pos;
+  SeqResult r{sh.s, sh.done_pos};
   __syncthreads();
   return r;
 }

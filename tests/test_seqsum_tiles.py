@@ -105,40 +105,79 @@ def seq_sum(xs, s=F32(0.0)):
     return out
 
 
-def tile_exact(xs, s):
+def tile_exact(xs, s, j0=0, kind=None, target=0.0):
     """Term-by-term replay inside one tile (the device does it with a warp
-    scan of the exact maps; each binade-leaving term is a real add)."""
-    for x in xs:
+    scan of the exact maps; each binade-leaving term is a real add).
+    Returns (s, first j meeting the target or -1)."""
+    for i, x in enumerate(xs):
         if not np.isfinite(s):
             s = F32(s + F32(x))
+        else:
+            eu = grid_exp(s)
+            n = apply(elem_exact(x, eu), seq_n(s))
+            s = F32(s + F32(x)) if n >= LIMIT else seq_float(n, eu)
+        if meets(s, kind, target):
+            return s, j0 + i
+    return s, -1
+
+
+def meets(s, kind, target):
+    return (kind == "ge" and s >= target) or (kind == "gt" and s > target)
+
+
+def thr_n(kind, target, eu):
+    if kind is None:
+        return 1 << 32
+    q = float(target) * 2.0 ** -eu
+    return max(0, int(np.ceil(q))) if kind == "ge" else max(0, int(np.floor(q)) + 1)
+
+
+def tile_walk(xs, head=1024, kind=None, target=0.0):
+    """seq_scan: the head in order; then tile sums, a prefix from the head's
+    exact sum that predicts each tile's grid, maps on the predicted grids,
+    and the walk (a tile whose prediction is the current grid costs one add
+    unless its end leaves the binade or meets the target; any other tile is
+    replayed exactly).  Returns (s, hit, stats)."""
+    s, hit = F32(0.0), -1
+    for j, x in enumerate(xs[:head]):
+        s = F32(s + F32(x))
+        if meets(s, kind, target):
+            return s, j, {"tiles": 0, "replayed": 0}
+    starts = list(range(head, len(xs), TILE))
+    tsum = [float(np.sum(xs[t:t + TILE], dtype=F32)) for t in starts]
+    pre = float(s) + np.concatenate([[0.0], np.cumsum(tsum)[:-1]]) if starts else []
+    pred = [grid_exp(F32(p)) for p in pre]
+    stats = {"tiles": len(starts), "replayed": 0}
+    for t, j0 in enumerate(starts):
+        tile = xs[j0:j0 + TILE]
+        if not np.isfinite(s):
+            if meets(s, kind, target):
+                return s, j0, stats
+            s = F32(s + F32(np.sum(tile)))  # stays NaN or inf
             continue
         eu = grid_exp(s)
-        n = apply(elem_exact(x, eu), seq_n(s))
-        s = F32(s + F32(x)) if n >= LIMIT else seq_float(n, eu)
-    return s
-
-
-def tile_walk(xs, head=1024):
-    """seq_scan without a target: the head in order, then tiles by maps."""
-    s = F32(0.0)
-    for x in xs[:head]:
-        s = F32(s + F32(x))
-    stats = {"tiles": 0, "replayed": 0}
-    for t0 in range(head, len(xs), TILE):
-        tile = xs[t0:t0 + TILE]
-        stats["tiles"] += 1
-        if np.isfinite(s):
-            eu = grid_exp(s)
+        if pred[t] == eu:
             f = (0, 0)
             for x in tile:
                 f = compose(f, elem_fast(x, eu) if eu >= -126 else elem_exact(x, eu))
             n = apply(f, seq_n(s))
-            if n < LIMIT:
+            if n < LIMIT and n < thr_n(kind, target, eu):
                 s = seq_float(n, eu)
                 continue
         stats["replayed"] += 1
-        s = tile_exact(tile, s)
-    return s, stats
+        s, hit = tile_exact(tile, s, j0, kind, target)
+        if hit >= 0:
+            return s, hit, stats
+    return s, -1, stats
+
+
+def first_hit(xs, kind, target):
+    s = F32(0.0)
+    for j, x in enumerate(xs):
+        s = F32(s + F32(x))
+        if meets(s, kind, target):
+            return s, j
+    return s, -1
 
 
 def test_fast_map_equals_exact_map_and_float_addition():
@@ -196,7 +235,7 @@ def test_tile_walk_equals_sequential_sum(kind):
     for n in (1000, 1024, 1300, 9000, 40000):
         xs = _seq(kind, rng, n)
         want = seq_sum(xs)[-1]
-        got, st = tile_walk(xs)
+        got, _, st = tile_walk(xs)
         assert got.view(np.uint32) == want.view(np.uint32), (kind, n, got, want)
         if n > 1024 + TILE:
             assert st["tiles"] > st["replayed"]
@@ -210,3 +249,20 @@ def test_tile_walk_nan_and_inf():
     assert np.isnan(tile_walk(xs)[0])
     xs = np.full(3000, F32(3e38))
     assert tile_walk(xs)[0] == np.inf
+
+
+@pytest.mark.parametrize("kind", ["exp", "ties", "sorted"])
+def test_tile_walk_first_hit(kind):
+    """Targets: the cutoff (s >= p), the draws (s > r); the hit and the sum
+    at the hit are the reference loop's."""
+    rng = np.random.default_rng(7 + len(kind))
+    for n in (5000, 30000):
+        xs = _seq(kind, rng, n)
+        total = float(seq_sum(xs)[-1])
+        for frac in (0.001, 0.3, 0.9, 0.999999, 1.0, 1.5):
+            for k in ("ge", "gt"):
+                target = F32(total * frac)
+                want_s, want_j = first_hit(xs, k, target)
+                got_s, got_j, _ = tile_walk(xs, kind=k, target=target)
+                assert got_j == want_j, (kind, n, frac, k)
+                assert got_s.view(np.uint32) == want_s.view(np.uint32)
