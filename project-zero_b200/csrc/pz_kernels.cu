@@ -1784,6 +1784,16 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
   uint32_t *g_k1 = A.sort_b + static_cast<size_t>(blockIdx.x) * A.sort_stride;
   uint32_t *g_v1 = g_k1 + A.sort_stride / 2;
   const int n_full = *A.n_full;
+  // the sort room is free until the nucleus is collected: the row's tile
+  // sums (from pass 1a) and the exact replay's tile workspace go there
+  static_assert(kSeqHead % kSeqTile == 0 && kSeqHead / kSeqTile <= 8, "head tiles");
+  const int n_rtiles = (A.V + kSeqTile - 1) / kSeqTile;
+  const size_t rt_bytes = (static_cast<size_t>(n_rtiles) * 4 + 15) / 16 * 16;
+  const bool row_tsum = rt_bytes + 16 * kSeqMinTiles <= static_cast<size_t>(sm_cap) * 16;
+  float *tsum_row = reinterpret_cast<float *>(sm_k0);
+  const SeqTiles tw1 =
+      row_tsum ? seq_tiles_at(smem + fixed + rt_bytes, static_cast<size_t>(sm_cap) * 16 - rt_bytes)
+               : seq_tiles_at(sm_k0, static_cast<size_t>(sm_cap) * 16);
 
   for (int w = blockIdx.x; w < n_full; w += gridDim.x) {
     const int row = A.full_rows[w];
@@ -1805,6 +1815,8 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
     if (hist_on)
       for (int i = tid; i < bm_words; i += NT) bitmap[i] = 0u;
     for (int i = tid; i < kEBins; i += NT) bins[i] = 0u;
+    if (row_tsum)
+      for (int i = tid; i < n_rtiles; i += NT) tsum_row[i] = 0.0f;
     __syncthreads();
     int nh = 0;
     if (hist_on) {
@@ -1833,17 +1845,27 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
     const bool topp = P.mode != kModeSoftmaxFull;
     const float thr = __fsub_rn(mx, 20.0f);                             // top_p.c:53
     // pass 1a: e values (stored) and the bins, the row read with 16-byte
-    // loads, no barriers
+    // loads, no barriers; with row_tsum, also each 256-term tile's sum of e
+    // values (float, in any order: the exact replay only uses it to predict
+    // the running sum's binade)
     {
-      auto elem = [&](int i, float x) {
+      // e_i (0 where the max-20 filter drops the value); cnt: counted in the bins
+      auto elem = [&](int i, float x, bool &cnt) -> float {
         if (hist_on && ((bitmap[i >> 5] >> (i & 31)) & 1u)) x = penalize(x, sorted_count(hl, nh, i), P);
         const float v = temper(x, P);
-        float e = 0.0f;
+        cnt = false;
         if (!topp || v >= thr) {                                         // top_p.c:58
-          e = cr_expf(__fsub_rn(v, mx));                                 // :59, softmax.c:13
-          if (topp) atomicAdd(&bins[ebin(e)], 1u);
+          cnt = topp;
+          return cr_expf(__fsub_rn(v, mx));                              // :59, softmax.c:13
         }
+        return 0.0f;
+      };
+      auto elem_store = [&](int i, float x) -> float {
+        bool cnt;
+        const float e = elem(i, x, cnt);
+        if (cnt) atomicAdd(&bins[ebin(e)], 1u);
         E[i] = e;
+        return e;
       };
       constexpr int VEC = Vec16<T>::N;
       const uintptr_t addr = reinterpret_cast<uintptr_t>(rowp);
@@ -1851,30 +1873,83 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
       if (lead > V) lead = V;
       const int nvec = (V - lead) / VEC;
       const int body_end = lead + nvec * VEC;
-      for (int i = tid; i < lead; i += NT) elem(i, load_scalar<T>(rowp, i));
-      for (int i = body_end + tid; i < V; i += NT) elem(i, load_scalar<T>(rowp, i));
+      for (int i = tid; i < lead; i += NT) {
+        const float e = elem_store(i, load_scalar<T>(rowp, i));
+        if (row_tsum) atomicAdd(&tsum_row[i >> 8], e);
+      }
+      for (int i = body_end + tid; i < V; i += NT) {
+        const float e = elem_store(i, load_scalar<T>(rowp, i));
+        if (row_tsum) atomicAdd(&tsum_row[i >> 8], e);
+      }
+      const bool vst = (lead & 3) == 0;  // E + lead + 4m is 16-byte aligned
       const T *body = rowp + lead;
-#pragma unroll 2
-      for (int q = tid; q < nvec; q += NT) {
-        float xv[VEC];
-        Vec16<T>::load(body, q, xv);
+      const int lane = tid & 31;
+      // U consecutive vectors per lane per trip: a warp's trip covers one
+      // 256-term tile (U = 1 for bf16, 2 for f32)
+      constexpr int U = 256 / (32 * VEC) > 0 ? 256 / (32 * VEC) : 1;
+      constexpr int SPAN = U * VEC;
+      const int nunit = (nvec + U - 1) / U;
+      constexpr int UNR = U == 1 ? 2 : 1;  // two vectors in flight per lane
+#pragma unroll UNR
+      for (int q0 = tid - lane; q0 < nunit; q0 += NT) {  // warp-uniform trips
+        const int qu = q0 + lane;
+        const int i0 = lead + qu * SPAN;
+        float vs = 0.0f;
 #pragma unroll
-        for (int w = 0; w < VEC; w++) elem(lead + q * VEC + w, xv[w]);
+        for (int u = 0; u < U; u++) {
+          const int q = qu * U + u;
+          if (q < nvec) {
+            float xv[VEC];
+            Vec16<T>::load(body, q, xv);
+            const int iv = i0 + u * VEC;
+#pragma unroll
+            for (int w = 0; w < VEC; w++) {
+              bool cnt;
+              xv[w] = elem(iv + w, xv[w], cnt);
+              if (cnt) atomicAdd(&bins[ebin(xv[w])], 1u);
+              vs += xv[w];
+            }
+            if (vst) {
+#pragma unroll
+              for (int w = 0; w < VEC; w += 4)
+                *reinterpret_cast<float4 *>(E + iv + w) = make_float4(xv[w], xv[w + 1], xv[w + 2], xv[w + 3]);
+            } else {
+#pragma unroll
+              for (int w = 0; w < VEC; w++) E[iv + w] = xv[w];
+            }
+          }
+        }
+        if (row_tsum) {
+          // the warp's vectors in one tile: one add per warp
+          const int t0w = __shfl_sync(0xFFFFFFFFu, i0, 0) >> 8;
+          const bool one = qu >= nunit || ((i0 >> 8) == t0w && ((i0 + SPAN - 1) >> 8) == t0w);
+          if (__all_sync(0xFFFFFFFFu, one)) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) vs += __shfl_xor_sync(0xFFFFFFFFu, vs, o);
+            if (lane == 0) atomicAdd(&tsum_row[t0w], vs);
+          } else if (qu < nunit) {
+            const int iend = min(i0 + SPAN, body_end);
+            if ((i0 >> 8) == ((iend - 1) >> 8)) {
+              atomicAdd(&tsum_row[i0 >> 8], vs);
+            } else {
+              for (int i = i0; i < iend; i++) atomicAdd(&tsum_row[i >> 8], E[i]);
+            }
+          }
+        }
       }
     }
     __syncthreads();
     // pass 1b: the exact normaliser over the stored e values
-    // the sort room is free until the nucleus is collected: tile workspace
-    const SeqTiles tw1 = seq_tiles_at(sm_k0, static_cast<size_t>(sm_cap) * 16);
-    const SeqResult s1 =
-        seq_scan<NT>(V, SeqSrcF32{E, 0.0f, false}, kSeqNone, 0.0f, ssh, head, kSeqHead, tw1, 0);
+    const SeqResult s1 = seq_scan<NT>(V, SeqSrcF32{E, 0.0f, false}, kSeqNone, 0.0f, ssh, head,
+                                      kSeqHead, tw1, 0, row_tsum ? tsum_row : nullptr, 1.0f);
     const float inv = __fdiv_rn(1.0f, s1.s);                            // :72, softmax.c:18
     int tok;
     if (!topp) {
       // generate.c:159-167: r = rng_float(), first i with r < cdf
       const float r = rng_next(rs);
       const SeqResult s2 =
-          seq_scan<NT>(V, SeqSrcF32{E, inv, true}, kSeqGT, r, ssh, head, kSeqHead, tw1, 0);
+          seq_scan<NT>(V, SeqSrcF32{E, inv, true}, kSeqGT, r, ssh, head, kSeqHead, tw1, 0,
+                       row_tsum ? tsum_row : nullptr, inv);
       tok = s2.hit >= 0 ? s2.hit : V - 1;
     } else {
       // the probability bound: bins from the top until a lower bound of the
@@ -1924,7 +1999,8 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
         const SeqTiles tw3 =
             nf <= sm_cap ? seq_tiles_at(in1 ? sm_k0 : sm_k1, static_cast<size_t>(sm_cap) * 8)
                          : seq_tiles_at(sm_k0, static_cast<size_t>(sm_cap) * 16);
-        const SeqResult s3 = seq_scan<NT>(nf, SeqSrcKey{ks}, kSeqGE, P.p, ssh, head, kSeqHead, tw3, 0);
+        const SeqResult s3 =
+            seq_scan<NT>(nf, SeqSrcKey{ks}, kSeqGE, P.p, ssh, head, kSeqHead, tw3, 0, nullptr, 1.0f);
         if (s3.hit < 0 && pmin > 0.0f) {  // not inside the prefix: take every entry
           pmin = 0.0f;
           continue;
@@ -1932,7 +2008,8 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
         cutoff = s3.hit >= 0 ? s3.hit + 1 : nf;
         const float r = __fmul_rn(rng_next(rs), s3.s);                  // :96
         // the same terms as s3 from term 0: its head and tile maps are reused
-        const SeqResult s4 = seq_scan<NT>(cutoff, SeqSrcKey{ks}, kSeqGT, r, ssh, head, kSeqHead, tw3, nf);
+        const SeqResult s4 =
+            seq_scan<NT>(cutoff, SeqSrcKey{ks}, kSeqGT, r, ssh, head, kSeqHead, tw3, nf, nullptr, 1.0f);
         pos = s4.hit >= 0 ? s4.hit : 0;                                 // :98-105
         break;
       }

@@ -234,13 +234,19 @@ __device__ __noinline__ SeqResult seq_tile_exact(const Src src, int j0, int star
     const int eu = seq_grid_exp(s);
     const uint32_t N0 = seq_N(s);
     const uint32_t thrN = seq_thr(kind, target, eu);
-    SeqMap F = seq_identity();
+    // the lane's element maps on this grid (identity outside [start, j1))
+    SeqMap m[8];
+    const float sc = seq_scale(eu < -126 ? -126 : eu);
 #pragma unroll
     for (int e = 0; e < 8; e++) {
       const int j = j0 + 8 * lane + e;
-      if (j >= start && j < j1) F = seq_compose(F, seq_elem(x[e], eu));
+      bool tie;
+      m[e] = (j < start || j >= j1) ? seq_identity()
+             : (eu >= -126 ? seq_elem_fast(x[e], sc, tie) : seq_elem(x[e], eu));
     }
-    SeqMap incl = F;
+    SeqMap incl = m[0];
+#pragma unroll
+    for (int e = 1; e < 8; e++) incl = seq_compose(incl, m[e]);
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       SeqMap w;
@@ -261,7 +267,7 @@ __device__ __noinline__ SeqResult seq_tile_exact(const Src src, int j0, int star
     for (int e = 0; e < 8; e++) {
       const int j = j0 + 8 * lane + e;
       if (j >= start && j < j1 && ev == 0x7FFFFFFF) {
-        const uint32_t Nn = seq_apply(seq_elem(x[e], eu), N);
+        const uint32_t Nn = seq_apply(m[e], N);
         if (Nn >= kSeqLimit) {
           ev = j;
           cross = true;
@@ -342,6 +348,7 @@ constexpr int kSeqMinTiles = 16;
 
 struct SeqShared {
   double warp_tot[32];
+  float head_tsum[8];  // head tiles' sums (head_cap <= 8 tiles)
   __align__(16) unsigned char spare[kSeqMinTiles * 16];  // tile workspace when the caller has none
   float s;
   int done_pos;
@@ -396,19 +403,51 @@ __device__ __forceinline__ double seq_block_exscan_d(double v, SeqShared &sh) {
   return r;
 }
 
+// The head: terms 0..K-1 of head_buf added in order by the calling thread;
+// returns the first j whose sum meets the target, or -1 (then s is the sum
+// of all K terms).  8 terms a round: the round's loads first, then the
+// chain of adds (padding terms are 0: adding 0 leaves s as it is), then the
+// round's prefixes tested against the target off the chain.
+__device__ __forceinline__ int seq_head(const float *head_buf, int K, int kind, float target,
+                                        float &s_out) {
+  float s = 0.0f;
+  int done = -1;
+  for (int j0 = 0; j0 < K && done < 0; j0 += 8) {
+    float h[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) h[e] = j0 + e < K ? head_buf[j0 + e] : 0.0f;
+    float ps[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      s = __fadd_rn(s, h[e]);
+      ps[e] = s;
+    }
+    if (kind != kSeqNone) {
+#pragma unroll
+      for (int e = 7; e >= 0; e--)
+        if (j0 + e < K && seq_meets(ps[e], kind, target)) done = j0 + e;
+      if (done >= 0) s = ps[done - j0];
+    }
+  }
+  s_out = s;
+  return done;
+}
+
 // Replays s = fl(s + x_j) for j = 0..n-1 (x_j >= 0) starting from s = 0.
 // With a target, stops at the first j where s_j >= target (kSeqGE) or
 // s_j > target (kSeqGT).  Block-wide call (NT threads, uniform arguments).
 //
-// The first head_cap terms (a multiple of 8; the running sum leaves its
-// binade most often early on, about once per doubling of the terms seen)
-// are added in order by one thread.  The rest is cut into tiles of 256
-// terms, with no barrier per tile:
-//   1. every warp sums its tiles' terms (float; an estimate only);
-//   2. a block scan of those sums, from the exact sum after the head,
-//      predicts the running sum at each tile's start, hence its grid;
-//   3. every warp computes its tiles' composite maps on the predicted
-//      grids (seq_warp_map);
+// The first head_cap terms (a multiple of kSeqTile; the running sum leaves
+// its binade most often early on, about once per doubling of the terms
+// seen) are added in order by one thread.  The rest is cut into tiles of
+// 256 terms, with no barrier per tile:
+//   1. tile sums (float; estimates only): computed by the warps, or given
+//      by the caller (tsum_in[u] * tsum_scale for the tile of terms
+//      256u .. 256u + 255, head tiles included);
+//   2. a block scan of those sums predicts the running sum at each tile's
+//      start, hence its grid;
+//   3. every warp computes its tiles' composite maps on the predicted grids
+//      (seq_warp_map) while one thread of warp 0 runs the head;
 //   4. warp 0 walks the tiles in order: a tile whose predicted grid is the
 //      current one costs one integer add, since N only grows and a tile
 //      leaves the binade, or meets the target, iff its end does; any other
@@ -416,127 +455,166 @@ __device__ __forceinline__ double seq_block_exscan_d(double v, SeqShared &sh) {
 //      another grid) is replayed exactly (seq_tile_exact).
 // The float sum differs from the exact one by far less than a binade, so
 // only tiles where the sum crosses a power of two miss their prediction.
+// tw holds the tiles' grids and maps; when the tiles outnumber it they are
+// walked in segments, each predicted from the exact sum at its start.
 // With reuse_n > 0 (the n of the previous call, over the same terms from
 // the same term 0, with the same head_cap and tw; reuse_n >= n), the head's
 // terms and, when that call's tiles fitted tw in one segment, its maps are
-// reused: steps 1-3 are skipped and only the walk runs, with this call's
-// target.  A map is only used for a tile that lies wholly below n.
+// reused: steps 1-3 are skipped and only the head and the walk run, with
+// this call's target.  A map is only used for a tile that lies wholly
+// below n.
 template <int NT, typename Src>
 __device__ __noinline__ SeqResult seq_scan(int n, const Src src, int kind, float target,
                                            SeqShared &sh, float *head_buf, int head_cap,
-                                           SeqTiles tw, int reuse_n) {
+                                           SeqTiles tw, int reuse_n, const float *tsum_in,
+                                           float tsum_scale) {
   constexpr int NW = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tw.cap < kSeqMinTiles) tw = seq_tiles_at(sh.spare, sizeof sh.spare);
   const int K = n < head_cap ? n : head_cap;
-  bool reuse = reuse_n > 0;
-  if (!reuse)
-    for (int j = tid; j < K; j += NT) head_buf[j] = src.at(j);
-  __syncthreads();
-  if (tid == 0) {
-    float s = 0.0f;
-    int done = -1;
-    // 8 terms a round: the round's loads first, then the chain of adds
-    // (padding terms are 0: adding 0 leaves s as it is), then the round's
-    // prefixes tested against the target off the chain
-    for (int j0 = 0; j0 < K && done < 0; j0 += 8) {
-      float h[8];
-#pragma unroll
-      for (int e = 0; e < 8; e++) h[e] = j0 + e < K ? head_buf[j0 + e] : 0.0f;
-      float ps[8];
-#pragma unroll
-      for (int e = 0; e < 8; e++) {
-        s = __fadd_rn(s, h[e]);
-        ps[e] = s;
-      }
-      if (kind != kSeqNone) {
-#pragma unroll
-        for (int e = 7; e >= 0; e--)
-          if (j0 + e < K && seq_meets(ps[e], kind, target)) done = j0 + e;
-        if (done >= 0) s = ps[done - j0];
-      }
-    }
-    sh.s = s;
-    sh.done_pos = done;
-  }
-  __syncthreads();
+  const int Kt = K / kSeqTile;  // head tiles (all full when there are walk tiles)
   const int ntiles = (n - K + kSeqTile - 1) / kSeqTile;
-  if (sh.done_pos >= 0 || ntiles == 0) {
-    SeqResult r{sh.s, sh.done_pos};
-    __syncthreads();
-    return r;
-  }
+  bool reuse = reuse_n > 0;
   if (reuse) {
     const int Kp = reuse_n < head_cap ? reuse_n : head_cap;
     if ((reuse_n - Kp + kSeqTile - 1) / kSeqTile > tw.cap) reuse = false;
   }
+  if (ntiles == 0 || reuse) {
+    if (reuse_n == 0)
+      for (int j = tid; j < K; j += NT) head_buf[j] = src.at(j);
+    __syncthreads();
+    if (tid == 0) sh.done_pos = seq_head(head_buf, K, kind, target, sh.s);
+    __syncthreads();
+    if (ntiles == 0 || sh.done_pos >= 0) {
+      SeqResult r{sh.s, sh.done_pos};
+      __syncthreads();
+      return r;
+    }
+  }
   for (int g0 = 0; g0 < ntiles; g0 += tw.cap) {
     const int nt = min(tw.cap, ntiles - g0);
     if (!reuse) {
-      // 1. tile sums
-      for (int t = warp; t < nt; t += NW) {
-        float x[8];
-        src.load8(K + (g0 + t) * kSeqTile + lane * 8, n, x);
-        float a = 0.0f;
+      const bool first = g0 == 0;
+      const int hk = first ? Kt : 0;  // head tiles summed in this segment
+      // 1. tile sums; the first segment also fills head_buf
+      if (tsum_in == nullptr) {
+        for (int u = warp; u < hk + nt; u += NW) {
+          const int j0 = u < hk ? u * kSeqTile : K + (g0 + u - hk) * kSeqTile;
+          float x[8];
+          src.load8(j0 + lane * 8, n, x);
+          float a = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 8; e++) a += x[e];
+          for (int e = 0; e < 8; e++) a += x[e];
+          if (u < hk) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
-        if (lane == 0) tw.tsum[t] = a;
+            for (int e = 0; e < 8; e++) head_buf[j0 + lane * 8 + e] = x[e];
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+          if (lane == 0) {
+            if (u < hk)
+              sh.head_tsum[u] = a;
+            else
+              tw.tsum[u - hk] = a;
+          }
+        }
+      } else {
+        if (first)
+          for (int j = tid; j < K; j += NT) head_buf[j] = src.at(j);
+        for (int u = tid; u < hk + nt; u += NT) {
+          const float a = __fmul_rn(tsum_in[u < hk ? u : Kt + g0 + u - hk], tsum_scale);
+          if (u < hk)
+            sh.head_tsum[u] = a;
+          else
+            tw.tsum[u - hk] = a;
+        }
       }
       __syncthreads();
       // 2. predicted grids: each thread a run of consecutive tiles
+      double base = 0.0;
+      if (first) {
+        for (int u = 0; u < hk; u++) base += static_cast<double>(sh.head_tsum[u]);
+      } else {
+        base = static_cast<double>(sh.s);
+      }
       const int per = (nt + NT - 1) / NT;
       const int r0 = min(nt, tid * per), r1 = min(nt, r0 + per);
       double run = 0.0;
       for (int t = r0; t < r1; t++) run += static_cast<double>(tw.tsum[t]);
-      double pre = static_cast<double>(sh.s) + seq_block_exscan_d<NT>(run, sh);
+      double pre = base + seq_block_exscan_d<NT>(run, sh);
       for (int t = r0; t < r1; t++) {
         tw.eu[t] = seq_grid_exp(static_cast<float>(pre));
         pre += static_cast<double>(tw.tsum[t]);
       }
       __syncthreads();
-      // 3. maps on the predicted grids
-      for (int t = warp; t < nt; t += NW) {
-        float x[8];
-        src.load8(K + (g0 + t) * kSeqTile + lane * 8, n, x);
-        const SeqMap f = seq_warp_map(x, tw.eu[t]);
-        if (lane == 0) tw.map[t] = f;
+      // 3. maps on the predicted grids; in the first segment warp 0 runs
+      // the head meanwhile
+      if (first && warp == 0) {
+        if (lane == 0) sh.done_pos = seq_head(head_buf, K, kind, target, sh.s);
+      } else {
+        const int w0 = first ? warp - 1 : warp, ws = first ? NW - 1 : NW;
+        for (int t = w0; t < nt; t += ws) {
+          float x[8];
+          src.load8(K + (g0 + t) * kSeqTile + lane * 8, n, x);
+          const SeqMap f = seq_warp_map(x, tw.eu[t]);
+          if (lane == 0) tw.map[t] = f;
+        }
       }
       __syncthreads();
+      if (first && sh.done_pos >= 0) break;
     }
-    // 4. the walk
+    // 4. the walk, 32 tiles a step: lane l takes tile t0 + l; an inclusive
+    // warp scan of the maps gives N after every tile; the first tile that
+    // is not a plain add (predicted on another grid, a partial tile under
+    // reuse, or N at its end leaves the binade or meets the target) is
+    // replayed exactly and the next step starts after it
     if (warp == 0) {
       float s = sh.s;
       int done = -1;
       int eu = seq_grid_exp(s);
       uint32_t N = seq_N(s);
       uint32_t thrN = seq_thr(kind, target, eu);
-      bool finite = s <= 3.40282347e38f;
       bool cur = true;  // s matches (eu, N)
-      SeqMap f = tw.map[0];
-      int ef = tw.eu[0];
-      for (int t = 0; t < nt; t++) {
-        const int j0 = K + (g0 + t) * kSeqTile, j1 = min(n, j0 + kSeqTile);
-        const SeqMap fc = f;
-        const int ec = ef;
-        if (t + 1 < nt) {  // the next tile's map, in flight during this one
-          f = tw.map[t + 1];
-          ef = tw.eu[t + 1];
-        }
-        if (!finite) {  // NaN or +inf: every later sum is s
-          if (seq_meets(s, kind, target)) done = j0;
+      int t0 = 0;
+      while (t0 < nt) {
+        if (!(s <= 3.40282347e38f)) {  // NaN or +inf: every later sum is s
+          if (seq_meets(s, kind, target)) done = K + (g0 + t0) * kSeqTile;
           break;
         }
-        if (ec == eu && (!reuse || j0 + kSeqTile <= n)) {
-          const uint32_t Nn = seq_apply(fc, N);
-          if (Nn < kSeqLimit && Nn < thrN) {
-            N = Nn;
-            cur = false;
-            continue;
-          }
+        const int t = t0 + lane;
+        const bool valid = t < nt;
+        SeqMap f = seq_identity();
+        bool ok = false;
+        if (valid) {
+          f = tw.map[t];
+          ok = tw.eu[t] == eu && (!reuse || K + (g0 + t + 1) * kSeqTile <= n);
+        }
+        SeqMap incl = f;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          SeqMap w;
+          w.e = __shfl_up_sync(0xFFFFFFFFu, incl.e, o);
+          w.o = __shfl_up_sync(0xFFFFFFFFu, incl.o, o);
+          if (lane >= o) incl = seq_compose(w, incl);
+        }
+        const uint32_t Na = seq_apply(incl, N);
+        const bool bad = valid && (!ok || Na >= kSeqLimit || Na >= thrN);
+        const unsigned bal = __ballot_sync(0xFFFFFFFFu, bad);
+        if (bal == 0u) {
+          const int last = min(31, nt - 1 - t0);
+          N = __shfl_sync(0xFFFFFFFFu, Na, last);
+          cur = false;
+          t0 += 32;
+          continue;
+        }
+        const int b = __ffs(bal) - 1;
+        const uint32_t Nb = __shfl_sync(0xFFFFFFFFu, Na, b > 0 ? b - 1 : 0);
+        if (b > 0) {
+          N = Nb;
+          cur = false;
         }
         if (!cur) s = seq_float(N, eu);
+        const int j0 = K + (g0 + t0 + b) * kSeqTile, j1 = min(n, j0 + kSeqTile);
         const SeqResult rt = seq_tile_exact(src, j0, j0, j1, s, kind, target);
         s = rt.s;
         cur = true;
@@ -544,13 +622,13 @@ __device__ __noinline__ SeqResult seq_scan(int n, const Src src, int kind, float
           done = rt.hit;
           break;
         }
-        finite = s <= 3.40282347e38f;
         const int eun = seq_grid_exp(s);
         if (eun != eu) {
           eu = eun;
           thrN = seq_thr(kind, target, eu);
         }
         N = seq_N(s);
+        t0 += b + 1;
       }
       if (!cur) s = seq_float(N, eu);
       if (lane == 0) {
