@@ -1591,8 +1591,8 @@ __device__ __forceinline__ float ebin_low(int b) {
 }
 
 __host__ __device__ size_t full_smem_fixed(int V, int hcap) {
-  const size_t bm_words = static_cast<size_t>(V) / 32 + 2;
-  return sizeof(uint32_t) * bm_words + sizeof(int32_t) * static_cast<size_t>(hcap) +
+  (void)V;
+  return sizeof(int32_t) * static_cast<size_t>(hcap) +
          sizeof(uint32_t) * (kFullThreads / 32) * 256 + sizeof(uint32_t) * 256 * 2 +
          sizeof(uint32_t) * kEBins + sizeof(float) * kSeqHead;
 }
@@ -1765,9 +1765,7 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
   __shared__ int s_nh, s_flag;
   __shared__ float s_pmin;
   const int tid = threadIdx.x;
-  const int bm_words = A.V / 32 + 2;
-  uint32_t *bitmap = reinterpret_cast<uint32_t *>(smem);
-  int32_t *hl = reinterpret_cast<int32_t *>(bitmap + bm_words);
+  int32_t *hl = reinterpret_cast<int32_t *>(smem);
   uint32_t *whist = reinterpret_cast<uint32_t *>(hl + A.hcap);
   uint32_t *tot = whist + (NT / 32) * 256;
   uint32_t *bins = tot + 256 * 2;
@@ -1812,8 +1810,6 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
     }
     const bool hist_on = H > 0 && H <= A.hcap;
     if (tid == 0) s_nh = 0;
-    if (hist_on)
-      for (int i = tid; i < bm_words; i += NT) bitmap[i] = 0u;
     for (int i = tid; i < kEBins; i += NT) bins[i] = 0u;
     if (row_tsum)
       for (int i = tid; i < n_rtiles; i += NT) tsum_row[i] = 0.0f;
@@ -1822,10 +1818,7 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
     if (hist_on) {
       for (int j = tid; j < H; j += NT) {
         const int t = hrow[j];
-        if (t >= 0 && t < V) {
-          hl[atomicAdd(&s_nh, 1)] = t;
-          atomicOr(&bitmap[t >> 5], 1u << (t & 31));
-        }
+        if (t >= 0 && t < V) hl[atomicAdd(&s_nh, 1)] = t;
       }
       __syncthreads();
       nh = s_nh;
@@ -1834,12 +1827,6 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
       for (int i = nh + tid; i < np2; i += NT) hl[i] = INT_MAX;
       block_sort_asc_i32<NT>(hl, np2);
     }
-    auto vof = [&](int i) -> float {
-      float x = load_scalar<T>(rowp, i);
-      if (hist_on && ((bitmap[i >> 5] >> (i & 31)) & 1u))
-        x = penalize(x, sorted_count(hl, nh, i), P);
-      return temper(x, P);
-    };
     const float mx = key_val(A.row_best[row]);
     unsigned long long rs = A.rng[row];
     const bool topp = P.mode != kModeSoftmaxFull;
@@ -1847,11 +1834,13 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
     // pass 1a: e values (stored) and the bins, the row read with 16-byte
     // loads, no barriers; with row_tsum, also each 256-term tile's sum of e
     // values (float, in any order: the exact replay only uses it to predict
-    // the running sum's binade)
+    // the running sum's binade).  History ids are taken unpenalised here and
+    // corrected in pass 1a' (a few thousand ids against ~10^5 values: the
+    // main pass carries no lookup).
     {
       // e_i (0 where the max-20 filter drops the value); cnt: counted in the bins
       auto elem = [&](int i, float x, bool &cnt) -> float {
-        if (hist_on && ((bitmap[i >> 5] >> (i & 31)) & 1u)) x = penalize(x, sorted_count(hl, nh, i), P);
+        (void)i;
         const float v = temper(x, P);
         cnt = false;
         if (!topp || v >= thr) {                                         // top_p.c:58
@@ -1939,6 +1928,31 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
       }
     }
     __syncthreads();
+    // pass 1a': each distinct history id's e value with its penalty
+    // (penalize, with the id's count in the history), replacing the
+    // unpenalised one: the bins and the tile sums move with it
+    if (hist_on) {
+      auto e_of = [&](float x, bool &cnt) -> float {
+        const float v = temper(x, P);
+        cnt = topp && v >= thr;
+        return (!topp || v >= thr) ? cr_expf(__fsub_rn(v, mx)) : 0.0f;  // top_p.c:58-59
+      };
+      for (int j = tid; j < nh; j += NT) {
+        const int t = hl[j];
+        if (j > 0 && hl[j - 1] == t) continue;  // the id's first place only
+        int c = 1;
+        while (j + c < nh && hl[j + c] == t) c++;
+        const float x = load_scalar<T>(rowp, t);
+        bool c0, c1;
+        const float e0 = e_of(x, c0);
+        const float e1 = e_of(penalize(x, c, P), c1);
+        E[t] = e1;
+        if (c0) atomicSub(&bins[ebin(e0)], 1u);
+        if (c1) atomicAdd(&bins[ebin(e1)], 1u);
+        if (row_tsum) atomicAdd(&tsum_row[t >> 8], e1 - e0);
+      }
+      __syncthreads();
+    }
     // pass 1b: the exact normaliser over the stored e values
     const SeqResult s1 = seq_scan<NT>(V, SeqSrcF32{E, 0.0f, false}, kSeqNone, 0.0f, ssh, head,
                                       kSeqHead, tw1, 0, row_tsum ? tsum_row : nullptr, 1.0f);
