@@ -1620,13 +1620,13 @@ size_t full_smem_bytes(int V, int hcap) {
 template <int NT>
 __device__ __noinline__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32_t *k1,
                                  uint32_t *v1, int n, uint32_t *whist,
-                                 uint32_t *tot, int *s_flag) {
+                                 uint32_t *tot, int *s_flag, int shift0) {
   constexpr int NW = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int seg = (n + NW - 1) / NW;
   const int s0 = min(n, warp * seg), s1 = min(n, s0 + seg);
   bool in1 = false;
-  for (int shift = 0; shift < 32; shift += 8) {
+  for (int shift = shift0; shift < 32; shift += 8) {
     uint32_t *ki = in1 ? k1 : k0, *vi = in1 ? v1 : v0;
     uint32_t *ko = in1 ? k0 : k1, *vo = in1 ? v0 : v1;
     for (int i = tid; i < NW * 256; i += NT) whist[i] = 0u;
@@ -1705,55 +1705,144 @@ __device__ __noinline__ bool block_radix_sort(uint32_t *k0, uint32_t *v0, uint32
   return in1;
 }
 
-// Collects, in index order, the entries i < V with e[i] > 0 and
-// prob = fl(e[i] * inv) >= pmin as (~prob bits, i) into (ko, vo); returns
-// their number.  Block-wide; e is 16-byte aligned and readable up to V
-// rounded up to a multiple of 8.
+// Collects the entries i < V with e[i] > 0 and prob = fl(e[i] * inv) >= pmin
+// as (~prob bits, i), with no block barrier per chunk: warp w scans the terms
+// [w * span, (w + 1) * span) (span = collect_span(V)) in index order and
+// writes its entries to ko/vo from place w * span on; seg_n[w] = their
+// number.  The warps' segments in warp order are the index order.  Also
+// counts each warp's keys by their low byte into whist[w * 256 + d] (the
+// first radix pass's histogram).  Block-wide; e is 16-byte aligned and
+// ko/vo hold V entries.  Returns the total.
 template <int NT>
-__device__ int collect_prefix(const float *e, int V, float inv, float pmin, uint32_t *ko, uint32_t *vo,
-                              int *red) {
-  constexpr int PT = 8;
-  int nf = 0;
-  float4 a, b, an, bn;
-  auto fetch = [&](int c, float4 &x0, float4 &x1) {
-    const int i = c + threadIdx.x * PT;
-    if (i < V) {
-      x0 = *reinterpret_cast<const float4 *>(e + i);
-      x1 = *reinterpret_cast<const float4 *>(e + i + 4);
+__host__ __device__ inline int collect_span(int V) {
+  return ((V + NT / 32 - 1) / (NT / 32) + 255) / 256 * 256;
+}
+
+template <int NT>
+__device__ __noinline__ int collect_segments(const float *e, int V, float inv, float pmin, uint32_t *ko,
+                                             uint32_t *vo, int *seg_n, uint32_t *whist) {
+  constexpr int NW = NT / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < NW * 256; i += NT) whist[i] = 0u;
+  __syncthreads();
+  const int span = collect_span<NT>(V);
+  const int a = min(V, warp * span), b = min(V, a + span);
+  uint32_t *wh = whist + warp * 256;
+  int cnt = 0;
+  float x[8], xn[8];
+  auto fetch = [&](int j, float(&d)[8]) {
+    if (j + 8 <= b) {
+      const float4 p = *reinterpret_cast<const float4 *>(e + j);
+      const float4 q = *reinterpret_cast<const float4 *>(e + j + 4);
+      d[0] = p.x; d[1] = p.y; d[2] = p.z; d[3] = p.w;
+      d[4] = q.x; d[5] = q.y; d[6] = q.z; d[7] = q.w;
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; u++) d[u] = j + u < b ? e[j + u] : 0.0f;
     }
   };
-  fetch(0, a, b);
-  for (int c0 = 0; c0 < V; c0 += NT * PT) {
-    if (c0 + NT * PT < V) fetch(c0 + NT * PT, an, bn);
-    const float ev[PT] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    const int i0 = c0 + threadIdx.x * PT;
+  if (a < b) fetch(a + lane * 8, x);
+  for (int j0 = a; j0 < b; j0 += 256) {
+    if (j0 + 256 < b) fetch(j0 + 256 + lane * 8, xn);  // in flight during this group
+    const int i0 = j0 + lane * 8;
     uint32_t keep = 0;
-    float pv[PT];
 #pragma unroll
-    for (int q = 0; q < PT; q++) {
-      pv[q] = 0.0f;
-      if (i0 + q < V && ev[q] > 0.0f) {
-        pv[q] = __fmul_rn(ev[q], inv);                                  // top_p.c:73-74
-        if (pv[q] >= pmin) keep |= 1u << q;
+    for (int u = 0; u < 8; u++) {
+      if (i0 + u < b && x[u] > 0.0f) {
+        x[u] = __fmul_rn(x[u], inv);                                    // top_p.c:73-74
+        if (x[u] >= pmin) keep |= 1u << u;
       }
     }
-    int total;
-    int pos = nf + block_exscan_int<NT>(__popc(keep), total, red);
+    const int c = __popc(keep);
+    int incl = c;
 #pragma unroll
-    for (int q = 0; q < PT; q++) {
-      if ((keep >> q) & 1u) {
-        ko[pos] = ~__float_as_uint(pv[q]);
-        vo[pos] = static_cast<uint32_t>(i0 + q);
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    int pos = a + cnt + incl - c;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      if ((keep >> u) & 1u) {
+        const uint32_t key = ~__float_as_uint(x[u]);
+        ko[pos] = key;
+        vo[pos] = static_cast<uint32_t>(i0 + u);
+        atomicAdd(&wh[key & 255u], 1u);
         pos++;
       }
     }
-    nf += total;
-    a = an;
-    b = bn;
+    cnt += __shfl_sync(0xFFFFFFFFu, incl, 31);
+#pragma unroll
+    for (int u = 0; u < 8; u++) x[u] = xn[u];
+  }
+  if (lane == 0) seg_n[warp] = cnt;
+  __threadfence_block();
+  __syncthreads();
+  int tot = 0;
+  for (int w = 0; w < NW; w++) tot += seg_n[w];
+  return tot;
+}
+
+// The first (low-byte) pass of block_radix_sort over collect_segments'
+// output: warp w's input is its segment (ks/vs from w * span, seg_n[w]
+// entries), whist holds the warps' low-byte counts; the n entries go to
+// ko/vo in order, stably.
+template <int NT>
+__device__ __noinline__ void radix_first_pass(const uint32_t *ks, const uint32_t *vs, const int *seg_n,
+                                              int span, uint32_t *ko, uint32_t *vo, uint32_t *whist,
+                                              uint32_t *tot) {
+  constexpr int NW = NT / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < 256) {
+    uint32_t run = 0;
+    for (int w = 0; w < NW; w++) {
+      const uint32_t c = whist[w * 256 + tid];
+      whist[w * 256 + tid] = run;
+      run += c;
+    }
+    tot[tid] = run;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t run = 0;
+    for (int d = 0; d < 256; d++) {
+      const uint32_t c = tot[d];
+      tot[d] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  if (tid < 256)
+    for (int w = 0; w < NW; w++) whist[w * 256 + tid] += tot[tid];
+  __syncthreads();
+  const int s0 = warp * span, s1 = s0 + seg_n[warp];
+  constexpr int RU = 8;
+  for (int j0 = s0; j0 < s1; j0 += 32 * RU) {
+    uint32_t key[RU], val[RU];
+#pragma unroll
+    for (int u = 0; u < RU; u++) {
+      const int j = j0 + u * 32 + lane;
+      key[u] = j < s1 ? ks[j] : 0u;
+      val[u] = j < s1 ? vs[j] : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < RU; u++) {
+      const int j = j0 + u * 32 + lane;
+      const bool act = j < s1;
+      const uint32_t d = act ? (key[u] & 255u) : (256u + lane);
+      const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
+      if (act) {
+        const uint32_t pos = whist[warp * 256 + d] + __popc(peers & lanemask_lt());
+        ko[pos] = key[u];
+        vo[pos] = val[u];
+      }
+      __syncwarp();
+      if (act && lane == __ffs(peers) - 1) whist[warp * 256 + d] += __popc(peers);
+      __syncwarp();
+    }
   }
   __threadfence_block();
   __syncthreads();
-  return nf;
 }
 
 template <typename T>
@@ -1761,7 +1850,7 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
   constexpr int NT = kFullThreads;
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ SeqShared ssh;
-  __shared__ int s_red[NT / 32];
+  __shared__ int s_seg[NT / 32];
   __shared__ int s_nh, s_flag;
   __shared__ float s_pmin;
   const int tid = threadIdx.x;
@@ -1992,21 +2081,22 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
       int cutoff = 0, pos = 0, nf = 0;
       const uint32_t *ks = nullptr, *vs = nullptr;
       for (int attempt = 0; attempt < 2; attempt++) {
-        nf = collect_prefix<NT>(E, V, inv, pmin, g_k0, g_v0, s_red);
+        // the nucleus candidates, each warp's in its own segment of g_k0/g_v0
+        // (index order), then the stable radix sort: its first pass gathers
+        // the segments
+        nf = collect_segments<NT>(E, V, inv, pmin, g_k0, g_v0, s_seg, whist);
+        const int span = collect_span<NT>(V);
         bool in1;
         if (nf <= sm_cap) {
-          for (int i = tid; i < nf; i += NT) {
-            sm_k0[i] = g_k0[i];
-            sm_v0[i] = g_v0[i];
-          }
-          __syncthreads();
-          in1 = block_radix_sort<NT>(sm_k0, sm_v0, sm_k1, sm_v1, nf, whist, tot, &s_flag);
+          radix_first_pass<NT>(g_k0, g_v0, s_seg, span, sm_k0, sm_v0, whist, tot);
+          in1 = block_radix_sort<NT>(sm_k0, sm_v0, sm_k1, sm_v1, nf, whist, tot, &s_flag, 8);
           ks = in1 ? sm_k1 : sm_k0;
           vs = in1 ? sm_v1 : sm_v0;
         } else {
-          in1 = block_radix_sort<NT>(g_k0, g_v0, g_k1, g_v1, nf, whist, tot, &s_flag);
-          ks = in1 ? g_k1 : g_k0;
-          vs = in1 ? g_v1 : g_v0;
+          radix_first_pass<NT>(g_k0, g_v0, s_seg, span, g_k1, g_v1, whist, tot);
+          in1 = block_radix_sort<NT>(g_k1, g_v1, g_k0, g_v0, nf, whist, tot, &s_flag, 8);
+          ks = in1 ? g_k0 : g_k1;
+          vs = in1 ? g_v0 : g_v1;
         }
         // cumulative to the cutoff (:80-88) and the truncated sum (:91-93)
         // tile workspace: the sort room's pair that does not hold the result
