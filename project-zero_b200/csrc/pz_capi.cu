@@ -354,16 +354,16 @@ constexpr double kStaggerFrac = 0.41;
 
 // CTAs of slice_kernel per SM: its shared memory (dynamic, plus its static
 // 1.3 KB and the 1 KB the hardware reserves per CTA) against the SM's 228 KB;
-// its registers (64 a thread) allow four.
-static int slice_occupancy(size_t smem) {
+// its registers allow four (slice_long_kernel, for lists longer than 64: two).
+static int slice_occupancy(size_t smem, int kcap) {
   const size_t per_sm = 228 * 1024;
   const int occ = static_cast<int>(per_sm / (smem + 2304));
-  return std::max(1, std::min(occ, 4));
+  return std::max(1, std::min(occ, pz::slice_ctas_per_sm_max(kcap)));
 }
 
 static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
                           size_t smem, int *B1_out, int *S_out, int *L_out) {
-  const int occ = slice_occupancy(smem);
+  const int occ = slice_occupancy(smem, kcap);
   const int slots = c->num_sms * occ;
   int B1 = 0, S = 1;
   if (B < slots) {
@@ -496,7 +496,7 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   // apart keeps some of them streaming at any time.  A CTA's life is about
   // its bytes at its share of HBM (CTAs in flight x bytes / bandwidth).
   {
-    const int occ = slice_occupancy(smem);
+    const int occ = slice_occupancy(smem, a.kcap);
     const int slots = ctx->num_sms * occ;
     const double cta_bytes = static_cast<double>(a.S == 1 ? V : a.L) * (dtype == PZ_DTYPE_BF16 ? 2 : 4);
     // (measured best: the life at three CTAs per SM, shared by the slots)

@@ -273,6 +273,7 @@ __device__ __noinline__ int sample_list(const unsigned long long *lk, int n_sel,
 // then zeros up to kcap (top-k rows); gbest: the best key (other rows);
 // rs: the row's RNG state.  fe, fp, ford, s_tok: the warp's shared scratch
 // of kcap entries each.
+template <bool LONG>
 __device__ __forceinline__ void finalize_row(const SliceArgs &A, int row, const RowPlan &P, bool bad_k,
                                           bool too_long, bool row_timed_out, bool x0nan,
                                           const unsigned long long *lst, int n_sel,
@@ -322,6 +323,11 @@ __device__ __forceinline__ void finalize_row(const SliceArgs &A, int row, const 
     if (P.keff <= 64) {
       // element-wise steps across the warp, the sequential sums on one lane
       t = warp_sample_small(lst, n_sel, P, rs, fe, fp, want_cand ? cprobs : nullptr);
+      if (t != INT_MIN && want_cand && cids != nullptr)
+        for (int i = lane; i < P.keff; i += 32) cids[i] = i < n_sel ? key_idx(lst[i]) : -1;
+    } else if (LONG) {
+      // longer lists: the same, with the sums on one lane eight terms at a time
+      t = warp_sample_long(lst, n_sel, P, rs, fe, fp, want_cand ? cprobs : nullptr);
       if (t != INT_MIN && want_cand && cids != nullptr)
         for (int i = lane; i < P.keff; i += 32) cids[i] = i < n_sel ? key_idx(lst[i]) : -1;
     }
@@ -513,10 +519,20 @@ constexpr int kSkPerChunk = 32 / kSkGroupLanes;
 constexpr int kGCap = 1024;     // candidate groups
 constexpr int kInsertAt = 2;    // list rows: chunk at which a warp files the first history ids
 constexpr int kCCap = 2048;     // candidate keys
+// Lists longer than kTQK (up to PZ_TOP_K_MAX, launched as slice_long_kernel):
+// a finer sketch, one entry per lane and 16 elements of a chunk (four f32 or
+// two bf16 vectors), so that the k-th largest entry is a tight bound for
+// k up to 1024 (about k entries are read again, 16 elements each).
+constexpr int kFineElems = 16;
+constexpr int kGCapFine = 4096;  // candidate entries of a long list
+__host__ __device__ inline int fine_per_chunk(int elem_bytes) {
+  return kChunkBytes / (elem_bytes * kFineElems);
+}
 __host__ __device__ inline int slice_sketch_entries(int V, int elem_bytes, int kcap) {
   if (kcap <= 1) return 0;
   const long long nchunks = (static_cast<long long>(V) * elem_bytes + kChunkBytes - 1) / kChunkBytes + 1;
-  return static_cast<int>((nchunks * kSkPerChunk + 31) / 32 * 32);
+  const long long per = kcap > kTQK ? fine_per_chunk(elem_bytes) : kSkPerChunk;
+  return static_cast<int>((nchunks * per + 31) / 32 * 32);
 }
 __device__ __forceinline__ uint32_t sk16(float m) { return m == m ? f2ord(m) >> 16 : 0u; }
 
@@ -703,6 +719,10 @@ size_t slice_smem_bytes(int kcap, int hts, int nslots, int V, int elem_bytes) {
 // decision's scratch (from kFinalizeOff on), or the rescan buffer.
 int slice_stages(int, int) { return kSlots; }
 
+// CTAs per SM the registers allow: slice_kernel four (64 a thread),
+// slice_long_kernel (launches with lists longer than kTQK) two.
+int slice_ctas_per_sm_max(int kcap) { return kcap > kTQK ? 2 : 4; }
+
 // Arrivals of first-wave CTAs per SM (counted across launches; consecutive
 // arrivals on an SM take consecutive slots modulo its CTAs in flight).
 __device__ unsigned g_slot_arrivals[256];
@@ -718,13 +738,14 @@ __device__ unsigned g_slot_arrivals[256];
 // with their bound (temperature is monotone) and look at the values of the
 // lanes that reach it.
 
-template <typename T>
-__global__ void __launch_bounds__(kSliceThreads, 4)
-    slice_kernel(const SliceArgs A) {
+// LONG: the launch's lists may be longer than kTQK (slice_long_kernel, two
+// CTAs per SM): those rows keep the fine sketch.  Otherwise every list is at
+// most kTQK long (slice_kernel, four CTAs per SM).
+template <typename T, bool LONG>
+__device__ __forceinline__ void slice_body(const SliceArgs &A) {
   constexpr int NT = kSliceThreads;
   constexpr int NW = kSliceWarps;
   constexpr int VEC = LaneVec<T>::N;          // elements per 16-byte vector
-  constexpr int HPT = 2 * VEC;                // block path: elements per offer
   constexpr int XPT = 16;                     // rescan items per thread per round
   constexpr int XPE = 4;                      // extra-round items per thread per round
   constexpr int MAXPER = (PZ_TOP_K_MAX + kCapB) / NT;
@@ -829,9 +850,16 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   // comes from the groups that can reach its bound; longer lists: one
   // block-wide buffer.
   const bool use_tq = k_sel > 1 && k_sel <= kTQK;
+  // longer lists (LONG launches only): the fine sketch, one entry per
+  // kFineElems elements (one lane's kFineVPE vectors of a chunk)
+  const bool fine = LONG && k_sel > kTQK;
+  const bool skp = use_tq || fine;  // the stream keeps only a sketch
+  constexpr int kFineEPL = kLaneVecs * VEC / kFineElems;  // fine entries per lane per chunk
+  constexpr int kFineVPE = kFineElems / VEC;               // vectors per fine entry
+  constexpr int kFineEPC = 32 * kFineEPL;                  // fine entries per chunk
+  const int sk_per_chunk = fine ? kFineEPC : kSkPerChunk;
   // the sketch covers a whole row (the largest slice), so this always holds
-  const bool sketch_ok = nchunks * kSkPerChunk <= sk_cap;
-  const bool use_block = k_sel > kTQK;
+  const bool sketch_ok = nchunks * sk_per_chunk <= sk_cap;
   const unsigned long long tau0 = (P0.mode == kModeTopK) ? key_topk_floor() : 0ull;
   const float tau0_f = tau0 == 0ull ? -INFINITY : key_val(tau0);
   const uint32_t goff = static_cast<uint32_t>(A.v_offset);
@@ -847,10 +875,10 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   // rows score history ids among the read-again groups with their penalised
   // value.  Other penalties: every history id in the history round.
   const bool pen_dec = P0.rep >= 1.0f && P0.freq >= 0.0f && P0.pres >= 0.0f;
-  const bool hist_stream = hist_on && use_tq && pen_dec;
+  const bool hist_stream = hist_on && skp && pen_dec;
 
   if (tid == 0) {
-    if ((use_tq || use_block) && A.stagger_ns > 0 && blockIdx.x < static_cast<unsigned>(A.stagger_ctas)) {
+    if (skp && A.stagger_ns > 0 && blockIdx.x < static_cast<unsigned>(A.stagger_ctas)) {
       // the first wave: this CTA's slot on its SM (arrival order), and a
       // start that many stagger steps late (the first copies already fly;
       // the wait is bounded by the clock and by a step count)
@@ -901,7 +929,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       hn[i] = 0u;
     }
     for (int i = tid; i < slice_hbm_words(A.V, A.hts, A.kcap); i += NT) hbm[i] = 0u;
-    if (use_tq)
+    if (skp)
       for (int i = tid; i < sk_cap / 32; i += NT) gbm[i] = 0u;
   };
   auto insert_ids = [&](const int (&t)[IPT]) {
@@ -910,18 +938,21 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       if (t[u] >= a && t[u] < b) {
         hash_insert(hk, hn, hmask, hshift, static_cast<uint32_t>(t[u]));
         if (has_hbm) atomicOr(&hbm[t[u] >> 7], 1u << ((t[u] >> 2) & 31));
-        if (use_tq && t[u] >= a_al && t[u] < b_al) {
+        if (skp && t[u] >= a_al && t[u] < b_al) {
           // the sketch group of column t: chunk, then the lane of its vector
+          // (and for the fine sketch, which of the lane's entries)
           constexpr int kPerChunk = kChunkBytes / static_cast<int>(sizeof(T));
           const int off = t[u] - a_al;
-          const int g = (off / kPerChunk) * kSkPerChunk + (((off % kPerChunk) / VEC) & 31) / kSkGroupLanes;
+          const int vi = (off % kPerChunk) / VEC;
+          const int g = fine ? (off / kPerChunk) * kFineEPC + (vi & 31) * kFineEPL + (vi >> 5) / kFineVPE
+                             : (off / kPerChunk) * kSkPerChunk + (vi & 31) / kSkGroupLanes;
           atomicOr(&gbm[g >> 5], 1u << (g & 31));
         }
       }
   };
   // argmax rows take the history round right after the table is built, so
   // the logits the ids name are fetched into L2 first
-  const bool pre = !use_tq && !use_block;
+  const bool pre = !skp;
   auto insert_rest = [&]() {  // the ids past the first NT*IPT
     for (int base = NT * IPT; base < H; base += NT * IPT) {
       int t[IPT];
@@ -938,7 +969,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       insert_ids(t);
     }
   };
-  if (hist_on && !use_tq) {
+  if (hist_on && !skp) {
     init_hist();
     if (pre) {
 #pragma unroll
@@ -950,7 +981,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
     insert_rest();
     __syncthreads();
   }
-  if (hist_on && use_tq) {
+  if (hist_on && skp) {
     // list rows: the table is filled during the stream (the first ids at the
     // warp's chunk kInsertAt, when their loads have landed), the rest after it
     init_hist();
@@ -979,11 +1010,13 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
     }
   };
   // list rows: the candidates read again after the stream, and their bound
-  unsigned long long *ck = reinterpret_cast<unsigned long long *>(ring + 8192);
+  // (long lists: in the block buffer)
+  unsigned long long *ck = fine ? cbuf : reinterpret_cast<unsigned long long *>(ring + 8192);
+  const int ccap = fine ? cap : kCCap;
   float tb = -INFINITY;
   auto cand_push = [&](unsigned long long key) {
     const int p = atomicAdd(&s_cnt, 1);
-    if (p < kCCap) ck[p] = key;
+    if (p < ccap) ck[p] = key;
   };
 
   // ---- row 0's first logit (the NaN rule of argmax.c:3-13) ---------------
@@ -997,7 +1030,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       s_x0nan = (v != v) ? 1 : 0;
     }
   };
-  if (!use_tq) x0_check();
+  if (!skp) x0_check();
 
   // ---- head, tail and the penalised history ids: exact keys ---------------
   // Argmax rows take them before the stream (the best of them is a strong
@@ -1046,19 +1079,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
         if (cnts[e] > 0) x = penalize(x, cnts[e], P);
         xv[e] = greedy ? x : temper(x, P);
       }
-      if (use_block) {
-        unsigned long long keys[XPE];
-        uint32_t valid = 0;
-  #pragma unroll
-        for (int e = 0; e < XPE; e++) {
-          keys[e] = 0ull;
-          if (((have >> e) & 1u) && xv[e] == xv[e]) {
-            keys[e] = mkkey(xv[e], static_cast<uint32_t>(lis[e]) + goff);
-            valid |= 1u << e;
-          }
-        }
-        offer_round<NT, MAXPER, XPE>(cbuf, cap, hwm, k_sel, sh, keys, valid);
-      } else if (use_tq) {
+      if (skp) {
         // after the stream the bound is tight: most values stop here
   #pragma unroll
         for (int e = 0; e < XPE; e++)
@@ -1074,7 +1095,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       }
     }
   };
-  if (!use_tq && !use_block) {
+  if (!skp) {
     history_round();
     const uint32_t bo = __reduce_max_sync(0xFFFFFFFFu, best != 0ull ? f2ord(best_f) : kOrdNegInf);
     if (lane == 0) atomicMax(&s_tauv, bo);
@@ -1087,7 +1108,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   // through a raw threshold instead.
   const bool mulT = greedy || !P.divide;
   const float scale = greedy ? 1.0f : P.inv_T;
-  if (use_tq) {
+  if (skp) {
     // List rows: the stream only records the sketch (each group's raw
     // maximum; temperature is monotone, so it orders the tempered values too).
     int slot = 0;
@@ -1106,12 +1127,32 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       asm volatile("" ::"f"(m));
       if (i + NS < nw) issue(i + NS, slot);
       cp_async_commit();
+      if (fine) {
+        // the lane's own entries (kFineVPE vectors each), stored together
+        uint32_t pk = 0u;
 #pragma unroll
-      for (int o = 1; o < kSkGroupLanes; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-      const uint32_t v16 = sk16(m);
-      if ((lane & (kSkGroupLanes - 1)) == 0 && sketch_ok)
-        sketch[(warp + NW * i) * kSkPerChunk + lane / kSkGroupLanes] = static_cast<uint16_t>(v16);
-      run_max = max(run_max, v16);
+        for (int j = 0; j < kFineEPL; j++) {
+          float q = mv[j * kFineVPE];
+#pragma unroll
+          for (int t = 1; t < kFineVPE; t++) q = fmaxf(q, mv[j * kFineVPE + t]);
+          pk |= sk16(q) << (16 * j);
+        }
+        if (sketch_ok) {
+          const int g0 = (warp + NW * i) * kFineEPC + lane * kFineEPL;
+          if (kFineEPL == 2)
+            *reinterpret_cast<uint32_t *>(sketch + g0) = pk;
+          else
+            sketch[g0] = static_cast<uint16_t>(pk);
+        }
+        run_max = max(run_max, sk16(m));
+      } else {
+#pragma unroll
+        for (int o = 1; o < kSkGroupLanes; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        const uint32_t v16 = sk16(m);
+        if ((lane & (kSkGroupLanes - 1)) == 0 && sketch_ok)
+          sketch[(warp + NW * i) * kSkPerChunk + lane / kSkGroupLanes] = static_cast<uint16_t>(v16);
+        run_max = max(run_max, v16);
+      }
       if (i == kInsertAt && hist_on) insert_ids(hid);
       slot = slot + 1 == NS ? 0 : slot + 1;
     }
@@ -1120,7 +1161,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       if (lane == 0 && wmax > 0u) atomicMax(&s_skmax, wmax);
     }
     if (hist_on && nw <= kInsertAt) insert_ids(hid);  // a warp with too few chunks
-  } else if (!use_block) {
+  } else {
     // argmax: the threshold is the block's best value so far (warp-uniform);
     // only a lane's maximum and its ties can beat it
     uint32_t seen_tau = *reinterpret_cast<volatile uint32_t *>(&s_tauv);
@@ -1187,57 +1228,6 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       }
       slot = slot + 1 == NS ? 0 : slot + 1;
     }
-  } else {
-    // long lists: one block-wide buffer, all warps in step (round r: chunk
-    // warp + NW*r of every warp)
-    float tau_f = tau0_f;
-    const int R = (nchunks + NW - 1) / NW;
-    for (int r = 0; r < R; r++) {
-      const bool mine = r < nw;
-      cp_async_wait<NS - 1>();
-      const unsigned char *sb = wring + (r % NS) * kChunkBytes;
-      const int c = warp + NW * r;
-      const int cv = mine ? kChunkBytes / 16 : 0;  // a short last chunk is NaN-filled
-      const int e0 = a_al + c * (kChunkBytes / static_cast<int>(sizeof(T)));
-#pragma unroll
-      for (int h = 0; h < kLaneVecs / 2; h++) {
-        float xv[HPT];
-#pragma unroll
-        for (int uu = 0; uu < 2; uu++) {
-          const int j = (2 * h + uu) * 32 + lane;
-          if (j < cv) {
-            Vec16S<T>::load(sb, j, xv + uu * VEC);
-          } else {
-#pragma unroll
-            for (int w = 0; w < VEC; w++) xv[uu * VEC + w] = nanf_;
-          }
-        }
-        float vmax = -INFINITY;
-#pragma unroll
-        for (int e = 0; e < HPT; e++) {
-          xv[e] = temper(xv[e], P);
-          vmax = fmaxf(vmax, xv[e]);
-        }
-        if (__syncthreads_or(vmax >= tau_f)) {
-          unsigned long long keys[HPT];
-          uint32_t valid = 0;
-#pragma unroll
-          for (int e = 0; e < HPT; e++) {
-            keys[e] = 0ull;
-            if (xv[e] >= tau_f) {
-              const int li = e0 + ((2 * h + e / VEC) * 32 + lane) * VEC + (e % VEC);
-              if (in_hist(li)) continue;
-              keys[e] = mkkey(xv[e], static_cast<uint32_t>(li) + goff);
-              valid |= 1u << e;
-            }
-          }
-          offer_round<NT, MAXPER, HPT>(cbuf, cap, hwm, k_sel, sh, keys, valid);
-          tau_f = key_val(sh.tau);
-        }
-      }
-      if (r + NS < nw) issue(r + NS, r % NS);
-      cp_async_commit();
-    }
   }
   cp_async_wait<0>();
   // The CTA that will most likely take this slot next (one wave of CTAs
@@ -1251,31 +1241,21 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
     }
   }
 
-  // long-list rows: the history round after the stream, where the bound is tight
-  if (use_block) history_round();
-  if (use_tq && hist_on) insert_rest();
+  if (skp && hist_on) insert_rest();
   __syncthreads();
   const bool timed_out = s_timeout != 0;
 
   // ---- this slice's list -> scratch ---------------------------------------
   unsigned long long *lst = reinterpret_cast<unsigned long long *>(ring);  // the list
-  unsigned long long *rb = use_block ? cbuf : lst;                         // block buffer
-  if (use_block) {
-    int n = sh.n < cap ? sh.n : cap;
-    __syncthreads();
-    if (n > k_sel) {
-      block_select<NT, MAXPER>(cbuf, n, k_sel, sh);
-      n = k_sel;
-    }
-    if (tid == 0) s_n = n;
-  } else if (!use_tq) {
+  unsigned long long *rb = fine ? cbuf : lst;                              // block buffer
+  if (!skp) {
     best = warp_max_u64(best);
     if (lane == 0) s_red[warp] = best;
   }
   __syncthreads();
   bool exact_rescan = false;
   int n_tq = 0;  // list length (sketch path)
-  if (use_tq) {
+  if (skp) {
     // ---- a list row's list, from the sketch ---------------------------------
     // The bound: the k-th largest sketch value, by a two-pass radix select
     // over the 16-bit values; tb, the tempered floor of that value.
@@ -1287,9 +1267,13 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
     // group; a group maximum that is a history id can fall below tb once
     // penalised, and if fewer than k candidates remain, a second pass bounds
     // with the groups that hold no history id, whose k maxima stand.
-    const int ng = sketch_ok ? nchunks * kSkPerChunk : 0;
+    // Long lists (fine sketch): the same with one entry per kFineElems
+    // elements as the group, and the list ranked by a block-wide select and
+    // sort in the block buffer.
+    const int ng = sketch_ok ? nchunks * sk_per_chunk : 0;
+    const int gcap = fine ? kGCapFine : kGCap;
     uint32_t *bins = reinterpret_cast<uint32_t *>(ring);  // 2 x 256 counts
-    int *glist = reinterpret_cast<int *>(ring + 2048);    // kGCap groups
+    int *glist = reinterpret_cast<int *>(ring + 2048);    // gcap groups
     unsigned long long *sorted = reinterpret_cast<unsigned long long *>(ring + 6144);
     int nc = 0, ngs = 0;
     for (int pass = 0; pass < 2; pass++) {
@@ -1310,6 +1294,42 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       // usually one pass: the values within 255 of the largest, M, each in
       // its own bin; else the high byte, then the low byte
       const uint32_t M = s_skmax;
+      uint32_t b16 = 0u;  // 0: fewer than k groups, no bound
+      if (fine) {
+        // k up to 1024 is rarely within 255 of the largest: the high byte,
+        // then the low byte within its bin, each count aggregated per warp
+        // (the values crowd a few bins)
+        auto count = [&](int hsel, uint32_t *bn) {
+          for (int g0 = 0; g0 < ng; g0 += NT) {
+            const int g = g0 + tid;
+            int d = -1;
+            if (g < ng) {
+              const uint32_t v = sketch[g];
+              if (v != 0u && eligible(g)) {
+                if (hsel < 0)
+                  d = static_cast<int>(v >> 8);
+                else if (static_cast<int>(v >> 8) == hsel)
+                  d = static_cast<int>(v & 255u);
+              }
+            }
+            const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
+            if (d >= 0 && lane == __ffs(peers) - 1) atomicAdd(&bn[d], static_cast<uint32_t>(__popc(peers)));
+          }
+        };
+        count(-1, bins);
+        __syncthreads();
+        if (warp == 0) radix_pick(bins, kb, &s_sel[0], &s_sel[1]);
+        __syncthreads();
+        const int hb = s_sel[0];
+        if (hb >= 0) {
+          const int need = s_sel[1];
+          count(hb, bins + 256);
+          __syncthreads();
+          if (warp == 0) radix_pick(bins + 256, need, &s_sel[2], &s_sel[3]);
+          __syncthreads();
+          b16 = (static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(s_sel[2]);
+        }
+      } else {
       for (int g = tid; g < ng; g += NT) {
         const uint32_t v = sketch[g];
         if (v != 0u && M - v < 256u && eligible(g)) atomicAdd(&bins[255u - (M - v)], 1u);
@@ -1317,7 +1337,6 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       __syncthreads();
       if (warp == 0) radix_pick(bins, kb, &s_sel[0], &s_sel[1]);
       __syncthreads();
-      uint32_t b16 = 0u;  // 0: fewer than k groups, no bound
       if (s_sel[0] >= 0) {
         b16 = M - 255u + static_cast<uint32_t>(s_sel[0]);
       } else {
@@ -1343,6 +1362,7 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
           b16 = (static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(s_sel[2]);
         }
       }
+      }
       const uint32_t bord = b16 << 16;
       tb = bord > kOrdNegInf ? temper(ord2f(bord), P) : -INFINITY;
       // the groups to read again: a maximum below ord2f((v + 1) << 16)
@@ -1359,15 +1379,16 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
         base = __shfl_sync(0xFFFFFFFFu, base, 0);
         if (sel) {
           const int p = base + __popc(bal & lanemask_lt());
-          if (p < kGCap) glist[p] = g;
+          if (p < gcap) glist[p] = g;
         }
       }
       __syncthreads();
       ngs = s_gcnt;
-      if (ngs <= kGCap) {
-        // each group: kSkGroupLanes lanes x kLaneVecs vectors, read from L2
-        // or HBM, XG at a time per thread with all loads in flight together
-        constexpr int GV = kSkGroupLanes * kLaneVecs;
+      if (ngs <= gcap) {
+        // each group: kSkGroupLanes lanes x kLaneVecs vectors (fine: one
+        // lane's kFineVPE vectors), read from L2 or HBM, XG at a time per
+        // thread with all loads in flight together
+        const int GV = fine ? kFineVPE : kSkGroupLanes * kLaneVecs;
         constexpr int XG = 4;
         constexpr int kPerChunk = kChunkBytes / static_cast<int>(sizeof(T));
         for (int base = 0; base < ngs * GV; base += NT * XG) {
@@ -1381,8 +1402,16 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
             if (it < ngs * GV) {
               const int g = glist[it / GV];
               const int v = it % GV;
-              const int c = g / kSkPerChunk, pq = g % kSkPerChunk;
-              const int vi = (v / kSkGroupLanes) * 32 + pq * kSkGroupLanes + (v % kSkGroupLanes);
+              int c, vi;
+              if (fine) {
+                c = g / kFineEPC;
+                const int r = g % kFineEPC;
+                vi = ((r % kFineEPL) * kFineVPE + v) * 32 + r / kFineEPL;
+              } else {
+                c = g / kSkPerChunk;
+                const int pq = g % kSkPerChunk;
+                vi = (v / kSkGroupLanes) * 32 + pq * kSkGroupLanes + (v % kSkGroupLanes);
+              }
               const int cv = c == nchunks - 1 ? (body_bytes - c * kChunkBytes) >> 4 : kChunkBytes / 16;
               if (vi < cv) {
                 qv[e] = __ldg(reinterpret_cast<const uint4 *>(body + static_cast<size_t>(c) * kChunkBytes) + vi);
@@ -1423,12 +1452,26 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
       }
       __syncthreads();
       nc = s_cnt;
-      if (ngs > kGCap || nc > kCCap) break;
+      if (ngs > gcap || nc > ccap) break;
       if (nc >= k_sel || !hist_on || b16 == 0u) break;
       __syncthreads();  // every thread has read s_cnt before the next pass resets it
     }
-    if (ngs > kGCap || nc > kCCap || !sketch_ok) {
+    if (ngs > gcap || nc > ccap || !sketch_ok) {
       exact_rescan = true;  // too many to keep: redo the slice below
+    } else if (fine) {
+      // the best k_sel candidates (block-wide radix select), then sorted
+      // descending (bitonic, padded with zero keys to a power of two)
+      int n = nc;
+      if (n > k_sel) {
+        block_select<NT, MAXPER>(cbuf, n, k_sel, sh);
+        n = k_sel;
+      }
+      int n2 = 1;
+      while (n2 < n) n2 <<= 1;
+      for (int i = n + tid; i < n2; i += NT) cbuf[i] = 0ull;
+      block_sort_desc<NT>(cbuf, n2);
+      n_tq = n;
+      lst = cbuf;
     } else {
       for (int i = tid; i < nc; i += NT) {
         const unsigned long long key = ck[i];
@@ -1493,13 +1536,13 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
   unsigned long long gbest = 0ull;
   bool row_timed_out = timed_out, x0nan = s_x0nan != 0;
   if (blockIdx.x < static_cast<unsigned>(A.B1)) {
-    if (use_block || exact_rescan) {
+    if (exact_rescan) {
       fl = rb;
       n_sel = s_n;
       for (int i = n_sel + lane; i < A.kcap; i += 32) fl[i] = 0ull;
       __syncwarp();
       warp_sort_desc(fl, A.kcap);
-    } else if (use_tq) {
+    } else if (skp) {
       n_sel = n_tq;
       for (int i = n_sel + lane; i < A.kcap; i += 32) fl[i] = 0ull;
       __syncwarp();
@@ -1517,10 +1560,10 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
     int m = 0;
     const size_t si = static_cast<size_t>(blockIdx.x) - A.B1;  // (row - B1) * S + slice
     unsigned long long *dst = A.slice_keys + si * static_cast<size_t>(A.kcap);
-    if (use_block || exact_rescan) {
+    if (exact_rescan) {
       m = s_n;
       for (int i = lane; i < m; i += 32) dst[i] = rb[i];
-    } else if (use_tq) {
+    } else if (skp) {
       m = n_tq;
       for (int i = lane; i < m; i += 32) dst[i] = lst[i];
     } else {
@@ -1551,8 +1594,20 @@ __global__ void __launch_bounds__(kSliceThreads, 4)
     row_timed_out |= ml.timed_out != 0;
     x0nan = (__ldcg(A.row_flags + row) & 1u) != 0u;
   }
-  finalize_row(A, row, P, bad_k, too_long, row_timed_out, x0nan, fl, n_sel, gbest, s_rng, fe, fp, ford,
-               s_tokp);
+  finalize_row<LONG>(A, row, P, bad_k, too_long, row_timed_out, x0nan, fl, n_sel, gbest, s_rng, fe, fp,
+                     ford, s_tokp);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSliceThreads, 4) slice_kernel(const SliceArgs A) {
+  slice_body<T, false>(A);
+}
+
+// Launches whose list length (kcap) is above kTQK: the fine sketch for the
+// long lists, two CTAs per SM (room for its sketch and a 2048-id history).
+template <typename T>
+__global__ void __launch_bounds__(kSliceThreads, 2) slice_long_kernel(const SliceArgs A) {
+  slice_body<T, true>(A);
 }
 
 
@@ -2509,6 +2564,10 @@ cudaError_t set_kernel_attributes() {
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(slice_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(slice_long_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(slice_long_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(full_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(full_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
@@ -2526,10 +2585,16 @@ cudaError_t set_kernel_attributes() {
 cudaError_t launch_slice(const SliceArgs &a, int dtype, size_t smem, cudaStream_t st) {
   // rows [0, B1) one CTA each, then S CTAs for each later row
   const unsigned grid = static_cast<unsigned>(a.B1) + static_cast<unsigned>(a.B - a.B1) * a.S;
-  if (dtype == PZ_DTYPE_F32)
+  if (a.kcap > kTQK) {
+    if (dtype == PZ_DTYPE_F32)
+      slice_long_kernel<float><<<grid, kSliceThreads, smem, st>>>(a);
+    else
+      slice_long_kernel<uint16_t><<<grid, kSliceThreads, smem, st>>>(a);
+  } else if (dtype == PZ_DTYPE_F32) {
     slice_kernel<float><<<grid, kSliceThreads, smem, st>>>(a);
-  else
+  } else {
     slice_kernel<uint16_t><<<grid, kSliceThreads, smem, st>>>(a);
+  }
   return cudaGetLastError();
 }
 

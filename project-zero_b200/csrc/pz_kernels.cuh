@@ -135,6 +135,7 @@ cudaError_t launch_slice(const SliceArgs &a, int dtype, size_t smem,
                          cudaStream_t st);
 size_t slice_smem_bytes(int kcap, int hts, int nstages, int V, int elem_bytes);
 int slice_stages(int kcap, int hts);
+int slice_ctas_per_sm_max(int kcap);
 cudaError_t launch_full(const FullArgs &a, int dtype, int grid, size_t smem,
                         cudaStream_t st);
 size_t full_smem_bytes(int V, int hcap);

@@ -172,4 +172,147 @@ __device__ __noinline__ int warp_sample_small(const unsigned long long *lk, int 
   return tok;
 }
 
+// The same steps as sample_list (top_p.c:37-105 on the list, or
+// top_k.c:50-72) for lists of any length up to PZ_TOP_K_MAX, one warp:
+// element-wise steps lane-strided, each sequential float sum on lane 0 in
+// the reference's order, eight terms at a time with the next eight loaded
+// while the current ones are added, and the CDF searches by ballot.  e, c:
+// shared scratch of keff floats each.  Returns INT_MIN, with rs untouched,
+// if the probabilities are not in list order (the caller then runs
+// sample_list, whose stable sort handles that case).
+__device__ __noinline__ int warp_sample_long(const unsigned long long *lk, int n_sel, const RowPlan P,
+                                             unsigned long long &rs, float *e, float *c, float *pr_out) {
+  const int lane = static_cast<int>(lane_id());
+  const int keff = P.keff;
+  auto val = [&](int i) -> float { return i < n_sel ? key_val(lk[i]) : -1e30f; };
+  auto idv = [&](int i) -> int { return i < n_sel ? key_idx(lk[i]) : -1; };
+  const float mx = val(0);
+  // lane 0's running sums of x[0..n), written to out[] when out is not
+  // null; stops after the eight-term block holding the first sum >= stop
+  // and returns that sum's index (n if none; sums past it are scratch), and
+  // the last sum formed in *last
+  auto seq_run = [&](const float *x, int n, float *out, float stop, float *last) -> int {
+    int hit = n;
+    float s = 0.0f;
+    if (lane == 0) {
+      float t[8];
+      int j = 0;
+      if (n >= 8) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) t[q] = x[q];
+      }
+      for (; j + 8 <= n; j += 8) {
+        float u[8];
+        const bool more = j + 16 <= n;
+        if (more) {
+#pragma unroll
+          for (int q = 0; q < 8; q++) u[q] = x[j + 8 + q];
+        }
+        float ss[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          s = __fadd_rn(s, t[q]);
+          ss[q] = s;
+        }
+        if (out != nullptr) {
+#pragma unroll
+          for (int q = 0; q < 8; q++) out[j + q] = ss[q];
+        }
+        if (ss[7] >= stop) {
+          // the sums only grow (the terms are not negative): the first hit is in this block
+          int h = j + 7;
+#pragma unroll
+          for (int q = 6; q >= 0; q--)
+            if (ss[q] >= stop) h = j + q;
+          hit = h;
+          break;
+        }
+        if (more) {
+#pragma unroll
+          for (int q = 0; q < 8; q++) t[q] = u[q];
+        }
+      }
+      if (hit == n) {
+        for (; j < n; j++) {
+          s = __fadd_rn(s, x[j]);
+          if (out != nullptr) out[j] = s;
+          if (s >= stop) {
+            hit = j;
+            break;
+          }
+        }
+      }
+    }
+    __syncwarp();
+    *last = __shfl_sync(0xFFFFFFFFu, s, 0);
+    return __shfl_sync(0xFFFFFFFFu, hit, 0);
+  };
+  // first j < n with r < cdf[j], or -1
+  auto first_below = [&](const float *cdf, int n, float r) -> int {
+    for (int base = 0; base < n; base += 32) {
+      const int j = base + lane;
+      const uint32_t b = __ballot_sync(0xFFFFFFFFu, j < n && r < cdf[j]);
+      if (b) return base + __ffs(b) - 1;
+    }
+    return -1;
+  };
+  int tok;
+  float s_last;
+  if (P.p_on) {
+    const float thr = __fsub_rn(mx, 20.0f);                             // top_p.c:53
+    for (int i = lane; i < keff; i += 32) {
+      const float v = val(i);
+      e[i] = (v >= thr) ? cr_expf(__fsub_rn(v, mx)) : -1.0f;            // :58-59
+    }
+    __syncwarp();
+    // the entries the filter keeps lead the list (it is sorted by value)
+    int n = keff;
+    for (int base = 0; base < keff; base += 32) {
+      const int i = base + lane;
+      const uint32_t b = __ballot_sync(0xFFFFFFFFu, i < keff && !(e[i] >= 0.0f));
+      if (b) {
+        n = base + __ffs(b) - 1;
+        break;
+      }
+    }
+    if (n == 0) {                                                       // :68-69
+      if (pr_out)
+        for (int i = lane; i < keff; i += 32) pr_out[i] = 0.0f;
+      return idv(0);
+    }
+    seq_run(e, n, nullptr, INFINITY, &s_last);                          // :62
+    const float inv = __fdiv_rn(1.0f, s_last);                          // :72
+    // stable sort by probability (:77) is the identity when they descend
+    bool up = false;
+    for (int i = lane; i < n; i += 32)
+      if (i > 0 && __fmul_rn(e[i], inv) > __fmul_rn(e[i - 1], inv)) up = true;
+    if (__any_sync(0xFFFFFFFFu, up)) return INT_MIN;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) e[i] = __fmul_rn(e[i], inv);     // :73-74
+    __syncwarp();
+    const int hit = seq_run(e, n, c, P.p, &s_last);                     // :80-88
+    const int cutoff = hit < n ? hit + 1 : n;
+    const float trunc = c[cutoff - 1];                                  // :91-93
+    const float r = __fmul_rn(rng_next(rs), trunc);                     // :96
+    const int w = first_below(c, cutoff, r);                            // :98-105
+    tok = idv(w >= 0 ? w : 0);
+    if (pr_out)
+      for (int i = lane; i < keff; i += 32) pr_out[i] = i < n ? e[i] : 0.0f;
+  } else {
+    for (int i = lane; i < keff; i += 32) e[i] = cr_expf(__fsub_rn(val(i), mx));  // top_k.c:54
+    __syncwarp();
+    seq_run(e, keff, nullptr, INFINITY, &s_last);                       // :55
+    const float sum = s_last;
+    const float r = rng_next(rs);                                       // :62
+    for (int i = lane; i < keff; i += 32) e[i] = __fdiv_rn(e[i], sum);  // :57-59
+    __syncwarp();
+    seq_run(e, keff, c, INFINITY, &s_last);
+    const int w = first_below(c, keff, r);                              // :63-70
+    tok = idv(w >= 0 ? w : 0);                                          // :72
+    if (pr_out)
+      for (int i = lane; i < keff; i += 32) pr_out[i] = e[i];
+  }
+  return tok;
+}
+
 }  // namespace pz

@@ -13,6 +13,11 @@ lower a value), or every history id scored apart (other penalties); a
 second pass bounds with the groups holding no history id when the first
 finds fewer than k candidates.
 
+Lists longer than 64 (slice_long_kernel) keep a finer sketch: one entry per
+lane and 16 elements of a chunk (a lane's four f32 vectors, or two of its
+four bf16 vectors), up to 4096 candidate entries and 2048 candidates; the
+rest of the argument is the same (`fine=True` below).
+
 This restatement checks, on random and adversarial rows, that the exact
 top-k of the row (the reference's ranking: value descending, lower index
 first) is always among the candidates, which is what makes the device's
@@ -53,11 +58,26 @@ def penalize(x, c, rep, freq, pres):
     return (v - F32(pen)).astype(F32)
 
 
-def groups_of(V, vec=4):
+def groups_of(V, vec=4, fine=False):
     """Column lists of the sketch groups of a row starting 16-byte aligned
-    (vec = 4 f32 or 8 bf16 values per 16-byte vector; a chunk is 2 KB)."""
+    (vec = 4 f32 or 8 bf16 values per 16-byte vector; a chunk is 2 KB).
+    fine: one group per lane and 16 elements (entry j of lane l holds the
+    lane's vectors j*vpe .. j*vpe+vpe-1, vector u of lane l being the
+    chunk's vector u*32+l)."""
     out = []
     per_chunk = 2048 // (16 // vec)
+    if fine:
+        vpe = 16 // vec
+        for c in range((V + per_chunk - 1) // per_chunk):
+            for lane in range(32):
+                for j in range(4 // vpe):
+                    cols = []
+                    for u in range(j * vpe, (j + 1) * vpe):
+                        base = c * per_chunk + (u * 32 + lane) * vec
+                        cols.extend(range(base, base + vec))
+                    cols = [q for q in cols if q < V]
+                    out.append(np.array(cols, dtype=np.int64))
+        return out
     for c in range((V + per_chunk - 1) // per_chunk):
         for p in range(8):
             cols = []
@@ -74,11 +94,12 @@ def kth_largest(vals, k):
     return int(vals[k - 1]) if len(vals) >= k else 0
 
 
-def candidates(x, k, hist, T, divide, rep, freq, pres, vec=4):
+def candidates(x, k, hist, T, divide, rep, freq, pres, vec=4, fine=False):
     """The list path's candidate columns for one row (None: overflow, the
     device redoes the slice exactly)."""
     V = len(x)
-    grp = groups_of(V, vec)
+    grp = groups_of(V, vec, fine)
+    gcap, ccap = (4096, 2048) if fine else (1024, 2048)
     counts = {}
     for h in hist:
         counts[int(h)] = counts.get(int(h), 0) + 1
@@ -100,7 +121,7 @@ def candidates(x, k, hist, T, divide, rep, freq, pres, vec=4):
         tb = temper(ord2f(bord), T, divide) if bord > ORD_NEG_INF else F32(-np.inf)
         up = np.minimum((sk << 16) | 0xFFFF, ord_inf)
         sel = (sk != 0) & ~(temper(ord2f(up), T, divide) < tb)
-        if sel.sum() > 1024:
+        if sel.sum() > gcap:
             return None
         cand = set()
         for g in np.nonzero(sel)[0]:
@@ -120,7 +141,7 @@ def candidates(x, k, hist, T, divide, rep, freq, pres, vec=4):
                 v = temper(penalize(x[j], c, rep, freq, pres), T, divide)
                 if v >= tb:
                     cand.add(j)
-        if len(cand) > 2048:
+        if len(cand) > ccap:
             return None
         if len(cand) >= k or not hist_on or b16 == 0:
             return cand
@@ -194,3 +215,34 @@ def test_exact_list_is_among_candidates(kind, dtype):
             continue  # overflow: the device redoes the slice exactly
         want = exact_topk(x, k, hist, T, divide, rep, freq, pres)
         assert want <= cand, (kind, trial, sorted(want - cand)[:5])
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("kind", KINDS)
+def test_exact_long_list_is_among_candidates(kind, dtype):
+    """Lists of 65 to 1024 entries through the fine sketch."""
+    rs = np.random.default_rng(300 + KINDS.index(kind) + (50 if dtype == "bf16" else 0))
+    vec = 4 if dtype == "f32" else 8
+    n_checked = 0
+    for trial in range(6):
+        k = int(rs.choice([65, 200, 1024]))
+        V = 60000 if k == 1024 else (20000 if trial % 2 else 6000)
+        x = make_row(rs, V, kind)
+        if dtype == "bf16":
+            x = to_bf16_values(x)
+        T = float(rs.choice([0.3, 0.7, 1.5]))
+        divide = bool(trial % 2)
+        mode = trial % 3
+        if mode == 0:
+            hist, rep, freq, pres = [], 1.0, 0.0, 0.0
+        else:
+            top = np.argsort(-np.nan_to_num(x, nan=-np.inf))[:1200]
+            hist = list(rs.choice(V, 300)) + list(top[: 600 if mode == 1 else 100])
+            rep, freq, pres = (3.0, 0.5, 0.2) if mode == 1 else (0.8, 0.0, -0.5)
+        cand = candidates(x, k, hist, T, divide, rep, freq, pres, vec, fine=True)
+        if cand is None:
+            continue  # overflow: the device redoes the slice exactly
+        n_checked += 1
+        want = exact_topk(x, k, hist, T, divide, rep, freq, pres)
+        assert want <= cand, (kind, trial, sorted(want - cand)[:5])
+    assert n_checked > 0
