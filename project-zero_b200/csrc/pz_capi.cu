@@ -287,7 +287,8 @@ pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
   bool ok = c->alloc(&c->slice_keys, static_cast<size_t>(c->slices_cap) * c->kcap_max) &&
             c->alloc(&c->slice_cnt, c->slices_cap) && c->alloc(&c->row_arrive, B) &&
             c->alloc(&c->row_flags, B) && c->alloc(&c->row_tau, B) && c->alloc(&c->row_best, B) &&
-            c->alloc(&c->full_rows, B) && c->alloc(&c->n_full, 1) &&
+            c->alloc(&c->full_rows, static_cast<size_t>(B) * pz::kFullClasses) &&
+            c->alloc(&c->n_full, pz::kFullClasses + 1) &&
             c->alloc(&c->sort_a, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
             c->alloc(&c->sort_b, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
             c->alloc(&c->full_e, static_cast<size_t>(c->full_grid) * c->e_stride);
@@ -475,6 +476,7 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   a.row_best = ctx->row_best;
   a.full_rows = ctx->full_rows;
   a.n_full = ctx->n_full;
+  a.full_stride = ctx->lim.max_batch;
   a.emit_keys = ctx->emit;
   a.rng = rng_state;
   a.out = out;
@@ -510,7 +512,7 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     a.stagger_occ = occ;
   }
   const bool full_pass = !emit && !no_full;
-  if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t), st) != cudaSuccess)
+  if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t) * (pz::kFullClasses + 1), st) != cudaSuccess)
     return fail(PZ_ERR_CUDA);
   cudaEvent_t *ev = next_prof_slot(ctx, st);
   if (ev) cudaEventRecord(ev[0], st);
@@ -532,6 +534,7 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     f.row_flags = ctx->row_flags;
     f.full_rows = ctx->full_rows;
     f.n_full = ctx->n_full;
+    f.full_stride = ctx->lim.max_batch;
     f.sort_a = ctx->sort_a;
     f.sort_b = ctx->sort_b;
     f.sort_stride = ctx->sort_stride;

@@ -273,6 +273,17 @@ __device__ __noinline__ int sample_list(const unsigned long long *lk, int n_sel,
 // then zeros up to kcap (top-k rows); gbest: the best key (other rows);
 // rs: the row's RNG state.  fe, fp, ford, s_tok: the warp's shared scratch
 // of kcap entries each.
+// full_kernel's cost class of a full-vocabulary row: its work grows with
+// the temperature and with top_p (a flatter distribution keeps more values
+// and a longer nucleus to sort and replay).  Measured on config 4, a row's
+// time is about 390 us x T + 1100 us x p plus a constant; softmax rows (two
+// whole-row replays, no sort) sit in the middle.
+__device__ __forceinline__ int full_class(const RowPlan &P) {
+  const float key = P.p_on ? P.T + 2.8f * P.p : P.T + 1.5f;
+  const float c = (key - 1.0f) * 2.5f;
+  return c >= static_cast<float>(kFullClasses - 1) ? kFullClasses - 1 : (c > 0.0f ? static_cast<int>(c) : 0);
+}
+
 template <bool LONG>
 __device__ __forceinline__ void finalize_row(const SliceArgs &A, int row, const RowPlan &P, bool bad_k,
                                           bool too_long, bool row_timed_out, bool x0nan,
@@ -346,7 +357,8 @@ __device__ __forceinline__ void finalize_row(const SliceArgs &A, int row, const 
     pending = true;
     if (lane == 0) {
       A.row_best[row] = gbest;
-      A.full_rows[atomicAdd(A.n_full, 1)] = row;
+      const int c = full_class(P);
+      A.full_rows[c * A.full_stride + atomicAdd(A.n_full + c, 1)] = row;
     }
   }
   if (lane == 0) {
@@ -1925,7 +1937,17 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
   uint32_t *g_v0 = g_k0 + A.sort_stride / 2;
   uint32_t *g_k1 = A.sort_b + static_cast<size_t>(blockIdx.x) * A.sort_stride;
   uint32_t *g_v1 = g_k1 + A.sort_stride / 2;
-  const int n_full = *A.n_full;
+  // rows by cost class, claimed heaviest class first (an atomic counter:
+  // a CTA takes the next row when it is done with one, so long rows do not
+  // pile up on a few CTAs)
+  int cls_n[kFullClasses];
+  int n_full = 0;
+#pragma unroll
+  for (int c = 0; c < kFullClasses; c++) {
+    cls_n[c] = A.n_full[c];
+    n_full += cls_n[c];
+  }
+  __shared__ int s_w;
   // the sort room is free until the nucleus is collected: the row's tile
   // sums (from pass 1a) and the exact replay's tile workspace go there
   static_assert(kSeqHead % kSeqTile == 0 && kSeqHead / kSeqTile <= 8, "head tiles");
@@ -1937,8 +1959,17 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
       row_tsum ? seq_tiles_at(smem + fixed + rt_bytes, static_cast<size_t>(sm_cap) * 16 - rt_bytes)
                : seq_tiles_at(sm_k0, static_cast<size_t>(sm_cap) * 16);
 
-  for (int w = blockIdx.x; w < n_full; w += gridDim.x) {
-    const int row = A.full_rows[w];
+  for (;;) {
+    if (tid == 0) s_w = atomicAdd(A.n_full + kFullClasses, 1);
+    __syncthreads();
+    const int w = s_w;
+    if (w >= n_full) break;
+    int cls = kFullClasses - 1, pos = w;
+    while (pos >= cls_n[cls]) {
+      pos -= cls_n[cls];
+      cls--;
+    }
+    const int row = A.full_rows[cls * A.full_stride + pos];
     const pz_sampler_config cfg = A.cfg[row];
     const RowPlan P = plan_row(cfg, A.V);
     const T *rowp = static_cast<const T *>(A.logits) + static_cast<size_t>(row) * static_cast<size_t>(A.ld);

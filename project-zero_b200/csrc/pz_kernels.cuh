@@ -21,6 +21,11 @@ constexpr int kSliceThreads = 256;
 constexpr int kFullThreads = 512;
 constexpr int kFullCtasPerSm = 2;   // full_kernel rows in flight per SM
 constexpr int kCapB = 1024;   // candidate buffer room above the list length
+// Rows handed to full_kernel are filed in cost classes (class c at
+// full_rows + c * full_stride, its count in n_full[c]); full_kernel's CTAs
+// claim them one at a time through the counter n_full[kFullClasses],
+// heaviest class first.
+constexpr int kFullClasses = 8;
 constexpr int kRowBits = 2;   // row_flags bits
 
 struct SliceArgs {
@@ -56,8 +61,9 @@ struct SliceArgs {
   uint32_t *row_flags;             // [B]
   unsigned long long *row_tau;     // [B] shared list threshold (0 between calls)
   unsigned long long *row_best;    // [B]
-  int32_t *full_rows;              // [B]
-  int32_t *n_full;                 // [1]
+  int32_t *full_rows;              // [kFullClasses][full_stride]
+  int32_t *n_full;                 // [kFullClasses + 1] (zero before the call)
+  int full_stride;
   unsigned long long *emit_keys;   // [B][kcap+1] (mode_emit); slot kcap = count | flags
   // outputs
   unsigned long long *rng;
@@ -80,8 +86,9 @@ struct FullArgs {
   int hcap;
   const unsigned long long *row_best;
   const uint32_t *row_flags;
-  const int32_t *full_rows;
-  const int32_t *n_full;
+  const int32_t *full_rows;       // [kFullClasses][full_stride]
+  int32_t *n_full;                // [kFullClasses] counts, then the claim counter
+  int full_stride;
   uint32_t *sort_a;     // [gridDim][2*maxV] (prob key, index) pairs
   uint32_t *sort_b;
   int64_t sort_stride;  // uint32 elements per CTA in sort_a/sort_b
