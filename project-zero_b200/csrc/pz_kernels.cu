@@ -1645,16 +1645,18 @@ __global__ void __launch_bounds__(kSliceThreads, 2) slice_long_kernel(const Slic
 //            inside it (the bound was not conservative enough), every entry
 //            is collected instead.
 // ---------------------------------------------------------------------------
-constexpr int kEBins = 512;
+constexpr int kEBins = 2048;
 constexpr int kSeqHead = 1024;  // terms of each sum added in order by one thread
-// Bin of a positive e value: 16 bins per binade, from 2^-32 up (e <= 1).
+// Bin of a positive e value: 64 bins per binade, from 2^-32 up (e <= 1).
+// The bins' lower edges give a lower bound of the mass above a bin, within
+// 2^(1/64) (1.1 %) of it, so the collected prefix ends close to the cutoff.
 __device__ __forceinline__ int ebin(float e) {
-  const int b = static_cast<int>(__float_as_uint(e) >> 19) - (95 << 4);
+  const int b = static_cast<int>(__float_as_uint(e) >> 17) - (95 << 6);
   return b < 0 ? 0 : (b >= kEBins ? kEBins - 1 : b);
 }
 // Smallest e of bin b (bin 0 also holds everything below 2^-32).
 __device__ __forceinline__ float ebin_low(int b) {
-  return b == 0 ? 0.0f : __uint_as_float(static_cast<uint32_t>(b + (95 << 4)) << 19);
+  return b == 0 ? 0.0f : __uint_as_float(static_cast<uint32_t>(b + (95 << 6)) << 17);
 }
 
 __host__ __device__ size_t full_smem_fixed(int V, int hcap) {
