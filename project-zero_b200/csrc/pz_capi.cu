@@ -149,7 +149,8 @@ struct pz_sampler_ctx {
   unsigned long long *row_tau = nullptr;
   unsigned long long *row_best = nullptr;
   int32_t *full_rows = nullptr;
-  int32_t *n_full = nullptr;
+  int32_t *n_full = nullptr;      // [kFullClasses + 2]: full-row counts, claim counter, deferred rows
+  int32_t *defer_rows = nullptr;  // [max_batch] rows for slice_long_kernel
   uint32_t *sort_a = nullptr;
   uint32_t *sort_b = nullptr;
   float *full_e = nullptr;
@@ -288,7 +289,7 @@ pz_status pz_ctx_create(pz_sampler_ctx **out, int device,
             c->alloc(&c->slice_cnt, c->slices_cap) && c->alloc(&c->row_arrive, B) &&
             c->alloc(&c->row_flags, B) && c->alloc(&c->row_tau, B) && c->alloc(&c->row_best, B) &&
             c->alloc(&c->full_rows, static_cast<size_t>(B) * pz::kFullClasses) &&
-            c->alloc(&c->n_full, pz::kFullClasses + 1) &&
+            c->alloc(&c->n_full, pz::kFullClasses + 2) && c->alloc(&c->defer_rows, B) &&
             c->alloc(&c->sort_a, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
             c->alloc(&c->sort_b, static_cast<size_t>(c->full_grid) * c->sort_stride) &&
             c->alloc(&c->full_e, static_cast<size_t>(c->full_grid) * c->e_stride);
@@ -460,8 +461,6 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
   a.cfg = cfg;
   a.hist = hist;
   a.hist_off = hist_off;
-  a.kcap = next_pow2(std::max(kmax, 1));
-  a.kmax = std::max(kmax, 1);
   a.hcap = (hist != nullptr && hmax > 0) ? hmax : 0;
   a.hts = a.hcap > 0 ? next_pow2(2 * a.hcap) : 0;
   a.hshift = 32;
@@ -487,38 +486,73 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
     a.row_status = outputs->row_status;
     a.cand_stride = outputs->cand_stride;
   }
-  a.nstages = pz::slice_stages(a.kcap, a.hts);
-  const size_t smem =
-      pz::slice_smem_bytes(a.kcap, a.hts, a.nstages, a.V, dtype == PZ_DTYPE_BF16 ? 2 : 4);
-  choose_slices(ctx, B, V, a.kcap, smem, &a.B1, &a.S, &a.L);
-  if (smem > static_cast<size_t>(pz::max_dynamic_smem())) return fail(PZ_ERR_UNSUPPORTED);
-  // Stagger of the first wave's list-row CTAs.  A wave's CTAs start
-  // together, stream together and then all run their end-of-row work with
-  // HBM idle; starting the CTA slots of an SM a fraction of a CTA's life
-  // apart keeps some of them streaming at any time.  A CTA's life is about
-  // its bytes at its share of HBM (CTAs in flight x bytes / bandwidth).
-  {
-    const int occ = slice_occupancy(smem, a.kcap);
+  // Sizes launch x for lists up to km: its list capacity, shared memory,
+  // row split (whole: one CTA per row, no split) and first-wave stagger.
+  auto size_launch = [&](pz::SliceArgs &x, int km, bool whole, size_t *smem_out) -> bool {
+    x.kcap = next_pow2(std::max(km, 1));
+    x.kmax = std::max(km, 1);
+    x.nstages = pz::slice_stages(x.kcap, x.hts);
+    const size_t sm = pz::slice_smem_bytes(x.kcap, x.hts, x.nstages, x.V, dtype == PZ_DTYPE_BF16 ? 2 : 4);
+    if (whole) {
+      x.B1 = B;
+      x.S = 1;
+      x.L = V;
+    } else {
+      choose_slices(ctx, B, V, x.kcap, sm, &x.B1, &x.S, &x.L);
+    }
+    if (sm > static_cast<size_t>(pz::max_dynamic_smem())) return false;
+    // Stagger of the first wave's list-row CTAs.  A wave's CTAs start
+    // together, stream together and then all run their end-of-row work with
+    // HBM idle; starting the CTA slots of an SM a fraction of a CTA's life
+    // apart keeps some of them streaming at any time.  A CTA's life is about
+    // its bytes at its share of HBM (CTAs in flight x bytes / bandwidth).
+    const int occ = slice_occupancy(sm, x.kcap);
     const int slots = ctx->num_sms * occ;
-    const double cta_bytes = static_cast<double>(a.S == 1 ? V : a.L) * (dtype == PZ_DTYPE_BF16 ? 2 : 4);
+    const double cta_bytes = static_cast<double>(x.S == 1 ? V : x.L) * (dtype == PZ_DTYPE_BF16 ? 2 : 4);
     // (measured best: the life at three CTAs per SM, shared by the slots)
-    const double life_ns = cta_bytes * std::min(ctx->num_sms * 3, B * a.S) / kHbmBytesPerNs * 3.0 / occ;
+    const double life_ns = cta_bytes * std::min(ctx->num_sms * 3, B * x.S) / kHbmBytesPerNs * 3.0 / occ;
     static const int forced = [] {
       const char *e = std::getenv("PZ_STAGGER_NS");  // tuning override
       return e ? std::atoi(e) : -1;
     }();
-    a.stagger_ns = forced >= 0 ? forced : static_cast<int>(kStaggerFrac * life_ns);
-    a.stagger_ctas = slots;
-    a.stagger_occ = occ;
+    x.stagger_ns = forced >= 0 ? forced : static_cast<int>(kStaggerFrac * life_ns);
+    x.stagger_ctas = slots;
+    x.stagger_occ = occ;
+    *smem_out = sm;
+    return true;
+  };
+  // A large batch whose lists may be longer than kTQK runs in two launches:
+  // slice_kernel (up to four CTAs per SM) samples every row but those, which
+  // it files for slice_long_kernel (two per SM, the fine sketch).
+  const bool defer = !emit && kmax > pz::kTQK && B >= 4 * ctx->num_sms;
+  size_t smem = 0, smem2 = 0;
+  pz::SliceArgs a2{};
+  if (defer) {
+    a.defer_kmax = kmax;
+    a.defer_rows = ctx->defer_rows;
+    a.n_defer = ctx->n_full + pz::kFullClasses + 1;
+    a2 = a;
+    a2.defer_kmax = 0;
+    a2.deferred = 1;
+    if (!size_launch(a2, kmax, true, &smem2) || !size_launch(a, pz::kTQK, true, &smem))
+      return fail(PZ_ERR_UNSUPPORTED);
+  } else if (!size_launch(a, kmax, false, &smem)) {
+    return fail(PZ_ERR_UNSUPPORTED);
   }
   const bool full_pass = !emit && !no_full;
-  if (full_pass && cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t) * (pz::kFullClasses + 1), st) != cudaSuccess)
+  if ((full_pass || defer) &&
+      cudaMemsetAsync(ctx->n_full, 0, sizeof(int32_t) * (pz::kFullClasses + 2), st) != cudaSuccess)
     return fail(PZ_ERR_CUDA);
   cudaEvent_t *ev = next_prof_slot(ctx, st);
   if (ev) cudaEventRecord(ev[0], st);
   cudaError_t ce = pz::launch_slice(a, dtype, smem, st);
   if (ce != cudaSuccess) return fail_cuda(ce);
-  int kernels = 1;  // slice_kernel decides every row itself
+  int kernels = 1;  // slice_kernel decides every row itself (but deferred ones)
+  if (defer) {
+    ce = pz::launch_slice(a2, dtype, smem2, st);
+    if (ce != cudaSuccess) return fail_cuda(ce);
+    kernels++;
+  }
   if (ev) cudaEventRecord(ev[1], st);
   if (full_pass) {
     FullArgs f{};

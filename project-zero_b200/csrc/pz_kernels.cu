@@ -518,7 +518,6 @@ __device__ __noinline__ float raw_floor(float t, const RowPlan P) {
   return -INFINITY;
 }
 
-constexpr int kTQK = 64;        // lists up to this long use the sketch path
 
 // The sketch of a list row's stream: for every chunk, the largest raw value
 // of each group of kSkGroupLanes lanes' vectors (64 f32 or 128 bf16
@@ -777,8 +776,9 @@ __device__ __forceinline__ void slice_body(const SliceArgs &A) {
   // CTA u < B1 takes all of row u; the rows after B1 come in S slices of L
   // columns each (the last CTAs launched, filling the GPU's final wave)
   const int u = blockIdx.x;
+  if (LONG && A.deferred && u >= *A.n_defer) return;  // more CTAs than deferred rows
   const bool split = u >= A.B1;
-  const int row = split ? A.B1 + (u - A.B1) / A.S : u;
+  const int row = (LONG && A.deferred) ? A.defer_rows[u] : (split ? A.B1 + (u - A.B1) / A.S : u);
   const int a = split ? (u - A.B1) % A.S * A.L : 0;
   const int b = split ? min(A.V, a + A.L) : A.V;
 
@@ -857,6 +857,13 @@ __device__ __forceinline__ void slice_body(const SliceArgs &A) {
   const bool greedy = P0.mode == kModeGreedy;
   // a list longer than this launch was sized for (hint broken): flag the row
   const bool bad_k = P0.mode == kModeTopK && (P0.keff > A.kmax || P0.keff > A.kcap);
+  if (!LONG && bad_k && A.defer_kmax > 0 && P0.keff <= A.defer_kmax) {
+    // a longer list than this launch keeps: slice_long_kernel samples the
+    // row in the next launch (this CTA's first copies land before it leaves)
+    cp_async_wait<0>();
+    if (tid == 0) A.defer_rows[atomicAdd(A.n_defer, 1)] = row;
+    return;
+  }
   const int k_sel = (P0.mode == kModeTopK && !bad_k) ? P0.keff : 1;
   // lists up to kTQK long: the stream keeps only the sketch, and the list
   // comes from the groups that can reach its bound; longer lists: one

@@ -21,6 +21,7 @@ constexpr int kSliceThreads = 256;
 constexpr int kFullThreads = 512;
 constexpr int kFullCtasPerSm = 2;   // full_kernel rows in flight per SM
 constexpr int kCapB = 1024;   // candidate buffer room above the list length
+constexpr int kTQK = 64;      // lists up to this long: slice_kernel's coarse sketch
 // Rows handed to full_kernel are filed in cost classes (class c at
 // full_rows + c * full_stride, its count in n_full[c]); full_kernel's CTAs
 // claim them one at a time through the counter n_full[kFullClasses],
@@ -54,6 +55,14 @@ struct SliceArgs {
   int stagger_ns;
   int stagger_ctas;
   int stagger_occ;      // CTAs in flight per SM
+  // Batches with lists longer than kTQK, in two launches: slice_kernel
+  // (kmax <= kTQK) files each row whose list is longer than kmax, up to
+  // defer_kmax, in defer_rows instead of flagging it; slice_long_kernel
+  // (deferred = 1) then takes row defer_rows[u] in CTA u < *n_defer.
+  int defer_kmax;                  // 0: no deferring
+  int deferred;
+  int32_t *defer_rows;             // [B]
+  int32_t *n_defer;                // [1] (zero before the first launch)
   // scratch
   unsigned long long *slice_keys;  // [(B-B1)*S][kcap] split rows' slice lists
   int32_t *slice_cnt;              // [(B-B1)*S]
