@@ -1927,7 +1927,7 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ SeqShared ssh;
   __shared__ int s_seg[NT / 32];
-  __shared__ int s_nh, s_flag;
+  __shared__ int s_nh, s_flag, s_pbin;
   __shared__ float s_pmin;
   const int tid = threadIdx.x;
   int32_t *hl = reinterpret_cast<int32_t *>(smem);
@@ -2152,24 +2152,45 @@ __global__ void __launch_bounds__(kFullThreads, kFullCtasPerSm) full_kernel(cons
     } else {
       // the probability bound: bins from the top until a lower bound of the
       // float cumulative over them clears top_p (with margin)
-      if (tid == 0) {
-        double mass = 0.0, cnt = 0.0;
-        float pmin = 0.0f;
+      // (every thread a run of kEBins / NT bins from the top, a block scan of
+      // the counts and masses above it; the highest bin whose bound clears
+      // the target wins)
+      {
+        static_assert(kEBins % NT == 0, "bins per thread");
+        constexpr int BPT = kEBins / NT;
         const double want = static_cast<double>(P.p) + 1e-3;
+        const double dinv = static_cast<double>(inv);
+        const int btop = kEBins - 1 - tid * BPT;  // this thread's bins: btop down to btop - BPT + 1
+        double c_run = 0.0, m_run = 0.0;
+#pragma unroll
+        for (int j = 0; j < BPT; j++) {
+          const int b = btop - j;
+          if (b > 0) {
+            const double c = static_cast<double>(bins[b]);
+            c_run += c;
+            m_run += c * static_cast<double>(ebin_low(b)) * dinv;
+          }
+        }
+        if (tid == 0) s_pbin = -1;
+        double cnt = seq_block_exscan_d<NT>(c_run, ssh);
+        double mass = seq_block_exscan_d<NT>(m_run, ssh);
         if (want < 0.999) {
-          for (int b = kEBins - 1; b > 0; b--) {
+          for (int j = 0; j < BPT; j++) {
+            const int b = btop - j;
+            if (b <= 0) break;
             const uint32_t c = bins[b];
             if (c == 0u) continue;
             cnt += c;
-            mass += static_cast<double>(c) * static_cast<double>(ebin_low(b)) * static_cast<double>(inv);
+            mass += static_cast<double>(c) * static_cast<double>(ebin_low(b)) * dinv;
             const double bound = mass * (1.0 - 5.97e-8) * (1.0 - (cnt + 1.0) * 5.97e-8);
             if (bound >= want) {
-              pmin = __fmul_rn(ebin_low(b), inv);
+              atomicMax(&s_pbin, b);
               break;
             }
           }
         }
-        s_pmin = pmin;
+        __syncthreads();
+        if (tid == 0) s_pmin = s_pbin > 0 ? __fmul_rn(ebin_low(s_pbin), inv) : 0.0f;
       }
       __syncthreads();
       float pmin = s_pmin;
