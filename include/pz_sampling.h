@@ -274,14 +274,15 @@ pz_status pz_sample_batch_static(const void *logits, pz_dtype dtype, int B,
  * slots of CUDA events (n = 0 turns timing off); while on, each of the next
  * n sampling calls on the context records events around its kernels on the
  * call's stream.  pz_ctx_profile_read waits for the recorded calls and
- * returns the summed milliseconds of the streaming kernel (slice_kernel,
- * which also decides the rows) and of the rest of each call (the
+ * returns the summed milliseconds of the streaming kernels (slice_kernel,
+ * which also decides the rows, and in large batches with lists longer
+ * than 64 the slice_long_kernel launch after it) and of the rest of each call (the
  * full-vocabulary pass, when a row needs one), the number of calls timed
  * and the number of kernels they launched; it then starts a new count. */
 pz_status pz_ctx_profile(pz_sampler_ctx *ctx, int n_calls);
 pz_status pz_ctx_profile_read(pz_sampler_ctx *ctx, double *slice_ms,
                               double *rest_ms, int *calls, int *kernels);
-/* The same timing split by phase: phase_ms[0] slice_kernel, [1] the
+/* The same timing split by phase: phase_ms[0] the slice kernels, [1] the
  * full-vocabulary pass (full_kernel), [2] the vocab-sharded allgather,
  * [3] merge_kernel; summed over the timed calls.  Starts a new count. */
 pz_status pz_ctx_profile_phases(pz_sampler_ctx *ctx, double phase_ms[4],
