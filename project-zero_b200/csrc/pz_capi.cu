@@ -340,9 +340,11 @@ void pz_row_shard(int B, int world, int rank, int *begin, int *count) {
 // How rows are cut into CTAs.  With at least as many rows as the GPU has
 // CTA slots (SMs x CTAs per SM at the kernel's occupancy), one CTA per row,
 // and the CTA decides its row.  With fewer rows, every row is split into S
-// slices, just enough to fill the slots once: every slice pays a setup and
-// an end-of-slice merge, and the last of a row's slices to finish merges
-// the S lists and decides the row.  Launches of argmax rows only (list
+// slices, as many as fit the slots in one wave (B x S <= slots: a second,
+// partial wave would cost a whole CTA life; config 2, 256 rows, ran 37.2 us
+// at S = 3 and 33.4 us at S = 2): every slice pays a setup and an
+// end-of-slice merge, and the last of a row's slices to finish merges the S
+// lists and decides the row.  Launches of argmax rows only (list
 // length 1) also split the rows of their last, partial wave (rows B1 on),
 // so that this wave fills the GPU too; for list rows that was measured
 // slower (a slice's short stream reaches a tight bound too late).  Slices
@@ -369,7 +371,7 @@ static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
   const int slots = c->num_sms * occ;
   int B1 = 0, S = 1;
   if (B < slots) {
-    S = (slots + B - 1) / B;
+    S = slots / B;
   } else if (kcap == 1 && B % slots != 0) {
     B1 = B / slots * slots;
     S = slots / (B - B1);
