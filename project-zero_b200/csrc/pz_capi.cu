@@ -348,7 +348,10 @@ void pz_row_shard(int B, int world, int rank, int *begin, int *count) {
 // length 1) also split the rows of their last, partial wave (rows B1 on),
 // so that this wave fills the GPU too; for list rows that was measured
 // slower (a slice's short stream reaches a tight bound too late).  Slices
-// of at least 2048 columns, the split rows' lists within the context's
+// of at least 128 KB of logits (every slice's setup, bound and list, and
+// the last one's merge of S lists, cost more than its stream below that:
+// one config-1 row drew in 47.4 us as 63 slices of 2048 columns and in
+// 28.9 us as 4 slices of 32064), the split rows' lists within the context's
 // scratch, and S lists of the launch's list length within the merge area
 // (2048 keys).
 // B200 HBM3e, bytes per ns (measured copy bandwidth), and the fraction of
@@ -365,7 +368,7 @@ static int slice_occupancy(size_t smem, int kcap) {
   return std::max(1, std::min(occ, pz::slice_ctas_per_sm_max(kcap)));
 }
 
-static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
+static void choose_slices(const pz_sampler_ctx *c, int B, int V, int elem_bytes, int kcap,
                           size_t smem, int *B1_out, int *S_out, int *L_out) {
   const int occ = slice_occupancy(smem, kcap);
   const int slots = c->num_sms * occ;
@@ -385,7 +388,8 @@ static void choose_slices(const pz_sampler_ctx *c, int B, int V, int kcap,
     B1 = 0;
     S = forced;
   }
-  S = std::min(S, std::max(1, (V + 2047) / 2048));
+  const int min_cols = (128 * 1024) / elem_bytes;
+  S = std::min(S, std::max(1, (V + min_cols - 1) / min_cols));
   S = std::min(S, std::max(1, c->slices_cap / std::max(B - B1, 1)));
   S = std::min(S, std::max(1, 2048 / std::max(kcap, 1)));
   S = std::max(S, 1);
@@ -500,7 +504,7 @@ static pz_status sample_impl(pz_sampler_ctx *ctx, const void *logits,
       x.S = 1;
       x.L = V;
     } else {
-      choose_slices(ctx, B, V, x.kcap, sm, &x.B1, &x.S, &x.L);
+      choose_slices(ctx, B, V, dtype == PZ_DTYPE_BF16 ? 2 : 4, x.kcap, sm, &x.B1, &x.S, &x.L);
     }
     if (sm > static_cast<size_t>(pz::max_dynamic_smem())) return false;
     // Stagger of the first wave's list-row CTAs.  A wave's CTAs start

@@ -255,10 +255,11 @@ def test_penalties_that_raise_values(cuda, pz, oracle_lib):
             assert mism == 0, (seed, dtype)
 
 
-@pytest.mark.parametrize("B", [148 + 21, 296 + 30, 444 + 30, 592 + 30, 592 + 3])
+@pytest.mark.parametrize("B", [100, 148 + 21, 296 + 30, 444 + 30, 592 + 30, 592 + 3])
 def test_last_wave_rows_split(cuda, pz, oracle_lib, B):
     """Batches on either side of the GPU's CTA slots (148 SMs x 2 to 4 CTAs):
-    below, every row is split over several CTAs and decided by the slice
+    at half the slots or fewer, every row is split over several CTAs (slices
+    of at least 128 KB, as many as fit one wave) and decided by the slice
     that finishes last; above, one CTA per row, except that argmax-only
     launches split the rows of their last, partial wave.  Mixed settings
     (greedy, top-k, top-p, k = 1024, history) cover every kind of row; a
