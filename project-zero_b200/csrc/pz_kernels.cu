@@ -2596,6 +2596,18 @@ __global__ void history_append_kernel(int32_t *ring, int B, int W, const int32_t
 
 __global__ void counter_step_kernel(int32_t *counter) { *counter += 1; }
 
+// Both steps in one block when the batch fits one (one launch fewer per
+// decode step): every thread reads the counter before the barrier, then
+// thread 0 advances it.
+__global__ void history_append_step_kernel(int32_t *ring, int B, int W, const int32_t *tokens,
+                                           int32_t *counter) {
+  const int r = threadIdx.x;
+  const int pos = *counter % W;
+  if (r < B) ring[static_cast<size_t>(r) * W + pos] = tokens[r];
+  __syncthreads();
+  if (r == 0) *counter += 1;
+}
+
 __global__ void rng_seed_kernel(unsigned long long *s, int B,
                                 unsigned long long base,
                                 const unsigned long long *seeds) {
@@ -2703,6 +2715,10 @@ cudaError_t launch_lm_head(const float *x, int B, int dim, const uint16_t *w, in
 cudaError_t launch_history_append(int32_t *ring, int B, int W, const int32_t *tokens,
                                   int32_t *counter, cudaStream_t st) {
   if (B > 0) {
+    if (B <= 1024) {
+      history_append_step_kernel<<<1, (B + 31) / 32 * 32, 0, st>>>(ring, B, W, tokens, counter);
+      return cudaGetLastError();
+    }
     history_append_kernel<<<(B + 255) / 256, 256, 0, st>>>(ring, B, W, tokens, counter);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
