@@ -1805,7 +1805,7 @@ __device__ __noinline__ int collect_segments(const float *e, int V, float inv, f
   const int a = min(V, warp * span), b = min(V, a + span);
   uint32_t *wh = whist + warp * 256;
   int cnt = 0;
-  float x[8], xn[8];
+  float x[8], xn[8], xm[8];
   auto fetch = [&](int j, float(&d)[8]) {
     if (j + 8 <= b) {
       const float4 p = *reinterpret_cast<const float4 *>(e + j);
@@ -1817,9 +1817,11 @@ __device__ __noinline__ int collect_segments(const float *e, int V, float inv, f
       for (int u = 0; u < 8; u++) d[u] = j + u < b ? e[j + u] : 0.0f;
     }
   };
+  // two groups ahead in flight while this one is tested
   if (a < b) fetch(a + lane * 8, x);
+  if (a + 256 < b) fetch(a + 256 + lane * 8, xn);
   for (int j0 = a; j0 < b; j0 += 256) {
-    if (j0 + 256 < b) fetch(j0 + 256 + lane * 8, xn);  // in flight during this group
+    if (j0 + 512 < b) fetch(j0 + 512 + lane * 8, xm);
     const int i0 = j0 + lane * 8;
     uint32_t keep = 0;
 #pragma unroll
@@ -1828,6 +1830,14 @@ __device__ __noinline__ int collect_segments(const float *e, int V, float inv, f
         x[u] = __fmul_rn(x[u], inv);                                    // top_p.c:73-74
         if (x[u] >= pmin) keep |= 1u << u;
       }
+    }
+    if (!__any_sync(0xFFFFFFFFu, keep != 0u)) {  // most groups keep nothing
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        x[u] = xn[u];
+        xn[u] = xm[u];
+      }
+      continue;
     }
     const int c = __popc(keep);
     int incl = c;
@@ -1849,7 +1859,10 @@ __device__ __noinline__ int collect_segments(const float *e, int V, float inv, f
     }
     cnt += __shfl_sync(0xFFFFFFFFu, incl, 31);
 #pragma unroll
-    for (int u = 0; u < 8; u++) x[u] = xn[u];
+    for (int u = 0; u < 8; u++) {
+      x[u] = xn[u];
+      xn[u] = xm[u];
+    }
   }
   if (lane == 0) seg_n[warp] = cnt;
   __threadfence_block();
